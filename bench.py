@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 WaveSim3D FDTD step (BASELINE config 3 by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c3] [--variant zstream]
+
+One "step" is one FDTD time step of the whole grid.  Rank 0 prints one JSON
+line.  For N > 1 the script runs under torchrun, one rank per GPU, each rank
+owning a z-slab of the grid (strong scaling: the grid is fixed as N grows).
+
+value     global cells x K / device time of the K timed steps (CUDA events on
+          the launch stream, max over ranks), fields resident in HBM.
+e2e       the same metric for a whole job through the public API with pinned
+          host buffers: upload p, p_prev, c2 and the source wavelets, K steps,
+          download p -- all inside the timed region.
+roofline  algorithmic bytes (12 B/cell/step uniform, 16 B heterogeneous) per
+          step / the average step duration, against MEASURED_PEAKS.json.
+cpu_baseline  the C restatement of the reference CPU step (oracle/, "port")
+          timed on this host's cores over a bounded sample (rank 0, N = 1).
+--impl reference  the reference's CPU implementation of the path (the same
+          C restatement: the Rust crate cannot be built here) on this host's
+          cores, same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "Mcells/s (3D FDTD step, whole job)"
+UNIT = "Mcells/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c3")
+    ap.add_argument("--variant", default="zstream")
+    ap.add_argument("--grid", default=None,
+                    help="WxHxD: the workload's recipe at another size (profiling cases)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--comparators", action="store_true",
+                    help="also time the naive and reference-shaped kernels")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def slab_bounds(D: int, world: int, rank: int) -> tuple[int, int]:
+    base, extra = divmod(D, world)
+    zb = rank * base + min(rank, extra)
+    return zb, zb + base + (1 if rank < extra else 0)
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def ncu_traffic(workload: str, variant: str):
+    """DRAM bytes per launch of the step kernel from a committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        d = json.load(f)
+    e = d.get(f"{workload}/{variant}")
+    return None if e is None else e.get("dram_bytes_per_launch")
+
+
+class ClockSampler:
+    """Samples SM clocks and clock-event reasons through NVML (read-only)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device: int, period_s: float = 0.02):
+        self.samples, self.reasons = [], 0
+        self.period = period_s
+        self._stop = threading.Event()
+        self._t = None
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+def cpu_sample_run(wl, target_s: float = 12.0, nthreads: int = 0):
+    """Time the oracle (CPU port of the reference step) on a bounded sample of
+    the workload: full-grid steps when they fit in ~target_s, else a z-slab."""
+    import oracle
+    nthreads = nthreads or oracle.max_threads()
+    # Probe one step on a small slab to size the sample.
+    probe_d = min(wl.D, max(8, int(4e6 // (wl.W * wl.H)) + 2))
+    sub = wl.scaled(wl.W, wl.H, probe_d, steps=4) if probe_d < wl.D else wl
+    g = oracle.from_workload(sub)
+    t0 = time.perf_counter()
+    g.run(1, nthreads)
+    t1 = time.perf_counter() - t0
+    rate = sub.cells / max(t1, 1e-9)  # cells/s
+    full_step_s = wl.cells / rate
+    if full_step_s * 2 <= target_s:
+        steps = max(2, int(target_s / full_step_s))
+        sample = wl
+        g = oracle.from_workload(sample)
+        g.run(1, nthreads)  # warm-up step
+        desc = f"{steps} full {wl.W}x{wl.H}x{wl.D} steps after 1 warm-up step"
+    else:
+        planes = max(8, min(wl.D, int(target_s / 2 * rate / (wl.W * wl.H))))
+        sample = wl.scaled(wl.W, wl.H, planes, steps=4)
+        steps = 2
+        g = oracle.from_workload(sample)
+        g.run(1, nthreads)
+        desc = (f"{steps} steps of a {wl.W}x{wl.H}x{planes} slab of the {wl.name} recipe "
+                f"(same per-cell work) after 1 warm-up step")
+    t0 = time.perf_counter()
+    g.run(steps, nthreads)
+    dt = time.perf_counter() - t0
+    return sample.cells * steps / dt / 1e6, nthreads, desc, dt
+
+
+def run_reference(args, wl):
+    """--impl reference: the reference's CPU path (C restatement) on host cores."""
+    import oracle
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    nthreads = oracle.max_threads()
+    # One timed step = one full-grid step when affordable, else a z-slab sample.
+    probe = wl.scaled(wl.W, wl.H, min(wl.D, 34), steps=2)
+    g = oracle.from_workload(probe)
+    t0 = time.perf_counter()
+    g.run(1, nthreads)
+    rate = probe.cells / max(time.perf_counter() - t0, 1e-9)
+    budget = 150.0 / max(args.steps + args.warmup, 1)
+    if wl.cells / rate <= budget:
+        sample, desc = wl, f"full {wl.W}x{wl.H}x{wl.D} grid per step"
+    else:
+        planes = max(8, min(wl.D, int(budget * rate / (wl.W * wl.H))))
+        sample = wl.scaled(wl.W, wl.H, planes, steps=args.steps + args.warmup + 1)
+        desc = f"{wl.W}x{wl.H}x{planes} z-slab of the {wl.name} recipe per step (bounded sample)"
+    g = oracle.from_workload(sample)
+    g.run(args.warmup, nthreads)
+    t0 = time.perf_counter()
+    g.run(args.steps, nthreads)
+    dt = time.perf_counter() - t0
+    val = sample.cells * args.steps / dt / 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded SplitMix64 medium and sources)",
+        "config": {"workload": wl.name, "grid": [wl.W, wl.H, wl.D],
+                   "heterogeneous": wl.heterogeneous, "sponge": wl.sponge_width,
+                   "sources": int(len(wl.sources))},
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": nthreads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference Rust crate cannot be built in this image (no cargo, wgpu "
+                "dependency); this arm times its CPU step restated in C (oracle/)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def make_backend(wl, variant, device, zb, ze):
+    from rustcompute_b200 import GpuBackend3D
+    whole = (zb, ze) == (0, wl.D)
+    return GpuBackend3D.create(wl.W, wl.H, wl.D, c_squared=wl.c_squared, damping=wl.damping,
+                               device=device, variant=variant, sponge_width=wl.sponge_width,
+                               sponge_max=wl.sponge_max, z_begin=0 if whole else zb,
+                               z_end=0 if whole else ze)
+
+
+def upload_inputs(b, wl, p, pp, c2):
+    """The job's host inputs: both fields, the medium and the source wavelets."""
+    b.upload_fields(p, pp)
+    if c2 is not None:
+        b.set_c2_field(c2)
+    if len(wl.sources):
+        b.set_sources(wl.sources, wl.wavelet)
+
+
+def pinned(a):
+    import torch
+    if a is None:
+        return None
+    t = torch.empty(a.size, dtype=torch.float32, pin_memory=True)
+    t.numpy()[:] = a
+    return t.numpy()
+
+
+def run_ours(args, wl):
+    import torch
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        pg = dist
+    zb, ze = slab_bounds(wl.D, world, rank)
+    if world > 1:
+        raise SystemExit("multi-GPU z-slab exchange is not built yet")
+
+    p0, pp0 = wl.initial_fields(zb, ze)
+    c20 = wl.c2_field(zb, ze)
+    b = make_backend(wl, args.variant, local, zb, ze)
+    upload_inputs(b, wl, p0, pp0, c20)
+    stream = torch.cuda.current_stream(dev)
+    b.set_stream(stream.cuda_stream)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    # Warm-up.
+    b.step_n(None, args.warmup)
+    torch.cuda.synchronize(dev)
+
+    # Timed region: K steps, events between steps on the launch stream.
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    launches0 = b.stats()["kernel_launches"]
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        evs[0].record(stream)
+        for i in range(args.steps):
+            b.step_n(None, 1)
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    launches = b.stats()["kernel_launches"] - launches0
+    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    total_ms = evs[0].elapsed_time(evs[-1])
+    if pg is not None:
+        t = torch.tensor([total_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = wl.cells * args.steps / (total_ms * 1e-3) / 1e6
+
+    local_cells = (ze - zb) * wl.W * wl.H
+    bpc = wl.bytes_per_cell_step
+    alg_bytes = bpc * local_cells
+    avg_ms = sum(step_ms) / len(step_ms)
+    peaks = measured_peaks()
+    achieved = alg_bytes / (avg_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"],
+                "traffic": ncu_traffic(wl.name, args.variant),
+                "algorithmic_bytes_per_launch": alg_bytes,
+                "peak_source": peaks["source"], "kernel": "k_step_zstream"
+                if args.variant == "zstream" else args.variant,
+                "note": "per-launch time = average event interval per step on the launch "
+                        "stream (includes the 1-thread source-injection launch before "
+                        "each step)"}
+
+    result = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded SplitMix64 medium and sources)",
+        "config": {"workload": wl.name, "grid": [wl.W, wl.H, wl.D], "variant": args.variant,
+                   "heterogeneous": wl.heterogeneous, "sponge": wl.sponge_width,
+                   "sources": int(len(wl.sources)), "decomposition": f"z-slabs x{world}",
+                   "l2": "inputs larger than L2 (each field %d MiB > 126 MB)"
+                         % (wl.cells * 4 // 2 ** 20)},
+        "roofline": roofline,
+        "clocks": clk.summary(),
+        "gpu_launches": int(launches),
+    }
+
+    # e2e: one whole job through the public API with pinned host buffers.
+    b.close()
+    if not args.no_e2e:
+        pins = [pinned(a) for a in (p0, pp0, c20)]
+        outp = pinned(np.zeros(local_cells, np.float32))
+        b2 = make_backend(wl, args.variant, local, zb, ze)
+        b2.set_stream(stream.cuda_stream)
+        h2d = sum(a.nbytes for a in pins if a is not None)
+        h2d += wl.wavelet.nbytes + wl.sources.nbytes if len(wl.sources) else 0
+        d2h = outp.nbytes
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record(stream)
+        upload_inputs(b2, wl, *pins)
+        b2.step_n(None, args.steps)
+        b2.download_into(outp)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        wall_ms = (time.perf_counter() - t0) * 1e3
+        e2e_ms = max(e0.elapsed_time(e1), wall_ms)
+        if pg is not None:
+            t = torch.tensor([e2e_ms], device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        result["e2e"] = {"value": wl.cells * args.steps / (e2e_ms * 1e-3) / 1e6, "unit": UNIT,
+                         "h2d_bytes_per_step": h2d * world // args.steps,
+                         "d2h_bytes_per_step": d2h * world // args.steps,
+                         "job": f"upload p, p_prev{', c2' if wl.heterogeneous else ''}"
+                                f"{', source wavelets' if len(wl.sources) else ''} from pinned "
+                                f"host memory; {args.steps} steps; download p",
+                         "job_ms": e2e_ms}
+        b2.close()
+
+    if args.comparators and world == 1:
+        comps = {}
+        for v in ("naive", "refshape"):
+            bc = make_backend(wl, v, local, zb, ze)
+            upload_inputs(bc, wl, p0, pp0, c20)
+            bc.set_stream(stream.cuda_stream)
+            bc.step_n(None, 3)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            n = max(10, min(args.steps, 50))
+            torch.cuda.synchronize(dev)
+            e0.record(stream)
+            bc.step_n(None, n)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1)
+            comps[v] = {"value": wl.cells * n / (ms * 1e-3) / 1e6, "unit": UNIT, "steps": n}
+            bc.close()
+        result["comparators"] = comps
+
+    if rank == 0 and world == 1 and not args.no_cpu:
+        val, cores, desc, secs = cpu_sample_run(wl)
+        result["cpu_baseline"] = {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
+                                  "sample": desc, "seconds": secs}
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def main():
+    args = parse()
+    from rustcompute_b200 import configs
+    if args.grid:
+        W, H, D = (int(v) for v in args.grid.lower().split("x"))
+        wl = configs.build(args.workload, W, H, D)
+    else:
+        wl = configs.build(args.workload)
+    if args.impl == "reference":
+        run_reference(args, wl)
+        return
+    run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,192 @@
+/*
+ * ws3d.h -- C-ABI of the B200-native WaveSim3D FDTD step library (libws3d.so).
+ *
+ * This is the drop-in boundary for the ringkernel-wavesim3d GPU backends of
+ * mivertowski/RustCompute.  Each entry point names the reference interface it
+ * replaces (paths relative to crates/ringkernel-wavesim3d/ unless stated).
+ *
+ * Conventions
+ *  - Plain C types only: an opaque context handle, pointers and sizes.
+ *  - Every function returns a ws3d_status (no exceptions cross the ABI).  On
+ *    failure ws3d_last_error(ctx) holds a one-line message.  The status codes
+ *    map 1:1 onto the reference's error enums GpuError (gpu_backend.rs:13-23)
+ *    and PersistentBackendError (persistent_backend.rs:58-84).
+ *  - Host field buffers are caller-owned, contiguous, z-major f32 arrays:
+ *    index = z*W*H + y*W + x (grid3d.rs:120-122), covering the planes the
+ *    context owns (the whole grid unless a z-slab was requested).
+ *  - Device buffers are owned by the context and freed by ws3d_destroy.
+ *  - Launches are asynchronous on the context's stream; calls that return host
+ *    data (download, energy, max) synchronise that stream.
+ *  - One context per host thread.  There is no CPU fallback: when the device,
+ *    the kernel image or a launch fails, the call fails.
+ *
+ * Semantics of one step (grid3d.rs:222-269, gpu_backend.rs:27-100):
+ *   interior Normal cell:  lap   = ((((W+E)+S)+N)+D)+U - 6p
+ *                          p_new = (2p - p_prev) + c2*lap
+ *                          out   = p_new*damping [*sponge(d)]
+ *   any other cell:        out   = p_prev
+ *   Absorber/Obstacle:     out  *= reflection_coeff
+ *   then (pressure, pressure_prev) = (out, pressure)
+ * every multiply and add separately rounded (no FMA), so results are
+ * bit-identical to the reference CPU arithmetic.
+ */
+#ifndef WS3D_H
+#define WS3D_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WS3D_ABI_VERSION 1u
+
+#if defined(__GNUC__)
+#define WS3D_API __attribute__((visibility("default")))
+#else
+#define WS3D_API
+#endif
+
+typedef enum ws3d_status {
+    WS3D_OK = 0,
+    WS3D_EDEVICE = 1,     /* GpuError::DeviceError, PersistentBackendError::DeviceError */
+    WS3D_ECOMPILE = 2,    /* GpuError::CompileError (no kernel image for this device) */
+    WS3D_ELAUNCH = 3,     /* GpuError::LaunchError, PersistentBackendError::LaunchError */
+    WS3D_EMEMORY = 4,     /* GpuError::MemoryError */
+    WS3D_ESIMULATION = 5, /* PersistentBackendError::SimulationError */
+    WS3D_ECOMMAND = 6,    /* PersistentBackendError::CommandError */
+    WS3D_EREADBACK = 7,   /* PersistentBackendError::ReadbackError */
+    WS3D_EINVAL = 8,      /* invalid argument: size, index, null pointer */
+    WS3D_ETIMEOUT = 9,    /* a device-side bounded wait gave up */
+    WS3D_EPEER = 10       /* peer access or neighbour attach failed */
+} ws3d_status;
+
+/* Step-kernel variants. */
+enum {
+    WS3D_VARIANT_ZSTREAM = 0,  /* default: 2-D tile streaming along z, 128-bit loads */
+    WS3D_VARIANT_NAIVE = 1,    /* one thread per cell, fused boundary (comparator) */
+    WS3D_VARIANT_REFSHAPE = 2  /* the reference's launch shape: 8x8x4 stencil launch
+                                  plus a separate full-grid boundary launch */
+};
+
+typedef struct ws3d_desc {
+    uint32_t width, height, depth; /* global grid in cells (GridParams, grid3d.rs:486-500) */
+    float c_squared;               /* scalar Courant^2 (AcousticParams3D::c_squared) */
+    float damping;                 /* AcousticParams3D::simple_damping */
+    uint32_t sponge_width;         /* sponge width in cells, 0 = off */
+    float sponge_max;              /* sponge coefficient at the face */
+    int32_t device;                /* CUDA device ordinal */
+    uint32_t z_begin, z_end;       /* owned global z planes [z_begin, z_end); 0,0 = all */
+    uint32_t variant;              /* WS3D_VARIANT_* */
+    uint32_t reserved0;
+    uint64_t spin_budget;          /* bounded-wait iterations for device waits, 0 = default */
+} ws3d_desc;
+
+typedef struct ws3d_stats {
+    uint64_t step;                 /* steps taken since create/reset (grid.step) */
+    uint64_t kernel_launches;      /* kernels this context launched since create */
+    uint64_t device_bytes;         /* device memory held by the context */
+    uint32_t width, height, depth; /* global grid */
+    uint32_t z_begin, z_end;       /* owned planes */
+    uint32_t pitch;                /* device row pitch in floats (multiple of 32) */
+    uint32_t variant;
+    uint32_t has_c2_field;
+    uint32_t has_cell_field;
+    uint32_t n_sources;
+    uint32_t reserved;
+} ws3d_stats;
+
+typedef struct ws3d_ctx ws3d_ctx;
+
+/* Library identification. */
+WS3D_API uint32_t ws3d_abi_version(void);
+WS3D_API const char *ws3d_status_string(ws3d_status s);
+
+/* Fill `d` with defaults for a W x H x D grid: c_squared 0.25, damping 1,
+ * no sponge, device 0, whole grid, default variant. */
+WS3D_API void ws3d_desc_init(ws3d_desc *d, uint32_t width, uint32_t height, uint32_t depth);
+
+/* GpuBackend3D::new (gpu_backend.rs:204-311): allocate device state for the
+ * grid and set up the reference boundary layout (grid3d.rs:96-116: every face
+ * cell Absorber with reflection 0.1, every other cell Normal).  Fields start at
+ * zero; upload them with ws3d_upload. */
+WS3D_API ws3d_status ws3d_create(const ws3d_desc *desc, ws3d_ctx **out);
+
+/* Drop for GpuBackend3D: free every device buffer. NULL is accepted. */
+WS3D_API void ws3d_destroy(ws3d_ctx *ctx);
+
+/* One-line message of the last failure on `ctx` ("" when none). */
+WS3D_API const char *ws3d_last_error(const ws3d_ctx *ctx);
+
+/* GpuBackend3D::upload_pressure (gpu_backend.rs:391-401): copy pressure and
+ * pressure_prev from the host.  Either pointer may be NULL to leave it. */
+WS3D_API ws3d_status ws3d_upload(ws3d_ctx *ctx, const float *pressure, const float *pressure_prev);
+
+/* GpuBackend3D::download_pressure (gpu_backend.rs:383-388): copy the current
+ * field (and, when non-NULL, the previous field) to the host.  Synchronous. */
+WS3D_API ws3d_status ws3d_download(ws3d_ctx *ctx, float *pressure, float *pressure_prev);
+
+/* GpuBackend3D::reset (gpu_backend.rs:404-408): upload both fields and set the
+ * step counter to zero. */
+WS3D_API ws3d_status ws3d_reset(ws3d_ctx *ctx, const float *pressure, const float *pressure_prev);
+
+/* Upload SimulationGrid3D::cell_types (u8: 0 Normal, 1 Absorber, 2 Reflector,
+ * 3 Obstacle, gpu_backend.rs:261-270) and reflection_coeff, as
+ * GpuBackend3D::new does (gpu_backend.rs:260-292).  Passing NULL for both
+ * returns to the default face layout, which the kernels evaluate without
+ * reading any per-cell boundary data. */
+WS3D_API ws3d_status ws3d_set_cells(ws3d_ctx *ctx, const uint8_t *cell_types, const float *reflection);
+
+/* Per-cell Courant^2 field (north-star extension of the scalar c_squared,
+ * grid3d.rs:223).  NULL returns to the scalar desc.c_squared. */
+WS3D_API ws3d_status ws3d_set_c2_field(ws3d_ctx *ctx, const float *c2);
+
+/* Point sources driven every step with the inject_impulse semantic
+ * (grid3d.rs:146-152; per-step drive as in bin/wavesim3d.rs:80-100): before
+ * step s, for k in 0..n: a = s < len ? wavelet[k*len + s] : 0,
+ * pressure[i_k] += a, pressure_prev[i_k] += a*0.5.  xyz holds n global (x,y,z)
+ * triples.  n = 0 removes all sources. */
+WS3D_API ws3d_status ws3d_set_sources(ws3d_ctx *ctx, uint32_t n, const uint32_t *xyz,
+                             const float *wavelet, uint64_t len);
+
+/* GpuBackend3D::step (gpu_backend.rs:314-380), n times.  Asynchronous. */
+WS3D_API ws3d_status ws3d_step(ws3d_ctx *ctx, uint64_t n);
+
+/* GpuBackend3D::inject_impulse (gpu_backend.rs:411-442). Out-of-range
+ * coordinates are ignored like grid3d.rs:147. */
+WS3D_API ws3d_status ws3d_inject_impulse(ws3d_ctx *ctx, uint32_t x, uint32_t y, uint32_t z,
+                                float amplitude);
+
+/* GpuBackend3D::inject_spherical_impulse (gpu_backend.rs:445-487), with the
+ * CPU semantics of grid3d.rs:161-191: factor = expf(-d2/(2r)) for d2 <= r^2,
+ * pressure += a*factor, pressure_prev += a*factor*0.5.  The factors are
+ * evaluated on the host in f32 and applied by a kernel. */
+WS3D_API ws3d_status ws3d_inject_spherical_impulse(ws3d_ctx *ctx, uint32_t cx, uint32_t cy,
+                                          uint32_t cz, float amplitude, float radius);
+
+/* SimulationGrid3D::total_energy (grid3d.rs:445-447), accumulated in f64 on
+ * the device over the owned cells.  Synchronous. */
+WS3D_API ws3d_status ws3d_energy(ws3d_ctx *ctx, double *sum_sq);
+
+/* SimulationGrid3D::max_pressure (grid3d.rs:450-455).  Synchronous. */
+WS3D_API ws3d_status ws3d_max_pressure(ws3d_ctx *ctx, float *max_abs);
+
+/* GpuBackend3D::memory_usage (gpu_backend.rs:490-493): device bytes held. */
+WS3D_API size_t ws3d_memory_usage(const ws3d_ctx *ctx);
+
+/* Wait for every launch on the context's stream. */
+WS3D_API ws3d_status ws3d_sync(ws3d_ctx *ctx);
+
+/* Use a caller-owned cudaStream_t (passed as void*) for every later launch;
+ * NULL returns to the context's own stream. */
+WS3D_API ws3d_status ws3d_set_stream(ws3d_ctx *ctx, void *cuda_stream);
+WS3D_API ws3d_status ws3d_get_stream(const ws3d_ctx *ctx, void **cuda_stream);
+
+WS3D_API ws3d_status ws3d_stats_get(const ws3d_ctx *ctx, ws3d_stats *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WS3D_H */

@@ -1,0 +1,126 @@
+"""ctypes binding of libws3d.so (the C-ABI declared in include/ws3d.h).
+
+The library is loaded from the package directory only.  There is no fallback:
+if the shared object is missing, importing the backend raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libws3d.so")
+
+# ws3d_status values (include/ws3d.h)
+WS3D_OK = 0
+WS3D_EDEVICE = 1
+WS3D_ECOMPILE = 2
+WS3D_ELAUNCH = 3
+WS3D_EMEMORY = 4
+WS3D_ESIMULATION = 5
+WS3D_ECOMMAND = 6
+WS3D_EREADBACK = 7
+WS3D_EINVAL = 8
+WS3D_ETIMEOUT = 9
+WS3D_EPEER = 10
+
+WS3D_VARIANT_ZSTREAM = 0
+WS3D_VARIANT_NAIVE = 1
+WS3D_VARIANT_REFSHAPE = 2
+
+
+class ws3d_desc(C.Structure):
+    _fields_ = [
+        ("width", C.c_uint32),
+        ("height", C.c_uint32),
+        ("depth", C.c_uint32),
+        ("c_squared", C.c_float),
+        ("damping", C.c_float),
+        ("sponge_width", C.c_uint32),
+        ("sponge_max", C.c_float),
+        ("device", C.c_int32),
+        ("z_begin", C.c_uint32),
+        ("z_end", C.c_uint32),
+        ("variant", C.c_uint32),
+        ("reserved0", C.c_uint32),
+        ("spin_budget", C.c_uint64),
+    ]
+
+
+class ws3d_stats(C.Structure):
+    _fields_ = [
+        ("step", C.c_uint64),
+        ("kernel_launches", C.c_uint64),
+        ("device_bytes", C.c_uint64),
+        ("width", C.c_uint32),
+        ("height", C.c_uint32),
+        ("depth", C.c_uint32),
+        ("z_begin", C.c_uint32),
+        ("z_end", C.c_uint32),
+        ("pitch", C.c_uint32),
+        ("variant", C.c_uint32),
+        ("has_c2_field", C.c_uint32),
+        ("has_cell_field", C.c_uint32),
+        ("n_sources", C.c_uint32),
+        ("reserved", C.c_uint32),
+    ]
+
+
+_P = C.c_void_p
+_F = C.POINTER(C.c_float)
+_U8 = C.POINTER(C.c_uint8)
+_U32 = C.POINTER(C.c_uint32)
+_CTX = C.c_void_p
+
+# name -> (restype, argtypes).  Every symbol declared in include/ws3d.h.
+SIGNATURES = {
+    "ws3d_abi_version": (C.c_uint32, []),
+    "ws3d_status_string": (C.c_char_p, [C.c_int]),
+    "ws3d_desc_init": (None, [C.POINTER(ws3d_desc), C.c_uint32, C.c_uint32, C.c_uint32]),
+    "ws3d_create": (C.c_int, [C.POINTER(ws3d_desc), C.POINTER(_CTX)]),
+    "ws3d_destroy": (None, [_CTX]),
+    "ws3d_last_error": (C.c_char_p, [_CTX]),
+    "ws3d_upload": (C.c_int, [_CTX, _F, _F]),
+    "ws3d_download": (C.c_int, [_CTX, _F, _F]),
+    "ws3d_reset": (C.c_int, [_CTX, _F, _F]),
+    "ws3d_set_cells": (C.c_int, [_CTX, _U8, _F]),
+    "ws3d_set_c2_field": (C.c_int, [_CTX, _F]),
+    "ws3d_set_sources": (C.c_int, [_CTX, C.c_uint32, _U32, _F, C.c_uint64]),
+    "ws3d_step": (C.c_int, [_CTX, C.c_uint64]),
+    "ws3d_inject_impulse": (C.c_int, [_CTX, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float]),
+    "ws3d_inject_spherical_impulse": (
+        C.c_int, [_CTX, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float]),
+    "ws3d_energy": (C.c_int, [_CTX, C.POINTER(C.c_double)]),
+    "ws3d_max_pressure": (C.c_int, [_CTX, _F]),
+    "ws3d_memory_usage": (C.c_size_t, [_CTX]),
+    "ws3d_sync": (C.c_int, [_CTX]),
+    "ws3d_set_stream": (C.c_int, [_CTX, _P]),
+    "ws3d_get_stream": (C.c_int, [_CTX, C.POINTER(_P)]),
+    "ws3d_stats_get": (C.c_int, [_CTX, C.POINTER(ws3d_stats)]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib_path() -> str:
+    return _LIB_PATH
+
+
+def load() -> C.CDLL:
+    """Load libws3d.so and bind every declared symbol (raises if absent)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(_LIB_PATH):
+            raise ImportError(
+                f"{_LIB_PATH} is missing: build it with `python -m rustcompute_b200.build` "
+                "(there is no CPU fallback)")
+        lib = C.CDLL(_LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib

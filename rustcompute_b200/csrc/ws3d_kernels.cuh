@@ -1,0 +1,428 @@
+// ws3d_kernels.cuh -- sm_100a device code for the WaveSim3D FDTD step.
+//
+// Device layout (HBM): every field is stored pitched.  A row holds `pitch`
+// floats (W rounded up to a multiple of 32, so every row starts on a
+// 128-byte boundary); a plane holds H rows; a slab holds the owned planes
+// plus one ghost plane below and one above.  Kernel pointers address owned
+// plane 0, so plane index -1 and nz are the ghosts.  Padding columns
+// (x >= W) are kept at zero: the kernels write them back unchanged.
+//
+// Arithmetic: every multiply and add is an explicitly rounded intrinsic
+// (__fadd_rn / __fmul_rn ...), which the compiler never contracts into an
+// FMA, in the operation order of the reference CPU step
+// (crates/ringkernel-wavesim3d/src/simulation/grid3d.rs:238-256).  Results
+// are therefore bit-identical to the reference arithmetic.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ws3d {
+
+constexpr uint8_t kNormal = 0, kAbsorber = 1, kReflector = 2, kObstacle = 3;
+constexpr float kFaceReflection = 0.1f;  // grid3d.rs:111
+
+struct StepParams {
+    const float* p;         // pressure (read), owned plane 0
+    float* pp;              // pressure_prev (read, then overwritten with the new field)
+    const float* c2f;       // per-cell Courant^2 or nullptr
+    const uint8_t* types;   // per-cell CellType or nullptr (default face layout)
+    const float* refl;      // per-cell reflection (with types)
+    const float* sponge;    // sponge table s[d], d < sponge_w
+    uint32_t W, H, pitch;   // global width/height, row pitch (floats)
+    uint32_t nz;            // owned planes
+    uint32_t z0;            // global z of owned plane 0
+    uint32_t Dg;            // global depth
+    uint64_t plane;         // H * pitch
+    float c2, damping;
+    uint32_t sponge_w;
+};
+
+__device__ __forceinline__ float4 ld4(const float* p) {
+    return __ldg(reinterpret_cast<const float4*>(p));
+}
+// Streamed once per step: keep it out of L1, normal L2 policy.
+__device__ __forceinline__ float4 ld4_stream(const float* p) {
+    return __ldcs(reinterpret_cast<const float4*>(p));
+}
+__device__ __forceinline__ void st4(float* p, float4 v) {
+    *reinterpret_cast<float4*>(p) = v;
+}
+
+// Reference update of one interior Normal cell (grid3d.rs:250-256), then the
+// optional sponge multiply.
+__device__ __forceinline__ float leapfrog(float w, float e, float s, float n, float dn,
+                                          float up, float c, float pprev, float c2,
+                                          float damping) {
+    float lap = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(w, e), s), n), dn), up);
+    lap = __fsub_rn(lap, __fmul_rn(6.0f, c));
+    float pn = __fadd_rn(__fsub_rn(__fmul_rn(2.0f, c), pprev), __fmul_rn(c2, lap));
+    return __fmul_rn(pn, damping);
+}
+
+__device__ __forceinline__ uint32_t face_dist(uint32_t x, uint32_t y, uint32_t zg,
+                                              const StepParams& a) {
+    uint32_t d = min(x, a.W - 1 - x);
+    d = min(d, min(y, a.H - 1 - y));
+    d = min(d, min(zg, a.Dg - 1 - zg));
+    return d;
+}
+
+// Full cell rule: stencil for interior Normal cells, keep p_prev otherwise,
+// then the boundary multiply for Absorber/Obstacle (grid3d.rs:353-370).
+template <bool kCells>
+__device__ __forceinline__ float cell_rule(uint32_t x, uint32_t y, uint32_t zg, bool interior,
+                                           float w, float e, float s, float n, float dn,
+                                           float up, float c, float pprev, float c2,
+                                           uint8_t t, float r, const StepParams& a) {
+    float v = pprev;
+    bool normal = kCells ? (t == kNormal) : interior;
+    if (interior && normal) {
+        v = leapfrog(w, e, s, n, dn, up, c, pprev, c2, a.damping);
+        if (a.sponge_w) {
+            uint32_t d = face_dist(x, y, zg, a);
+            if (d < a.sponge_w) v = __fmul_rn(v, __ldg(a.sponge + d));
+        }
+    }
+    if (kCells) {
+        if (t == kAbsorber || t == kObstacle) v = __fmul_rn(v, r);
+    } else {
+        if (!interior && x < a.W) v = __fmul_rn(v, kFaceReflection);
+    }
+    return v;
+}
+
+__device__ __forceinline__ bool is_interior(uint32_t x, uint32_t y, uint32_t zg,
+                                            const StepParams& a) {
+    return x >= 1 && x + 1 < a.W && y >= 1 && y + 1 < a.H && zg >= 1 && zg + 1 < a.Dg;
+}
+
+// ---------------------------------------------------------------------------
+// Z-streaming step kernel.
+//
+// CTA = 32 x TY threads covering a 128 x TY tile of an xy plane; the CTA walks
+// its tile through z planes [zb, ze).  Each thread owns one float4 column
+// (4 consecutive x).  Per plane it reads p (the front plane z+1), p_prev and
+// optionally c2 with 128-bit loads and writes the new field with one 128-bit
+// store: 12 (16 with c2) bytes per cell from HBM.  z neighbours come from a
+// three-plane register queue, x neighbours from the float4 itself plus warp
+// shuffles (one halo float at each end of the warp), y neighbours from the
+// current plane staged in shared memory with one halo row above and below.
+// Loads for plane z+1 are issued one iteration ahead.
+// ---------------------------------------------------------------------------
+template <bool kC2F, bool kCells, int TY>
+__global__ void __launch_bounds__(32 * TY, 3)
+k_step_zstream(StepParams a, uint32_t zchunk) {
+    __shared__ float4 srow[2][TY + 2][32];
+    __shared__ float shl[2][TY], shr[2][TY];
+
+    const int lane = threadIdx.x, w = threadIdx.y;
+    const uint32_t x0 = blockIdx.x * 128u;
+    const uint32_t x = x0 + 4u * lane;
+    const uint32_t y0 = blockIdx.y * TY;
+    const uint32_t y = y0 + w;
+    const uint32_t zb = blockIdx.z * zchunk;
+    const uint32_t ze = min(zb + zchunk, a.nz);
+    if (zb >= ze) return;  // uniform over the CTA
+
+    const bool xin = x < a.pitch;
+    const bool yin = y < a.H;
+    const bool act = xin && yin;
+    const bool ylo = (w == 0) && (y0 > 0) && xin;
+    const bool yhi = (w == TY - 1) && (y0 + TY < a.H) && xin;
+    const bool xl = (lane == 0) && (x0 > 0) && yin;
+    const bool xr = (lane == 31) && (x0 + 128u < a.W) && yin;
+
+    const long long P = (long long)a.plane;
+    const long long row = (long long)y * a.pitch + x;
+    const long long rowlo = (long long)(y0 - 1) * a.pitch + x;       // valid when ylo
+    const long long rowhi = (long long)(y0 + TY) * a.pitch + x;      // valid when yhi
+    const long long offxl = (long long)y * a.pitch + (long long)x0 - 1;   // valid when xl
+    const long long offxr = (long long)y * a.pitch + x0 + 128;            // valid when xr
+
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* __restrict__ p = a.p;
+    float* __restrict__ pp = a.pp;
+
+    // Prologue: planes zb-1, zb in registers; plane zb staged in smem.
+    float4 pm = act ? ld4(p + (long long)(zb - 1) * P + row) : z4;
+    float4 pc = act ? ld4(p + (long long)zb * P + row) : z4;
+    srow[0][w + 1][lane] = pc;
+    if (ylo) srow[0][0][lane] = ld4(p + (long long)zb * P + rowlo);
+    if (yhi) srow[0][TY + 1][lane] = ld4(p + (long long)zb * P + rowhi);
+    if (xl) shl[0][w] = __ldg(p + (long long)zb * P + offxl);
+    if (xr) shr[0][w] = __ldg(p + (long long)zb * P + offxr);
+    float4 pn = act ? ld4(p + (long long)(zb + 1) * P + row) : z4;
+    float4 vpp = act ? ld4_stream(pp + (long long)zb * P + row) : z4;
+    float4 vc2 = (kC2F && act) ? ld4_stream(a.c2f + (long long)zb * P + row) : z4;
+    uchar4 vt = make_uchar4(0, 0, 0, 0);
+    if (kCells && act) vt = *reinterpret_cast<const uchar4*>(a.types + (long long)zb * P + row);
+    __syncthreads();
+
+    int cur = 0;
+    for (uint32_t zl = zb; zl < ze; ++zl) {
+        const bool more = zl + 1 < ze;
+        // Prefetch for plane zl+1.
+        float4 pn2 = z4, vpp2 = z4, vc22 = z4, hy = z4;
+        float hx = 0.f;
+        uchar4 vt2 = make_uchar4(0, 0, 0, 0);
+        if (more) {
+            const long long zo1 = (long long)(zl + 1) * P;
+            if (act) {
+                pn2 = ld4(p + zo1 + P + row);
+                vpp2 = ld4_stream(pp + zo1 + row);
+                if (kC2F) vc22 = ld4_stream(a.c2f + zo1 + row);
+                if (kCells) vt2 = *reinterpret_cast<const uchar4*>(a.types + zo1 + row);
+            }
+            if (ylo) hy = ld4(p + zo1 + rowlo);
+            else if (yhi) hy = ld4(p + zo1 + rowhi);
+            if (xl) hx = __ldg(p + zo1 + offxl);
+            else if (xr) hx = __ldg(p + zo1 + offxr);
+        }
+
+        // Compute plane zl.
+        const float4 S = srow[cur][w][lane];
+        const float4 N = srow[cur][w + 2][lane];
+        float wl = __shfl_up_sync(0xffffffffu, pc.w, 1);
+        float er = __shfl_down_sync(0xffffffffu, pc.x, 1);
+        if (lane == 0) wl = shl[cur][w];
+        if (lane == 31) er = shr[cur][w];
+
+        if (act) {
+            const uint32_t zg = a.z0 + zl;
+            float4 out;
+            float c2x = kC2F ? vc2.x : a.c2, c2y = kC2F ? vc2.y : a.c2;
+            float c2z = kC2F ? vc2.z : a.c2, c2w = kC2F ? vc2.w : a.c2;
+            float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+            if (kCells) {
+                const long long o = (long long)zl * P + row;
+                if (vt.x == kAbsorber || vt.x == kObstacle) r0 = __ldg(a.refl + o + 0);
+                if (vt.y == kAbsorber || vt.y == kObstacle) r1 = __ldg(a.refl + o + 1);
+                if (vt.z == kAbsorber || vt.z == kObstacle) r2 = __ldg(a.refl + o + 2);
+                if (vt.w == kAbsorber || vt.w == kObstacle) r3 = __ldg(a.refl + o + 3);
+            }
+            out.x = cell_rule<kCells>(x + 0, y, zg, is_interior(x + 0, y, zg, a), wl, pc.y, S.x,
+                                      N.x, pm.x, pn.x, pc.x, vpp.x, c2x, vt.x, r0, a);
+            out.y = cell_rule<kCells>(x + 1, y, zg, is_interior(x + 1, y, zg, a), pc.x, pc.z,
+                                      S.y, N.y, pm.y, pn.y, pc.y, vpp.y, c2y, vt.y, r1, a);
+            out.z = cell_rule<kCells>(x + 2, y, zg, is_interior(x + 2, y, zg, a), pc.y, pc.w,
+                                      S.z, N.z, pm.z, pn.z, pc.z, vpp.z, c2z, vt.z, r2, a);
+            out.w = cell_rule<kCells>(x + 3, y, zg, is_interior(x + 3, y, zg, a), pc.z, er, S.w,
+                                      N.w, pm.w, pn.w, pc.w, vpp.w, c2w, vt.w, r3, a);
+            st4(pp + (long long)zl * P + row, out);
+        }
+
+        if (more) {
+            const int nxt = cur ^ 1;
+            srow[nxt][w + 1][lane] = pn;
+            if (ylo) srow[nxt][0][lane] = hy;
+            if (yhi) srow[nxt][TY + 1][lane] = hy;
+            if (xl) shl[nxt][w] = hx;
+            if (xr) shr[nxt][w] = hx;
+            __syncthreads();
+            pm = pc; pc = pn; pn = pn2; vpp = vpp2; vc2 = vc22; vt = vt2;
+            cur = nxt;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// One thread per cell, boundary fused (comparator variant).
+// ---------------------------------------------------------------------------
+template <bool kC2F, bool kCells>
+__global__ void __launch_bounds__(256) k_step_naive(StepParams a) {
+    const uint32_t x = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t y = blockIdx.y * blockDim.y + threadIdx.y;
+    const uint32_t zl = blockIdx.z * blockDim.z + threadIdx.z;
+    if (x >= a.W || y >= a.H || zl >= a.nz) return;
+    const long long P = (long long)a.plane;
+    const long long i = (long long)zl * P + (long long)y * a.pitch + x;
+    const uint32_t zg = a.z0 + zl;
+    const bool interior = is_interior(x, y, zg, a);
+    uint8_t t = 0;
+    float r = 0.f;
+    if (kCells) {
+        t = a.types[i];
+        if (t == kAbsorber || t == kObstacle) r = a.refl[i];
+    }
+    float w = 0.f, e = 0.f, s = 0.f, n = 0.f, dn = 0.f, up = 0.f, c = 0.f;
+    float c2 = kC2F ? a.c2f[i] : a.c2;
+    if (interior) {
+        c = a.p[i];
+        w = a.p[i - 1]; e = a.p[i + 1];
+        s = a.p[i - a.pitch]; n = a.p[i + a.pitch];
+        dn = a.p[i - P]; up = a.p[i + P];
+    }
+    a.pp[i] = cell_rule<kCells>(x, y, zg, interior, w, e, s, n, dn, up, c, a.pp[i], c2, t, r, a);
+}
+
+// ---------------------------------------------------------------------------
+// The reference's two-launch shape (gpu_backend.rs:27-100, :316-369): an
+// 8x8x4-block stencil launch over interior Normal cells that reads the cell
+// type of every cell, then a 1-D full-grid boundary launch.  Kept as the
+// "reference kernels recompiled for sm_100a" comparator.
+// ---------------------------------------------------------------------------
+template <bool kC2F>
+__global__ void __launch_bounds__(256) k_ref_stencil(StepParams a) {
+    const uint32_t x = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t y = blockIdx.y * blockDim.y + threadIdx.y;
+    const uint32_t zl = blockIdx.z * blockDim.z + threadIdx.z;
+    if (zl >= a.nz) return;
+    const uint32_t zg = a.z0 + zl;
+    if (!is_interior(x, y, zg, a)) return;
+    const long long P = (long long)a.plane;
+    const long long i = (long long)zl * P + (long long)y * a.pitch + x;
+    if (a.types[i] != kNormal) return;
+    const float c2 = kC2F ? a.c2f[i] : a.c2;
+    float v = leapfrog(a.p[i - 1], a.p[i + 1], a.p[i - a.pitch], a.p[i + a.pitch], a.p[i - P],
+                       a.p[i + P], a.p[i], a.pp[i], c2, a.damping);
+    if (a.sponge_w) {
+        uint32_t d = face_dist(x, y, zg, a);
+        if (d < a.sponge_w) v = __fmul_rn(v, a.sponge[d]);
+    }
+    a.pp[i] = v;
+}
+
+__global__ void __launch_bounds__(256) k_ref_boundary(float* pp, const uint8_t* types,
+                                                      const float* refl, uint64_t n) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint8_t t = types[i];
+    if (t == kAbsorber || t == kObstacle) pp[i] = __fmul_rn(pp[i], refl[i]);
+}
+
+// ---------------------------------------------------------------------------
+// Sources and impulses.
+// ---------------------------------------------------------------------------
+
+// Per-step point sources, applied in source order by one thread so that
+// coinciding sources add in the same order as the reference loop.
+__global__ void k_inject_sources(float* p, float* pp, const uint64_t* off, const float* wavelet,
+                                 uint32_t n, uint64_t len, uint64_t step) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    for (uint32_t k = 0; k < n; ++k) {
+        const float amp = step < len ? wavelet[(uint64_t)k * len + step] : 0.0f;
+        p[off[k]] = __fadd_rn(p[off[k]], amp);
+        pp[off[k]] = __fadd_rn(pp[off[k]], __fmul_rn(amp, 0.5f));
+    }
+}
+
+// grid3d.rs:146-152 / gpu_backend.rs:118-131 (offset precomputed on the host).
+__global__ void k_inject_point(float* p, float* pp, uint64_t off, float amp) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    p[off] = __fadd_rn(p[off], amp);
+    pp[off] = __fadd_rn(pp[off], __fmul_rn(amp, 0.5f));
+}
+
+// grid3d.rs:161-191: one thread per affected cell (distinct offsets).
+__global__ void k_inject_table(float* p, float* pp, const uint64_t* off, const float* factor,
+                               uint32_t n, float amp) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float v = __fmul_rn(amp, factor[i]);
+    p[off[i]] = __fadd_rn(p[off[i]], v);
+    pp[off[i]] = __fadd_rn(pp[off[i]], __fmul_rn(v, 0.5f));
+}
+
+// ---------------------------------------------------------------------------
+// Reductions over the owned cells (padding excluded).  Deterministic: each
+// block writes one partial into a scratch array; one block folds the
+// partials in a fixed order.
+// ---------------------------------------------------------------------------
+constexpr int kRedThreads = 256;
+
+__device__ __forceinline__ double warp_sum(double v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_down_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// rows = nz * H rows of W valid floats, row pitch `pitch`.
+__global__ void __launch_bounds__(kRedThreads) k_energy_partials(const float* p, uint32_t W,
+                                                                 uint32_t pitch, uint64_t rows,
+                                                                 double* partials) {
+    __shared__ double sm[kRedThreads / 32];
+    double acc = 0.0;
+    const uint64_t nvec = rows * (pitch / 4);
+    for (uint64_t v = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
+         v += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = v / (pitch / 4);
+        const uint32_t x = (uint32_t)(v - r * (pitch / 4)) * 4u;
+        if (x >= W) continue;
+        const float4 q = ld4_stream(p + r * pitch + x);
+        acc += (double)q.x * q.x;
+        if (x + 1 < W) acc += (double)q.y * q.y;
+        if (x + 2 < W) acc += (double)q.z * q.z;
+        if (x + 3 < W) acc += (double)q.w * q.w;
+    }
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double t = threadIdx.x < kRedThreads / 32 ? sm[threadIdx.x] : 0.0;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) partials[blockIdx.x] = t;
+    }
+}
+
+__global__ void __launch_bounds__(kRedThreads) k_fold_partials(const double* partials,
+                                                               uint32_t n, double* out) {
+    __shared__ double sm[kRedThreads / 32];
+    double acc = 0.0;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) acc += partials[i];
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double t = threadIdx.x < kRedThreads / 32 ? sm[threadIdx.x] : 0.0;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) *out = t;
+    }
+}
+
+__global__ void __launch_bounds__(kRedThreads) k_maxabs_partials(const float* p, uint32_t W,
+                                                                 uint32_t pitch, uint64_t rows,
+                                                                 float* partials) {
+    __shared__ float sm[kRedThreads / 32];
+    float acc = 0.f;
+    const uint64_t nvec = rows * (pitch / 4);
+    for (uint64_t v = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
+         v += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = v / (pitch / 4);
+        const uint32_t x = (uint32_t)(v - r * (pitch / 4)) * 4u;
+        if (x >= W) continue;
+        const float4 q = ld4_stream(p + r * pitch + x);
+        acc = fmaxf(acc, fabsf(q.x));
+        if (x + 1 < W) acc = fmaxf(acc, fabsf(q.y));
+        if (x + 2 < W) acc = fmaxf(acc, fabsf(q.z));
+        if (x + 3 < W) acc = fmaxf(acc, fabsf(q.w));
+    }
+    acc = warp_max(acc);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < kRedThreads / 32 ? sm[threadIdx.x] : 0.f;
+        t = warp_max(t);
+        if (threadIdx.x == 0) partials[blockIdx.x] = t;
+    }
+}
+
+__global__ void __launch_bounds__(kRedThreads) k_fold_max(const float* partials, uint32_t n,
+                                                          float* out) {
+    __shared__ float sm[kRedThreads / 32];
+    float acc = 0.f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) acc = fmaxf(acc, partials[i]);
+    acc = warp_max(acc);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < kRedThreads / 32 ? sm[threadIdx.x] : 0.f;
+        t = warp_max(t);
+        if (threadIdx.x == 0) *out = t;
+    }
+}
+
+}  // namespace ws3d

@@ -1,0 +1,251 @@
+"""GPU parity: the CUDA step (through the C-ABI) against the CPU oracle.
+
+Bar: bit-identical fields (the kernels use separately rounded f32 ops in the
+reference order).  The north-star tolerance is asserted first so a failure
+shows how far off a field is:  rel-L2 <= 1e-5 and max|diff| <= 1e-4 * peak.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from rustcompute_b200 import CellType, GpuBackend3D, InvalidArgument, SimulationGrid3D, configs
+from rustcompute_b200.grid import AcousticParams3D
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-5
+MAX_ABS_FRAC = 1e-4
+VARIANTS = ["zstream", "naive", "refshape"]
+
+
+def assert_parity(got, want, what=""):
+    got = np.asarray(got, np.float32)
+    want = np.asarray(want, np.float32)
+    assert got.shape == want.shape
+    assert np.all(np.isfinite(got)), f"{what}: non-finite values"
+    peak = float(np.max(np.abs(want))) if want.size else 0.0
+    diff = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    nrm = float(np.linalg.norm(want.astype(np.float64)))
+    rel = float(np.linalg.norm(diff)) / nrm if nrm > 0 else float(np.linalg.norm(diff))
+    assert rel <= REL_L2, f"{what}: rel-L2 {rel:.3e}"
+    assert float(diff.max(initial=0.0)) <= MAX_ABS_FRAC * peak + 1e-30, f"{what}: max-abs"
+    bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
+    assert bad.size == 0, f"{what}: {bad.size} cells differ in bits, first at {bad[:5]}"
+
+
+def gpu_for(wl, variant="zstream", grid=None):
+    g = grid or SimulationGrid3D(wl.W, wl.H, wl.D,
+                                 AcousticParams3D(c_squared=wl.c_squared, simple_damping=wl.damping))
+    if grid is None:
+        p, pp = wl.initial_fields()
+        g.pressure[:] = p
+        g.pressure_prev[:] = pp
+    b = GpuBackend3D(g, variant=variant, sponge_width=wl.sponge_width, sponge_max=wl.sponge_max)
+    c2 = wl.c2_field()
+    if c2 is not None:
+        b.set_c2_field(c2)
+    if len(wl.sources):
+        b.set_sources(wl.sources, wl.wavelet)
+    return g, b
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_c1_full_config_matches_oracle(variant):
+    """BASELINE config 1 exactly: 64^3, Gaussian sigma 3, 200 steps."""
+    wl = configs.build("c1")
+    ref = oracle.from_workload(wl)
+    ref.run(wl.steps, 1)
+    g, b = gpu_for(wl, variant)
+    b.step_n(g, wl.steps)
+    b.download_pressure(g, with_prev=True)
+    assert_parity(g.pressure, ref.pressure, f"c1/{variant}")
+    assert_parity(g.pressure_prev, ref.pressure_prev, f"c1-prev/{variant}")
+    assert g.step == 200
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("shape", [(13, 7, 5), (33, 17, 9), (130, 9, 20), (257, 11, 6),
+                                   (3, 3, 3), (4, 40, 3), (160, 70, 37)])
+@pytest.mark.parametrize("c2f,sponge", [(False, 0), (True, 3)])
+def test_ragged_grids_random_fields(variant, shape, c2f, sponge):
+    W, H, D = shape
+    rng = np.random.default_rng(W * 1000 + H * 10 + D)
+    n = W * H * D
+    prm = AcousticParams3D(c_squared=0.2, simple_damping=0.9995)
+    c2 = rng.uniform(0.01, 0.25, n).astype(np.float32) if c2f else None
+    sw = min(sponge, max((min(shape) - 1) // 2, 0))
+    ref = oracle.OracleGrid(W, H, D, prm, c2_field=c2, sponge_width=sw, sponge_max=0.1)
+    ref.pressure[:] = rng.standard_normal(n).astype(np.float32)
+    ref.pressure_prev[:] = rng.standard_normal(n).astype(np.float32)
+    g = SimulationGrid3D(W, H, D, prm)
+    g.pressure[:] = ref.pressure
+    g.pressure_prev[:] = ref.pressure_prev
+    b = GpuBackend3D(g, variant=variant, sponge_width=sw, sponge_max=0.1)
+    if c2 is not None:
+        b.set_c2_field(c2)
+    ref.run(7, 1)
+    b.step_n(g, 7)
+    b.download_pressure(g, with_prev=True)
+    assert_parity(g.pressure, ref.pressure, f"{shape}/{variant}")
+    assert_parity(g.pressure_prev, ref.pressure_prev, f"{shape}/{variant}/prev")
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_cell_types_obstacles_reflectors(variant):
+    """Full reference cell semantics (grid3d.rs:193-219, :353-370)."""
+    W, H, D = 70, 33, 21
+    prm = AcousticParams3D(c_squared=0.25, simple_damping=0.999)
+    ref = oracle.OracleGrid(W, H, D, prm)
+    ref.inject_impulse_c(35, 16, 10, 1.0)
+    ref.create_obstacle(20, 5, 4, 30, 12, 9, CellType.OBSTACLE)
+    ref.create_obstacle(40, 20, 12, 44, 25, 15, CellType.REFLECTOR)
+    ref.create_obstacle(50, 3, 3, 55, 8, 6, CellType.ABSORBER)
+    ref.set_cell_type(0, 10, 10, CellType.NORMAL)       # an un-absorbed face cell
+    ref.set_cell_type(W - 1, 5, 5, CellType.OBSTACLE)
+    ref.use_cells = True
+    g = SimulationGrid3D(W, H, D, prm)
+    g.pressure[:] = ref.pressure
+    g.pressure_prev[:] = ref.pressure_prev
+    g.cell_types[:] = ref.cell_types
+    g.reflection_coeff[:] = ref.reflection_coeff
+    b = GpuBackend3D(g, variant=variant)
+    assert b.stats()["has_cell_field"] == 1
+    ref.run(40, 1)
+    b.step_n(g, 40)
+    b.download_pressure(g, with_prev=True)
+    assert_parity(g.pressure, ref.pressure, f"cells/{variant}")
+    assert_parity(g.pressure_prev, ref.pressure_prev, f"cells-prev/{variant}")
+
+
+@pytest.mark.parametrize("variant", ["zstream", "naive"])
+def test_c2_scaled_sources_and_sponge(variant):
+    wl = configs.build("c2", 48, 44, 40, steps=120)
+    ref = oracle.from_workload(wl)
+    ref.run(wl.steps, 1)
+    g, b = gpu_for(wl, variant)
+    b.step_n(g, wl.steps)
+    b.download_pressure(g)
+    assert float(np.max(np.abs(ref.pressure))) > 1e-3
+    assert_parity(g.pressure, ref.pressure, f"c2s/{variant}")
+
+
+@pytest.mark.parametrize("variant", ["zstream", "naive"])
+def test_c3_scaled_heterogeneous(variant):
+    wl = configs.build("c3", 96, 72, 64, steps=90)
+    ref = oracle.from_workload(wl)
+    ref.run(wl.steps, 1)
+    g, b = gpu_for(wl, variant)
+    b.step_n(g, wl.steps)
+    b.download_pressure(g, with_prev=True)
+    assert_parity(g.pressure, ref.pressure, f"c3s/{variant}")
+    assert_parity(g.pressure_prev, ref.pressure_prev, f"c3s-prev/{variant}")
+
+
+def test_steps_split_across_calls_equal_one_call():
+    wl = configs.build("c2", 40, 40, 40, steps=50)
+    g1, b1 = gpu_for(wl)
+    b1.step_n(g1, 50)
+    b1.download_pressure(g1)
+    g2, b2 = gpu_for(wl)
+    for n in (1, 7, 2, 30, 10):
+        b2.step_n(g2, n)
+    b2.download_pressure(g2)
+    assert np.array_equal(g1.pressure, g2.pressure)
+
+
+def test_inject_impulse_and_spherical_match_oracle():
+    W, H, D = 40, 36, 30
+    prm = AcousticParams3D(c_squared=0.25, simple_damping=0.9999)
+    ref = oracle.OracleGrid(W, H, D, prm)
+    g = SimulationGrid3D(W, H, D, prm)
+    b = GpuBackend3D(g)
+    ref.inject_impulse_c(20, 18, 15, 1.0)
+    b.inject_impulse(20, 18, 15, 1.0)
+    ref.inject_spherical_impulse(10, 10, 10, 0.7, 4.5)
+    b.inject_spherical_impulse(10, 10, 10, 0.7, 4.5)
+    ref.inject_spherical_impulse(1, 2, 28, 0.3, 3.0)      # clipped by the faces
+    b.inject_spherical_impulse(1, 2, 28, 0.3, 3.0)
+    b.inject_impulse(400, 1, 1, 5.0)                        # ignored (out of range)
+    ref.run(25, 1)
+    b.step_n(g, 25)
+    b.download_pressure(g, with_prev=True)
+    assert_parity(g.pressure, ref.pressure, "impulses")
+    assert_parity(g.pressure_prev, ref.pressure_prev, "impulses-prev")
+
+
+def test_energy_and_max_pressure():
+    wl = configs.build("c1", 50, 42, 38, steps=30)
+    g, b = gpu_for(wl)
+    b.step_n(g, 30)
+    b.download_pressure(g)
+    e = b.energy()
+    want = float(np.dot(g.pressure.astype(np.float64), g.pressure.astype(np.float64)))
+    assert abs(e - want) <= 1e-12 * max(want, 1.0)
+    assert b.max_pressure() == float(np.max(np.abs(g.pressure)))
+
+
+def test_reference_gpu_tests_restated():
+    """gpu_backend.rs:506-549 (creation, step, impulse injection)."""
+    prm = AcousticParams3D.new(343.0, 0.1)
+    grid = SimulationGrid3D(32, 32, 32, prm)
+    grid.inject_impulse(16, 16, 16, 1.0)
+    gpu = GpuBackend3D(grid)
+    for _ in range(10):
+        gpu.step(grid)
+    gpu.download_pressure(grid)
+    assert grid.total_energy() > 0.0
+    assert grid.step == 10
+    grid2 = SimulationGrid3D(32, 32, 32, prm)
+    gpu2 = GpuBackend3D(grid2)
+    gpu2.inject_impulse(16, 16, 16, 1.0)
+    copy = SimulationGrid3D(32, 32, 32, prm)
+    gpu2.download_pressure(copy)
+    assert copy.pressure[copy.index(16, 16, 16)] > 0.5
+
+
+def test_reset_and_memory_usage():
+    wl = configs.build("c1", 24, 24, 24, steps=5)
+    g, b = gpu_for(wl)
+    b.step_n(g, 5)
+    p0, pp0 = wl.initial_fields()
+    g.pressure[:] = p0
+    g.pressure_prev[:] = pp0
+    b.reset(g)
+    assert b.stats()["step"] == 0
+    b.download_pressure(g)
+    assert np.array_equal(g.pressure, p0)
+    assert b.memory_usage() >= 2 * 24 * 24 * 24 * 4
+
+
+def test_errors_are_raised_not_swallowed():
+    g = SimulationGrid3D(16, 16, 16)
+    b = GpuBackend3D(g)
+    with pytest.raises(InvalidArgument):
+        b.set_c2_field(np.zeros(10, np.float32))
+    with pytest.raises(InvalidArgument):
+        b.set_sources(np.array([[99, 1, 1]]), np.zeros((1, 4), np.float32))
+    with pytest.raises(InvalidArgument):
+        b.inject_spherical_impulse(5, 5, 5, 1.0, -1.0)
+    with pytest.raises(InvalidArgument):
+        GpuBackend3D(g, variant="nope")
+
+
+def test_full_size_c3_zstream_equals_naive_and_oracle():
+    """BASELINE config 3 at full size (512^3, heterogeneous, sponge, source):
+    size-independent checks -- two independent kernels agree bit for bit after
+    20 steps, and both agree with the oracle (all host threads) after 2."""
+    wl = configs.build("c3")
+    g1, b1 = gpu_for(wl, "zstream")
+    g2, b2 = gpu_for(wl, "naive")
+    b1.step_n(g1, 2)
+    b1.download_pressure(g1)
+    ref = oracle.from_workload(wl)
+    ref.run(2, oracle.max_threads())
+    assert_parity(g1.pressure, ref.pressure, "c3-full-vs-oracle")
+    b1.step_n(g1, 18)
+    b2.step_n(g2, 20)
+    p1 = b1.download_field()
+    p2 = b2.download_field()
+    assert np.array_equal(p1, p2)
+    e = b1.energy()
+    assert np.isfinite(e) and e > 0
