@@ -37,7 +37,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-METRIC = "Mcells/s (3D FDTD step, whole job)"
+from rustcompute_b200.slab import slab_bounds  # noqa: E402
+
+METRIC = "Mcells/s and % HBM roofline at 1/2/4/8 B200 (3D FDTD step) vs host CPU"
 UNIT = "Mcells/s"
 
 
@@ -63,12 +65,6 @@ def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", str(rank)))
     return rank, world, local
-
-
-def slab_bounds(D: int, world: int, rank: int) -> tuple[int, int]:
-    base, extra = divmod(D, world)
-    zb = rank * base + min(rank, extra)
-    return zb, zb + base + (1 if rank < extra else 0)
 
 
 def measured_peaks() -> dict:
@@ -250,6 +246,8 @@ def pinned(a):
 
 
 def run_ours(args, wl):
+    import datetime
+
     import torch
     rank, world, local = dist_env()
     if world != args.gpus:
@@ -258,72 +256,77 @@ def run_ours(args, wl):
     dev = torch.device("cuda", local)
     pg = None
     if world > 1:
-        import datetime
-
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = dist
     zb, ze = slab_bounds(wl.D, world, rank)
-    if world > 1:
-        raise SystemExit("multi-GPU z-slab exchange is not built yet")
-
-    p0, pp0 = wl.initial_fields(zb, ze)
-    c20 = wl.c2_field(zb, ze)
-    b = make_backend(wl, args.variant, local, zb, ze)
-    upload_inputs(b, wl, p0, pp0, c20)
-    stream = torch.cuda.current_stream(dev)
-    b.set_stream(stream.cuda_stream)
+    local_cells = (ze - zb) * wl.W * wl.H
 
     def barrier():
         if pg is not None:
             pg.barrier()
 
-    # Warm-up.
-    b.step_n(None, args.warmup)
-    torch.cuda.synchronize(dev)
+    def max_over_ranks(v: float) -> float:
+        if pg is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
 
-    # Timed region: K steps, events between steps on the launch stream.
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    stream = torch.cuda.Stream(device=dev)   # a real stream (handle != 0) shared with the library
+    p0, pp0 = wl.initial_fields(zb, ze)
+    c20 = wl.c2_field(zb, ze)
+
+    def open_backend():
+        b = make_backend(wl, args.variant, local, zb, ze)
+        b.set_stream(stream.cuda_stream)
+        return b
+
+    b = open_backend()
+    upload_inputs(b, wl, p0, pp0, c20)
+    if world > 1:
+        from rustcompute_b200.slab import connect
+        connect(b, rank, world, pg.all_gather_object, barrier)
+
+    # Warm-up (>= 3 steps), then the timed region: K steps between two events
+    # on the launch stream; the library also times every step-kernel launch.
+    b.step_n(None, max(args.warmup, 3))
+    b.sync()
     launches0 = b.stats()["kernel_launches"]
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clk:
-        evs[0].record(stream)
-        for i in range(args.steps):
-            b.step_n(None, 1)
-            evs[i + 1].record(stream)
+        e0.record(stream)
+        kernel_ms = b.step_timed(args.steps)   # synchronises the stream at the end
+        e1.record(stream)
         torch.cuda.synchronize(dev)
     barrier()
     launches = b.stats()["kernel_launches"] - launches0
-    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
-    total_ms = evs[0].elapsed_time(evs[-1])
-    if pg is not None:
-        t = torch.tensor([total_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        total_ms = float(t.item())
+    total_ms = max_over_ranks(e0.elapsed_time(e1))
     value = wl.cells * args.steps / (total_ms * 1e-3) / 1e6
 
-    local_cells = (ze - zb) * wl.W * wl.H
     bpc = wl.bytes_per_cell_step
     alg_bytes = bpc * local_cells
-    avg_ms = sum(step_ms) / len(step_ms)
+    avg_kernel_ms = kernel_ms / args.steps
     peaks = measured_peaks()
-    achieved = alg_bytes / (avg_ms * 1e-3) / 1e9
+    achieved = alg_bytes / (avg_kernel_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"],
                 "traffic": ncu_traffic(wl.name, args.variant),
                 "algorithmic_bytes_per_launch": alg_bytes,
-                "peak_source": peaks["source"], "kernel": "k_step_zstream"
-                if args.variant == "zstream" else args.variant,
-                "note": "per-launch time = average event interval per step on the launch "
-                        "stream (includes the 1-thread source-injection launch before "
-                        "each step)"}
+                "bytes_per_cell_step": bpc,
+                "kernel_avg_ms": avg_kernel_ms,
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"
+                               if peaks["source"] == "measured" else "fallback",
+                "kernel": "k_step_zstream" if args.variant == "zstream" else args.variant,
+                "rank": rank}
 
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "warmup": max(args.warmup, 3), "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded SplitMix64 medium and sources)",
         "config": {"workload": wl.name, "grid": [wl.W, wl.H, wl.D], "variant": args.variant,
                    "heterogeneous": wl.heterogeneous, "sponge": wl.sponge_width,
@@ -334,60 +337,47 @@ def run_ours(args, wl):
         "clocks": clk.summary(),
         "gpu_launches": int(launches),
     }
+    b.close()
 
     # e2e: one whole job through the public API with pinned host buffers.
-    b.close()
     if not args.no_e2e:
         pins = [pinned(a) for a in (p0, pp0, c20)]
         outp = pinned(np.zeros(local_cells, np.float32))
-        b2 = make_backend(wl, args.variant, local, zb, ze)
-        b2.set_stream(stream.cuda_stream)
         h2d = sum(a.nbytes for a in pins if a is not None)
-        h2d += wl.wavelet.nbytes + wl.sources.nbytes if len(wl.sources) else 0
+        h2d += (wl.wavelet.nbytes + wl.sources.nbytes) if len(wl.sources) else 0
         d2h = outp.nbytes
+        b2 = open_backend()
         barrier()
         torch.cuda.synchronize(dev)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
-        e0.record(stream)
         upload_inputs(b2, wl, *pins)
+        if world > 1:
+            from rustcompute_b200.slab import connect
+            connect(b2, rank, world, pg.all_gather_object, barrier)
         b2.step_n(None, args.steps)
         b2.download_into(outp)
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        wall_ms = (time.perf_counter() - t0) * 1e3
-        e2e_ms = max(e0.elapsed_time(e1), wall_ms)
-        if pg is not None:
-            t = torch.tensor([e2e_ms], device=dev)
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-            e2e_ms = float(t.item())
+        e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3)
         result["e2e"] = {"value": wl.cells * args.steps / (e2e_ms * 1e-3) / 1e6, "unit": UNIT,
                          "h2d_bytes_per_step": h2d * world // args.steps,
                          "d2h_bytes_per_step": d2h * world // args.steps,
                          "job": f"upload p, p_prev{', c2' if wl.heterogeneous else ''}"
                                 f"{', source wavelets' if len(wl.sources) else ''} from pinned "
-                                f"host memory; {args.steps} steps; download p",
-                         "job_ms": e2e_ms}
+                                f"host memory; {args.steps} steps; download p"
+                                f"{'; slab handle exchange' if world > 1 else ''}",
+                         "job_ms": e2e_ms, "clock": "host wall clock, max over ranks"}
         b2.close()
 
     if args.comparators and world == 1:
         comps = {}
         for v in ("naive", "refshape"):
             bc = make_backend(wl, v, local, zb, ze)
-            upload_inputs(bc, wl, p0, pp0, c20)
             bc.set_stream(stream.cuda_stream)
+            upload_inputs(bc, wl, p0, pp0, c20)
             bc.step_n(None, 3)
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
             n = max(10, min(args.steps, 50))
-            torch.cuda.synchronize(dev)
-            e0.record(stream)
-            bc.step_n(None, n)
-            e1.record(stream)
-            torch.cuda.synchronize(dev)
-            ms = e0.elapsed_time(e1)
-            comps[v] = {"value": wl.cells * n / (ms * 1e-3) / 1e6, "unit": UNIT, "steps": n}
+            ms = bc.step_timed(n)
+            comps[v] = {"value": wl.cells * n / (ms * 1e-3) / 1e6, "unit": UNIT, "steps": n,
+                        "note": "step-kernel time only"}
             bc.close()
         result["comparators"] = comps
 

@@ -153,6 +153,12 @@ WS3D_API ws3d_status ws3d_set_sources(ws3d_ctx *ctx, uint32_t n, const uint32_t 
 /* GpuBackend3D::step (gpu_backend.rs:314-380), n times.  Asynchronous. */
 WS3D_API ws3d_status ws3d_step(ws3d_ctx *ctx, uint64_t n);
 
+/* ws3d_step plus CUDA-event timing of every step-kernel launch on the
+ * context's stream; synchronises and returns the summed kernel time in ms
+ * (benchmark support: bin/benchmark.rs:75-77 times step_n on the host
+ * without a synchronise, this measures on the device).  n <= 2^20. */
+WS3D_API ws3d_status ws3d_step_timed(ws3d_ctx *ctx, uint64_t n, double *kernel_ms);
+
 /* GpuBackend3D::inject_impulse (gpu_backend.rs:411-442). Out-of-range
  * coordinates are ignored like grid3d.rs:147. */
 WS3D_API ws3d_status ws3d_inject_impulse(ws3d_ctx *ctx, uint32_t x, uint32_t y, uint32_t z,
@@ -175,7 +181,9 @@ WS3D_API ws3d_status ws3d_max_pressure(ws3d_ctx *ctx, float *max_abs);
 /* GpuBackend3D::memory_usage (gpu_backend.rs:490-493): device bytes held. */
 WS3D_API size_t ws3d_memory_usage(const ws3d_ctx *ctx);
 
-/* Wait for every launch on the context's stream. */
+/* Wait for every launch on the context's stream.  Returns WS3D_ETIMEOUT
+ * when a bounded device wait of the z-slab exchange gave up since the last
+ * check (the status is cleared by reporting it). */
 WS3D_API ws3d_status ws3d_sync(ws3d_ctx *ctx);
 
 /* Use a caller-owned cudaStream_t (passed as void*) for every later launch;
@@ -184,6 +192,58 @@ WS3D_API ws3d_status ws3d_set_stream(ws3d_ctx *ctx, void *cuda_stream);
 WS3D_API ws3d_status ws3d_get_stream(const ws3d_ctx *ctx, void **cuda_stream);
 
 WS3D_API ws3d_status ws3d_stats_get(const ws3d_ctx *ctx, ws3d_stats *out);
+
+/* ---------------------------------------------------------------------------
+ * z-slab decomposition over several GPUs (one process per GPU).
+ *
+ * The reference has no multi-GPU FDTD; the exchange follows its P2P
+ * primitives (crates/ringkernel-cuda/src/multi_gpu/runtime.rs:377-434 peer
+ * enable, :782-870 cuMemcpyPeerAsync) but moves the halo inside the step
+ * kernel: the CTAs that compute a slab's first / last plane also store it
+ * into the neighbour's ghost plane over NVLink; a one-thread kernel then
+ * raises the neighbour's step-stamped flag (release, system scope); the
+ * neighbour's boundary CTAs wait for it (acquire, bounded) while its
+ * interior CTAs run.  Results are bit-identical to one GPU.
+ *
+ * Protocol (every rank, same order):
+ *   create with desc.z_begin/z_end -> upload -> ws3d_halo_export -> exchange
+ *   the handles (e.g. all_gather) -> ws3d_halo_attach(lower, upper) ->
+ *   ws3d_halo_sync(0) -> barrier -> ws3d_halo_sync(1) -> barrier -> steps.
+ * After any upload/reset, repeat the two ws3d_halo_sync phases.
+ * ------------------------------------------------------------------------- */
+typedef struct ws3d_halo_handles {
+    uint8_t buf[2][64];   /* cudaIpcMemHandle_t of both field buffers */
+    uint8_t flags[64];    /* cudaIpcMemHandle_t of the flag block */
+    uint32_t width, height, depth, pitch;
+    uint32_t z_begin, z_end;
+    int32_t device;
+    uint32_t reserved;
+} ws3d_halo_handles;
+
+/* Export this slab's buffers and flags for its neighbours. */
+WS3D_API ws3d_status ws3d_halo_export(ws3d_ctx *ctx, ws3d_halo_handles *out);
+
+/* Map the neighbours' exports (NULL at a global z face).  Fails with
+ * WS3D_EPEER when a mapping cannot be opened, WS3D_EINVAL when the slabs are
+ * not adjacent or differ in shape. */
+WS3D_API ws3d_status ws3d_halo_attach(ws3d_ctx *ctx, const ws3d_halo_handles *lower,
+                                      const ws3d_halo_handles *upper);
+
+/* In-process neighbours on the same device (tests and single-GPU slab
+ * splits): no device-side waits; advance them together with ws3d_step_group
+ * on one shared stream. */
+WS3D_API ws3d_status ws3d_halo_attach_local(ws3d_ctx *ctx, ws3d_ctx *lower, ws3d_ctx *upper);
+
+/* Phase 0: wait for this slab's stream (no signal of an earlier step stays in
+ * flight).  Phase 1: clear this slab's flags, copy its first and last planes
+ * into the neighbours' ghost planes and wait for the copies.  Run phase 0 on
+ * every rank, barrier, phase 1 on every rank, barrier. */
+WS3D_API ws3d_status ws3d_halo_sync(ws3d_ctx *ctx, uint32_t phase);
+
+/* Advance same-device slab contexts (ws3d_halo_attach_local) in lockstep:
+ * per step, every context's sources, then every context's step kernel, all
+ * on their shared stream. */
+WS3D_API ws3d_status ws3d_step_group(ws3d_ctx *const *ctxs, uint32_t n, uint64_t steps);
 
 #ifdef __cplusplus
 }

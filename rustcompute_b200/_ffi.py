@@ -66,6 +66,21 @@ class ws3d_stats(C.Structure):
     ]
 
 
+class ws3d_halo_handles(C.Structure):
+    _fields_ = [
+        ("buf", (C.c_uint8 * 64) * 2),
+        ("flags", C.c_uint8 * 64),
+        ("width", C.c_uint32),
+        ("height", C.c_uint32),
+        ("depth", C.c_uint32),
+        ("pitch", C.c_uint32),
+        ("z_begin", C.c_uint32),
+        ("z_end", C.c_uint32),
+        ("device", C.c_int32),
+        ("reserved", C.c_uint32),
+    ]
+
+
 _P = C.c_void_p
 _F = C.POINTER(C.c_float)
 _U8 = C.POINTER(C.c_uint8)
@@ -87,6 +102,7 @@ SIGNATURES = {
     "ws3d_set_c2_field": (C.c_int, [_CTX, _F]),
     "ws3d_set_sources": (C.c_int, [_CTX, C.c_uint32, _U32, _F, C.c_uint64]),
     "ws3d_step": (C.c_int, [_CTX, C.c_uint64]),
+    "ws3d_step_timed": (C.c_int, [_CTX, C.c_uint64, C.POINTER(C.c_double)]),
     "ws3d_inject_impulse": (C.c_int, [_CTX, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float]),
     "ws3d_inject_spherical_impulse": (
         C.c_int, [_CTX, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float]),
@@ -97,6 +113,12 @@ SIGNATURES = {
     "ws3d_set_stream": (C.c_int, [_CTX, _P]),
     "ws3d_get_stream": (C.c_int, [_CTX, C.POINTER(_P)]),
     "ws3d_stats_get": (C.c_int, [_CTX, C.POINTER(ws3d_stats)]),
+    "ws3d_halo_export": (C.c_int, [_CTX, C.POINTER(ws3d_halo_handles)]),
+    "ws3d_halo_attach": (C.c_int, [_CTX, C.POINTER(ws3d_halo_handles),
+                                   C.POINTER(ws3d_halo_handles)]),
+    "ws3d_halo_attach_local": (C.c_int, [_CTX, _CTX, _CTX]),
+    "ws3d_halo_sync": (C.c_int, [_CTX, C.c_uint32]),
+    "ws3d_step_group": (C.c_int, [C.POINTER(_CTX), C.c_uint32, C.c_uint64]),
 }
 
 _lib = None

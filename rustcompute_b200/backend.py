@@ -117,16 +117,18 @@ class GpuBackend3D:
     def create(cls, width: int, height: int, depth: int, *, c_squared: float = 0.25,
                damping: float = 1.0, device: int = 0, variant: str = "zstream",
                sponge_width: int = 0, sponge_max: float = 0.0, z_begin: int = 0,
-               z_end: int = 0) -> "GpuBackend3D":
-        """A backend without a host grid (fields start at zero)."""
+               z_end: int = 0, spin_budget_ns: int = 0) -> "GpuBackend3D":
+        """A backend without a host grid (fields start at zero).  z_begin/z_end
+        select a z-slab; spin_budget_ns bounds the device-side halo waits
+        (0 = library default, 2 s)."""
         self = cls.__new__(cls)
         self._open(width, height, depth, c_squared, damping, device=device, variant=variant,
                    sponge_width=sponge_width, sponge_max=sponge_max, z_begin=z_begin,
-                   z_end=z_end)
+                   z_end=z_end, spin_budget_ns=spin_budget_ns)
         return self
 
     def _open(self, width, height, depth, c_squared, damping, *, device, variant,
-              sponge_width, sponge_max, z_begin, z_end):
+              sponge_width, sponge_max, z_begin, z_end, spin_budget_ns=0):
         self._ctx = None
         self._lib = _ffi.load()
         d = _ffi.ws3d_desc()
@@ -137,6 +139,7 @@ class GpuBackend3D:
         d.sponge_max = np.float32(sponge_max)
         d.device = int(device)
         d.z_begin, d.z_end = int(z_begin), int(z_end)
+        d.spin_budget = int(spin_budget_ns)
         if variant not in VARIANTS:
             raise InvalidArgument(f"unknown variant {variant!r}; one of {sorted(VARIANTS)}")
         d.variant = VARIANTS[variant]
@@ -186,6 +189,13 @@ class GpuBackend3D:
         self._chk(self._lib.ws3d_step(self._ctx, int(n)), "GpuBackend3D::step_n")
         if grid is not None:
             grid.advance_clock(n)
+
+    def step_timed(self, n: int) -> float:
+        """`n` steps; returns the summed device time of the step-kernel launches
+        in ms (CUDA events on the launch stream).  Synchronises."""
+        out = C.c_double()
+        self._chk(self._lib.ws3d_step_timed(self._ctx, int(n), C.byref(out)), "step_timed")
+        return float(out.value)
 
     def download_pressure(self, grid: SimulationGrid3D, with_prev: bool = False) -> None:
         """gpu_backend.rs:383-388 (synchronous)."""

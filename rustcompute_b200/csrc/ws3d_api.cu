@@ -37,6 +37,8 @@ struct ws3d_ctx {
     float* wavelet = nullptr;
     uint32_t n_src = 0;
     uint64_t wl_len = 0;
+    long long* src_ghost = nullptr;   // per source: (row in the neighbour's ghost plane or -1, side)
+    std::vector<uint32_t> src_xyz;    // local sources, global coordinates
     double* red_scratch = nullptr;  // reduction partials + result
     uint32_t red_blocks = 0;
     cudaStream_t own_stream = nullptr;
@@ -46,6 +48,23 @@ struct ws3d_ctx {
     size_t device_bytes = 0;
     int sm_count = 0;
     std::string err;
+
+    // z-slab halo exchange
+    bool halo = false;               // neighbours attached
+    bool host_ordered = false;       // same-device neighbours: stream order, no device waits
+    bool halo_synced = false;        // ghost planes hold the neighbours' current boundary planes
+    float* lo_base[2] = {nullptr, nullptr};  // lower neighbour's buffers (mapped)
+    float* hi_base[2] = {nullptr, nullptr};  // upper neighbour's buffers (mapped)
+    uint64_t lo_ghost_off = 0;       // elements from lower's buffer base to its upper ghost
+    unsigned long long* flags = nullptr;     // [0] from lower, [1] from upper, [2] status
+    unsigned long long* lo_flag = nullptr;   // lower neighbour's flags[1]
+    unsigned long long* hi_flag = nullptr;   // upper neighbour's flags[0]
+    std::vector<void*> ipc_opened;   // mappings to close on destroy
+    uint64_t halo_steps = 0;         // steps since the last halo sync
+    uint64_t budget_ns = 2000000000ull;
+
+    // optional per-launch timing of the step kernel (ws3d_step_timed)
+    std::vector<cudaEvent_t> tev;
 };
 
 namespace {
@@ -137,6 +156,20 @@ StepParams make_params(const ws3d_ctx* c) {
     a.c2 = c->desc.c_squared;
     a.damping = c->desc.damping;
     a.sponge_w = c->sponge_w;
+    if (c->halo) {
+        const int nxt = c->cur ^ 1;
+        a.peer_lo = c->lo_base[nxt] ? c->lo_base[nxt] + c->lo_ghost_off : nullptr;
+        a.peer_hi = c->hi_base[nxt];
+        if (!c->host_ordered) {
+            a.wait_lo = c->lo_base[0] ? c->flags + 0 : nullptr;
+            a.wait_hi = c->hi_base[0] ? c->flags + 1 : nullptr;
+        }
+        // Before step s a neighbour raises its flag to s+1 (after its step s-1
+        // and after its sources of step s reached our ghost planes).
+        a.wait_val = c->halo_steps + 1;
+        a.budget_ns = c->budget_ns;
+        a.status = reinterpret_cast<unsigned int*>(c->flags + 2);
+    }
     return a;
 }
 
@@ -159,26 +192,19 @@ ws3d_status d2h_pitched(ws3d_ctx* c, T* dst, const T* src_slab, ws3d_status code
     return WS3D_OK;
 }
 
-// Launch geometry of the z-streaming kernel.
-constexpr int kTY = 8;
+// Halo flag block: [0] raised by the lower neighbour, [1] by the upper one,
+// [2] status word; padded to 256 bytes.
+constexpr size_t kFlagWords = 32;
 
-uint32_t zstream_chunk(const ws3d_ctx* c) {
-    const uint32_t tiles = ((c->pitch + 127) / 128) * ((c->H + kTY - 1) / kTY);
-    // Enough CTAs for ~8 resident waves over the SMs, but chunks of at least
-    // 16 planes so the two extra planes a chunk re-reads stay cheap.
-    const uint32_t want = (uint32_t)std::max(1, c->sm_count) * 3u * 8u;
-    uint32_t nchunks = std::max(1u, (want + tiles - 1) / tiles);
-    uint32_t chunk = (c->nz + nchunks - 1) / nchunks;
-    chunk = std::max(chunk, 16u);
-    return std::min(chunk, std::max(c->nz, 1u));
-}
+// Launch geometry of the z-streaming kernel (ws3d_index.h).
+constexpr int kTY = 8;
 
 template <bool kC2F, bool kCells>
 void launch_zstream(const ws3d_ctx* c, const StepParams& a) {
-    const uint32_t chunk = zstream_chunk(c);
-    dim3 block(32, kTY, 1);
-    dim3 grid((c->pitch + 127) / 128, (c->H + kTY - 1) / kTY, (c->nz + chunk - 1) / chunk);
-    k_step_zstream<kC2F, kCells, kTY><<<grid, block, 0, c->stream>>>(a, chunk);
+    const uint32_t chunk = zs_zchunk<kTY>(c->pitch, c->H, c->nz, c->sm_count);
+    uint32_t gx, gy, gz;
+    zs_grid<kTY>(c->pitch, c->H, c->nz, chunk, &gx, &gy, &gz);
+    k_step_zstream<kC2F, kCells, kTY><<<dim3(gx, gy, gz), dim3(32, kTY, 1), 0, c->stream>>>(a, chunk);
 }
 
 template <bool kC2F, bool kCells>
@@ -262,6 +288,59 @@ ws3d_status ensure_cell_arrays(ws3d_ctx* c) {
         c->types_hold_default = true;
     }
     return WS3D_OK;
+}
+
+// Per-source (row in the neighbour's ghost plane, side) for sources on the
+// first or last owned plane; -1 rows elsewhere or without neighbours.
+ws3d_status rebuild_source_ghosts(ws3d_ctx* c) {
+    dfree(c, c->src_ghost, 2 * (size_t)c->n_src);
+    if (!c->halo || c->n_src == 0) return WS3D_OK;
+    std::vector<long long> gr(2 * (size_t)c->n_src, -1);
+    bool any = false;
+    for (uint32_t k = 0; k < c->n_src; ++k) {
+        const uint32_t x = c->src_xyz[3 * k], y = c->src_xyz[3 * k + 1], z = c->src_xyz[3 * k + 2];
+        const long long row = (long long)y * c->pitch + x;
+        if (z == c->z0 && c->lo_base[0]) {
+            gr[2 * k] = (long long)c->lo_ghost_off + row;  // relative to the lower buffer base
+            gr[2 * k + 1] = 0;
+            any = true;
+        } else if (z == c->z0 + c->nz - 1 && c->hi_base[0]) {
+            gr[2 * k] = row;                                 // upper's lower ghost = its base
+            gr[2 * k + 1] = 1;
+            any = true;
+        }
+    }
+    if (!any) return WS3D_OK;
+    ws3d_status s = dalloc(c, &c->src_ghost, gr.size(), "source ghosts");
+    if (s != WS3D_OK) return s;
+    WS3D_CUDA(c, cudaMemcpy(c->src_ghost, gr.data(), gr.size() * sizeof(long long),
+                            cudaMemcpyHostToDevice),
+              WS3D_EMEMORY);
+    return WS3D_OK;
+}
+
+ws3d_status launch_sources(ws3d_ctx* c) {
+    if (!c->n_src) return WS3D_OK;
+    float* glo = c->lo_base[c->cur];  // neighbours' current pressure buffers
+    float* ghi = c->hi_base[c->cur];
+    k_inject_sources<<<1, 32, 0, c->stream>>>(c->buf[c->cur], c->buf[c->cur ^ 1], c->src_off,
+                                              c->wavelet, c->n_src, c->wl_len, c->step,
+                                              c->src_ghost, glo, ghi);
+    return check_launch(c, "k_inject_sources");
+}
+
+// Read (and clear) the device status word the bounded waits write.
+ws3d_status check_device_status(ws3d_ctx* c) {
+    if (!c->halo || c->host_ordered) return WS3D_OK;
+    unsigned int st = 0;
+    WS3D_CUDA(c, cudaMemcpy(&st, c->flags + 2, sizeof st, cudaMemcpyDeviceToHost), WS3D_EDEVICE);
+    if (!st) return WS3D_OK;
+    WS3D_CUDA(c, cudaMemset(c->flags + 2, 0, sizeof(unsigned long long)), WS3D_EDEVICE);
+    return fail(c, WS3D_ETIMEOUT,
+                "a step gave up waiting for the %s%s%s neighbour after %.3f s (its flag never "
+                "reached the step); the field of that step is not valid",
+                (st & 1u) ? "lower" : "", (st & 3u) == 3u ? " and " : "",
+                (st & 2u) ? "upper" : "", c->budget_ns * 1e-9);
 }
 
 bool desc_ok(const ws3d_desc* d, std::string* why) {
@@ -384,6 +463,10 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
         e = cudaMemcpy(c->sponge, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice);
         if (e != cudaSuccess) return bail(cuda_fail(c, WS3D_EMEMORY, e, "cudaMemcpy(sponge)"));
     }
+    if ((s = dalloc(c, &c->flags, kFlagWords, "halo flags")) != WS3D_OK) return bail(s);
+    e = cudaMemsetAsync(c->flags, 0, kFlagWords * sizeof(unsigned long long), c->stream);
+    if (e != cudaSuccess) return bail(cuda_fail(c, WS3D_EMEMORY, e, "cudaMemsetAsync(flags)"));
+    if (desc->spin_budget) c->budget_ns = desc->spin_budget;
     c->red_blocks = (uint32_t)std::max(1, c->sm_count) * 4u;
     if ((s = dalloc(c, &c->red_scratch, (size_t)c->red_blocks + 1, "reduction")) != WS3D_OK)
         return bail(s);
@@ -406,6 +489,11 @@ void ws3d_destroy(ws3d_ctx* c) {
         dfree(c, c->src_off, c->n_src);
         dfree(c, c->wavelet, (size_t)c->n_src * c->wl_len);
         dfree(c, c->red_scratch, (size_t)c->red_blocks + 1);
+        dfree(c, c->src_ghost, 2 * (size_t)c->n_src);
+        dfree(c, c->flags, kFlagWords);
+        for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
+        for (cudaEvent_t ev : c->tev) cudaEventDestroy(ev);
+        c->ipc_opened.clear();
         if (c->own_stream) cudaStreamDestroy(c->own_stream);
     }
     delete c;
@@ -419,6 +507,7 @@ ws3d_status ws3d_upload(ws3d_ctx* c, const float* p, const float* pp) {
     ws3d_status s = WS3D_OK;
     if (p && (s = h2d_pitched(c, c->buf[c->cur], p)) != WS3D_OK) return s;
     if (pp && (s = h2d_pitched(c, c->buf[c->cur ^ 1], pp)) != WS3D_OK) return s;
+    if (p) c->halo_synced = false;
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EMEMORY);
     return WS3D_OK;
 }
@@ -437,6 +526,7 @@ ws3d_status ws3d_reset(ws3d_ctx* c, const float* p, const float* pp) {
     if (!c) return WS3D_EINVAL;
     c->cur = 0;
     c->step = 0;
+    c->halo_synced = false;
     DeviceGuard g(c->desc.device);
     for (int b = 0; b < 2; ++b)
         WS3D_CUDA(c, cudaMemsetAsync(c->buf[b], 0, c->slab * sizeof(float), c->stream),
@@ -514,23 +604,27 @@ ws3d_status ws3d_set_sources(ws3d_ctx* c, uint32_t n, const uint32_t* xyz, const
     if (n > 0 && (!xyz || !wavelet || len == 0))
         return fail(c, WS3D_EINVAL, "set_sources: xyz/wavelet missing");
     if (n > 65536) return fail(c, WS3D_EINVAL, "set_sources: more than 65536 sources");
+    for (uint32_t k = 0; k < n; ++k)
+        if (xyz[3 * k] >= c->W || xyz[3 * k + 1] >= c->H || xyz[3 * k + 2] >= c->Dg)
+            return fail(c, WS3D_EINVAL, "set_sources: source %u at (%u,%u,%u) outside the grid",
+                        k, xyz[3 * k], xyz[3 * k + 1], xyz[3 * k + 2]);
     DeviceGuard g(c->desc.device);
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
     dfree(c, c->src_off, c->n_src);
     dfree(c, c->wavelet, (size_t)c->n_src * c->wl_len);
+    dfree(c, c->src_ghost, 2 * (size_t)c->n_src);
     c->n_src = 0;
     c->wl_len = 0;
+    c->src_xyz.clear();
     // Keep only the sources inside the owned planes, in their given order.
     std::vector<uint64_t> off;
     std::vector<float> wl;
     for (uint32_t k = 0; k < n; ++k) {
         const uint32_t x = xyz[3 * k], y = xyz[3 * k + 1], z = xyz[3 * k + 2];
-        if (x >= c->W || y >= c->H || z >= c->Dg)
-            return fail(c, WS3D_EINVAL, "set_sources: source %u at (%u,%u,%u) outside the grid",
-                        k, x, y, z);
         if (z < c->z0 || z >= c->z0 + c->nz) continue;
         off.push_back((uint64_t)(z - c->z0 + 1) * c->plane + (uint64_t)y * c->pitch + x);
         wl.insert(wl.end(), wavelet + (size_t)k * len, wavelet + (size_t)(k + 1) * len);
+        c->src_xyz.insert(c->src_xyz.end(), {x, y, z});
     }
     if (off.empty()) return WS3D_OK;
     ws3d_status s;
@@ -542,27 +636,125 @@ ws3d_status ws3d_set_sources(ws3d_ctx* c, uint32_t n, const uint32_t* xyz, const
               WS3D_EMEMORY);
     c->n_src = (uint32_t)off.size();
     c->wl_len = len;
+    return rebuild_source_ghosts(c);
+}
+
+namespace {
+ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed) {
+    if (c->halo && c->host_ordered)
+        return fail(c, WS3D_ECOMMAND, "step: same-device slabs advance through ws3d_step_group");
+    if (c->halo && !c->halo_synced)
+        return fail(c, WS3D_ECOMMAND, "step: fields changed since the last ws3d_halo_sync");
+    if (timed) {
+        while (c->tev.size() < 2 * n) {
+            cudaEvent_t ev;
+            WS3D_CUDA(c, cudaEventCreate(&ev), WS3D_EDEVICE);
+            c->tev.push_back(ev);
+        }
+    }
+    for (uint64_t i = 0; i < n; ++i) {
+        ws3d_status s = launch_sources(c);
+        if (s != WS3D_OK) return s;
+        if (c->halo) {
+            // Tell the neighbours that this slab finished its previous step (its
+            // ghost writes into them and its reads of its own ghosts) and that the
+            // sources of this step are in their ghost copies: their step may start.
+            k_halo_signal<<<1, 32, 0, c->stream>>>(c->lo_flag, c->hi_flag, c->halo_steps + 1);
+            if ((s = check_launch(c, "k_halo_signal")) != WS3D_OK) return s;
+        }
+        if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[2 * i], c->stream), WS3D_EDEVICE);
+        if ((s = launch_step(c)) != WS3D_OK) return s;
+        if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[2 * i + 1], c->stream), WS3D_EDEVICE);
+        c->cur ^= 1;
+        c->step++;
+        c->halo_steps++;
+    }
     return WS3D_OK;
 }
+}  // namespace
 
 ws3d_status ws3d_step(ws3d_ctx* c, uint64_t n) {
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
-    for (uint64_t i = 0; i < n; ++i) {
-        if (c->n_src) {
-            k_inject_sources<<<1, 32, 0, c->stream>>>(c->buf[c->cur], c->buf[c->cur ^ 1],
-                                                      c->src_off, c->wavelet, c->n_src,
-                                                      c->wl_len, c->step);
-            ws3d_status s = check_launch(c, "k_inject_sources");
-            if (s != WS3D_OK) return s;
-        }
-        ws3d_status s = launch_step(c);
-        if (s != WS3D_OK) return s;
-        c->cur ^= 1;
-        c->step++;
-    }
-    return WS3D_OK;
+    return step_impl(c, n, false);
 }
+
+ws3d_status ws3d_step_timed(ws3d_ctx* c, uint64_t n, double* kernel_ms) {
+    if (!c || !kernel_ms) return c ? fail(c, WS3D_EINVAL, "step_timed: kernel_ms is NULL")
+                                   : WS3D_EINVAL;
+    if (n > (1u << 20)) return fail(c, WS3D_EINVAL, "step_timed: more than 2^20 steps");
+    DeviceGuard g(c->desc.device);
+    ws3d_status s = step_impl(c, n, true);
+    if (s != WS3D_OK) return s;
+    WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_ELAUNCH);
+    double tot = 0.0;
+    for (uint64_t i = 0; i < n; ++i) {
+        float ms = 0.f;
+        WS3D_CUDA(c, cudaEventElapsedTime(&ms, c->tev[2 * i], c->tev[2 * i + 1]), WS3D_EDEVICE);
+        tot += ms;
+    }
+    *kernel_ms = tot;
+    return check_device_status(c);
+}
+
+namespace {
+// Add amp*factor to the listed cells (and amp*factor*0.5 to p_prev), and to
+// the neighbours' ghost copies of the cells on the first / last owned plane.
+ws3d_status apply_impulse_table(ws3d_ctx* c, const std::vector<uint64_t>& off,
+                                const std::vector<float>& fac, const std::vector<uint64_t>& glo,
+                                const std::vector<float>& flo, const std::vector<uint64_t>& ghi,
+                                const std::vector<float>& fhi, float amp) {
+    struct Part { const std::vector<uint64_t>* o; const std::vector<float>* f; float* ghost; };
+    const Part parts[3] = {{&off, &fac, nullptr},
+                           {&glo, &flo, c->lo_base[c->cur] ? c->lo_base[c->cur] + c->lo_ghost_off : nullptr},
+                           {&ghi, &fhi, c->hi_base[c->cur]}};
+    ws3d_status s = WS3D_OK;
+    for (int k = 0; k < 3 && s == WS3D_OK; ++k) {
+        const Part& q = parts[k];
+        if (q.o->empty() || (k > 0 && !q.ghost)) continue;
+        uint64_t* d_off = nullptr;
+        float* d_fac = nullptr;
+        if ((s = dalloc(c, &d_off, q.o->size(), "impulse offsets")) != WS3D_OK) return s;
+        if ((s = dalloc(c, &d_fac, q.f->size(), "impulse factors")) != WS3D_OK) {
+            dfree(c, d_off, q.o->size());
+            return s;
+        }
+        cudaError_t e1 = cudaMemcpyAsync(d_off, q.o->data(), q.o->size() * 8,
+                                         cudaMemcpyHostToDevice, c->stream);
+        cudaError_t e2 = cudaMemcpyAsync(d_fac, q.f->data(), q.f->size() * 4,
+                                         cudaMemcpyHostToDevice, c->stream);
+        const uint32_t n = (uint32_t)q.o->size();
+        if (e1 != cudaSuccess || e2 != cudaSuccess) {
+            s = cuda_fail(c, WS3D_EMEMORY, e1 != cudaSuccess ? e1 : e2, "cudaMemcpyAsync(impulse)");
+        } else if (k == 0) {
+            k_inject_table<<<(n + 255) / 256, 256, 0, c->stream>>>(
+                c->buf[c->cur], c->buf[c->cur ^ 1], d_off, d_fac, n, amp);
+            s = check_launch(c, "k_inject_table");
+        } else {
+            k_inject_ghost<<<(n + 255) / 256, 256, 0, c->stream>>>(q.ghost, d_off, d_fac, n, amp);
+            s = check_launch(c, "k_inject_ghost");
+        }
+        cudaStreamSynchronize(c->stream);
+        dfree(c, d_off, q.o->size());
+        dfree(c, d_fac, q.f->size());
+    }
+    return s;
+}
+
+// Collect (offset, factor) for the cells of an impulse that this slab owns.
+struct ImpulseCells {
+    std::vector<uint64_t> off, glo, ghi;
+    std::vector<float> fac, flo, fhi;
+    void add(const ws3d_ctx* c, uint32_t x, uint32_t y, uint32_t z, float f) {
+        if (z < c->z0 || z >= c->z0 + c->nz) return;
+        const uint64_t row = (uint64_t)y * c->pitch + x;
+        off.push_back((uint64_t)(z - c->z0 + 1) * c->plane + row);
+        fac.push_back(f);
+        if (z == c->z0 && c->lo_base[0]) { glo.push_back(row); flo.push_back(f); }
+        if (z + 1 == c->z0 + c->nz && c->hi_base[0]) { ghi.push_back(row); fhi.push_back(f); }
+    }
+};
+}  // namespace
 
 ws3d_status ws3d_inject_impulse(ws3d_ctx* c, uint32_t x, uint32_t y, uint32_t z, float amp) {
     if (!c) return WS3D_EINVAL;
@@ -570,8 +762,16 @@ ws3d_status ws3d_inject_impulse(ws3d_ctx* c, uint32_t x, uint32_t y, uint32_t z,
     if (z < c->z0 || z >= c->z0 + c->nz) return WS3D_OK;      // another slab owns it
     DeviceGuard g(c->desc.device);
     const uint64_t off = (uint64_t)(z - c->z0 + 1) * c->plane + (uint64_t)y * c->pitch + x;
-    k_inject_point<<<1, 32, 0, c->stream>>>(c->buf[c->cur], c->buf[c->cur ^ 1], off, amp);
-    return check_launch(c, "k_inject_point");
+    const bool on_lo = z == c->z0 && c->lo_base[0], on_hi = z + 1 == c->z0 + c->nz && c->hi_base[0];
+    if (!on_lo && !on_hi) {
+        k_inject_point<<<1, 32, 0, c->stream>>>(c->buf[c->cur], c->buf[c->cur ^ 1], off, amp);
+        return check_launch(c, "k_inject_point");
+    }
+    // amp * 1.0f == amp exactly, so the table path adds the same values.
+    ImpulseCells cells;
+    cells.add(c, x, y, z, 1.0f);
+    return apply_impulse_table(c, cells.off, cells.fac, cells.glo, cells.flo, cells.ghi, cells.fhi,
+                               amp);
 }
 
 ws3d_status ws3d_inject_spherical_impulse(ws3d_ctx* c, uint32_t cx, uint32_t cy, uint32_t cz,
@@ -583,8 +783,7 @@ ws3d_status ws3d_inject_spherical_impulse(ws3d_ctx* c, uint32_t cx, uint32_t cy,
     DeviceGuard g(c->desc.device);
     const int r = (int)radius;
     const float r_sq = radius * radius;
-    std::vector<uint64_t> off;
-    std::vector<float> fac;
+    ImpulseCells cells;
     for (int dz = -r; dz <= r; ++dz)
         for (int dy = -r; dy <= r; ++dy)
             for (int dx = -r; dx <= r; ++dx) {
@@ -593,36 +792,12 @@ ws3d_status ws3d_inject_spherical_impulse(ws3d_ctx* c, uint32_t cx, uint32_t cy,
                 if (x < 0 || y < 0 || z < 0 || x >= c->W || y >= c->H || z >= c->Dg) continue;
                 const float dist_sq = (float)(dx * dx + dy * dy + dz * dz);
                 if (!(dist_sq <= r_sq)) continue;
-                if (z < c->z0 || z >= (long long)c->z0 + c->nz) continue;
-                off.push_back((uint64_t)(z - c->z0 + 1) * c->plane + (uint64_t)y * c->pitch +
-                              (uint64_t)x);
-                fac.push_back(expf(-dist_sq / (2.0f * radius)));
+                cells.add(c, (uint32_t)x, (uint32_t)y, (uint32_t)z,
+                          expf(-dist_sq / (2.0f * radius)));
             }
-    if (off.empty()) return WS3D_OK;
-    uint64_t* d_off = nullptr;
-    float* d_fac = nullptr;
-    ws3d_status s;
-    if ((s = dalloc(c, &d_off, off.size(), "impulse offsets")) != WS3D_OK) return s;
-    if ((s = dalloc(c, &d_fac, fac.size(), "impulse factors")) != WS3D_OK) {
-        dfree(c, d_off, off.size());
-        return s;
-    }
-    cudaError_t e1 = cudaMemcpyAsync(d_off, off.data(), off.size() * 8, cudaMemcpyHostToDevice,
-                                     c->stream);
-    cudaError_t e2 = cudaMemcpyAsync(d_fac, fac.data(), fac.size() * 4, cudaMemcpyHostToDevice,
-                                     c->stream);
-    if (e1 == cudaSuccess && e2 == cudaSuccess) {
-        const uint32_t n = (uint32_t)off.size();
-        k_inject_table<<<(n + 255) / 256, 256, 0, c->stream>>>(c->buf[c->cur], c->buf[c->cur ^ 1],
-                                                              d_off, d_fac, n, amp);
-        s = check_launch(c, "k_inject_table");
-    } else {
-        s = cuda_fail(c, WS3D_EMEMORY, e1 != cudaSuccess ? e1 : e2, "cudaMemcpyAsync(impulse)");
-    }
-    cudaStreamSynchronize(c->stream);
-    dfree(c, d_off, off.size());
-    dfree(c, d_fac, fac.size());
-    return s;
+    if (cells.off.empty()) return WS3D_OK;
+    return apply_impulse_table(c, cells.off, cells.fac, cells.glo, cells.flo, cells.ghi, cells.fhi,
+                               amp);
 }
 
 ws3d_status ws3d_energy(ws3d_ctx* c, double* out) {
@@ -667,7 +842,7 @@ ws3d_status ws3d_sync(ws3d_ctx* c) {
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_ELAUNCH);
-    return WS3D_OK;
+    return check_device_status(c);
 }
 
 ws3d_status ws3d_set_stream(ws3d_ctx* c, void* stream) {
@@ -700,6 +875,185 @@ ws3d_status ws3d_stats_get(const ws3d_ctx* c, ws3d_stats* o) {
     o->has_c2_field = c->c2f != nullptr;
     o->has_cell_field = !c->cells_default;
     o->n_sources = c->n_src;
+    return WS3D_OK;
+}
+
+
+// ---------------------------------------------------------------------------
+// z-slab halo exchange.
+// ---------------------------------------------------------------------------
+namespace {
+ws3d_status attach_common(ws3d_ctx* c, bool has_lo, uint32_t lo_nz, bool has_hi) {
+    c->halo = has_lo || has_hi;
+    c->halo_synced = false;
+    c->halo_steps = 0;
+    c->lo_ghost_off = has_lo ? (uint64_t)(lo_nz + 1) * c->plane : 0;
+    if (c->desc.variant != WS3D_VARIANT_ZSTREAM && c->halo)
+        return fail(c, WS3D_EINVAL, "halo exchange needs the zstream variant");
+    return rebuild_source_ghosts(c);
+}
+
+bool same_geometry(const ws3d_ctx* c, uint32_t W, uint32_t H, uint32_t D, uint32_t pitch) {
+    return W == c->W && H == c->H && D == c->Dg && pitch == c->pitch;
+}
+}  // namespace
+
+ws3d_status ws3d_halo_export(ws3d_ctx* c, ws3d_halo_handles* out) {
+    if (!c || !out) return c ? fail(c, WS3D_EINVAL, "halo_export: out is NULL") : WS3D_EINVAL;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    DeviceGuard g(c->desc.device);
+    std::memset(out, 0, sizeof *out);
+    cudaIpcMemHandle_t h;
+    for (int b = 0; b < 2; ++b) {
+        WS3D_CUDA(c, cudaIpcGetMemHandle(&h, c->buf[b]), WS3D_EPEER);
+        std::memcpy(out->buf[b], &h, 64);
+    }
+    WS3D_CUDA(c, cudaIpcGetMemHandle(&h, c->flags), WS3D_EPEER);
+    std::memcpy(out->flags, &h, 64);
+    out->width = c->W;
+    out->height = c->H;
+    out->depth = c->Dg;
+    out->pitch = c->pitch;
+    out->z_begin = c->z0;
+    out->z_end = c->z0 + c->nz;
+    out->device = c->desc.device;
+    return WS3D_OK;
+}
+
+ws3d_status ws3d_halo_attach(ws3d_ctx* c, const ws3d_halo_handles* lo, const ws3d_halo_handles* hi) {
+    if (!c) return WS3D_EINVAL;
+    if (c->halo) return fail(c, WS3D_EPEER, "halo_attach: neighbours already attached");
+    if (lo && (!same_geometry(c, lo->width, lo->height, lo->depth, lo->pitch) || lo->z_end != c->z0))
+        return fail(c, WS3D_EINVAL, "halo_attach: lower slab [%u,%u) does not end at %u or differs in shape",
+                    lo->z_begin, lo->z_end, c->z0);
+    if (hi && (!same_geometry(c, hi->width, hi->height, hi->depth, hi->pitch) ||
+               hi->z_begin != c->z0 + c->nz))
+        return fail(c, WS3D_EINVAL, "halo_attach: upper slab [%u,%u) does not start at %u or differs in shape",
+                    hi->z_begin, hi->z_end, c->z0 + c->nz);
+    if ((lo && c->z0 == 0) || (hi && c->z0 + c->nz == c->Dg) || (!lo && c->z0 > 0) ||
+        (!hi && c->z0 + c->nz < c->Dg))
+        return fail(c, WS3D_EINVAL, "halo_attach: neighbours do not match the slab position");
+    DeviceGuard g(c->desc.device);
+    auto open = [&](const uint8_t* bytes, void** ptr) -> ws3d_status {
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, bytes, 64);
+        cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return cuda_fail(c, WS3D_EPEER, e, "cudaIpcOpenMemHandle");
+        c->ipc_opened.push_back(*ptr);
+        return WS3D_OK;
+    };
+    ws3d_status s;
+    void* q = nullptr;
+    if (lo) {
+        for (int b = 0; b < 2; ++b) {
+            if ((s = open(lo->buf[b], &q)) != WS3D_OK) return s;
+            c->lo_base[b] = static_cast<float*>(q);
+        }
+        if ((s = open(lo->flags, &q)) != WS3D_OK) return s;
+        c->lo_flag = static_cast<unsigned long long*>(q) + 1;  // I am its upper neighbour
+    }
+    if (hi) {
+        for (int b = 0; b < 2; ++b) {
+            if ((s = open(hi->buf[b], &q)) != WS3D_OK) return s;
+            c->hi_base[b] = static_cast<float*>(q);
+        }
+        if ((s = open(hi->flags, &q)) != WS3D_OK) return s;
+        c->hi_flag = static_cast<unsigned long long*>(q) + 0;  // I am its lower neighbour
+    }
+    c->host_ordered = false;
+    return attach_common(c, lo != nullptr, lo ? lo->z_end - lo->z_begin : 0, hi != nullptr);
+}
+
+ws3d_status ws3d_halo_attach_local(ws3d_ctx* c, ws3d_ctx* lo, ws3d_ctx* hi) {
+    if (!c) return WS3D_EINVAL;
+    if (c->halo) return fail(c, WS3D_EPEER, "halo_attach_local: neighbours already attached");
+    for (ws3d_ctx* n : {lo, hi}) {
+        if (!n) continue;
+        if (!same_geometry(c, n->W, n->H, n->Dg, n->pitch))
+            return fail(c, WS3D_EINVAL, "halo_attach_local: neighbour differs in shape");
+        if (n->desc.device != c->desc.device)
+            return fail(c, WS3D_EINVAL,
+                        "halo_attach_local: neighbours on other devices attach through "
+                        "ws3d_halo_export / ws3d_halo_attach (one process per GPU)");
+    }
+    if ((lo && lo->z0 + lo->nz != c->z0) || (hi && hi->z0 != c->z0 + c->nz) ||
+        (!lo && c->z0 > 0) || (!hi && c->z0 + c->nz < c->Dg))
+        return fail(c, WS3D_EINVAL, "halo_attach_local: neighbours do not match the slab position");
+    if (lo) {
+        c->lo_base[0] = lo->buf[0];
+        c->lo_base[1] = lo->buf[1];
+        c->lo_flag = lo->flags + 1;
+    }
+    if (hi) {
+        c->hi_base[0] = hi->buf[0];
+        c->hi_base[1] = hi->buf[1];
+        c->hi_flag = hi->flags + 0;
+    }
+    // Same device: the slabs advance in one stream through ws3d_step_group, so
+    // stream order replaces the device-side flags (two kernels that wait on one
+    // another never share a GPU).
+    c->host_ordered = true;
+    return attach_common(c, lo != nullptr, lo ? lo->nz : 0, hi != nullptr);
+}
+
+ws3d_status ws3d_halo_sync(ws3d_ctx* c, uint32_t phase) {
+    if (!c) return WS3D_EINVAL;
+    if (!c->halo) return WS3D_OK;
+    if (phase > 1) return fail(c, WS3D_EINVAL, "halo_sync: phase must be 0 or 1");
+    DeviceGuard g(c->desc.device);
+    // Phase 0: quiesce -- after it (and the barrier that follows on every
+    // rank) no signal of an earlier step is still in flight towards anyone.
+    WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
+    c->halo_synced = false;
+    if (phase == 0) return WS3D_OK;
+    // Phase 1: clear this slab's flags, then fill the neighbours' ghost planes
+    // with this slab's first / last plane of the current field.
+    WS3D_CUDA(c, cudaMemset(c->flags, 0, kFlagWords * sizeof(unsigned long long)), WS3D_EDEVICE);
+    c->halo_steps = 0;
+    const size_t bytes = c->plane * sizeof(float);
+    float* P = c->buf[c->cur];
+    if (c->lo_base[0])
+        WS3D_CUDA(c, cudaMemcpyAsync(c->lo_base[c->cur] + c->lo_ghost_off, P + c->plane, bytes,
+                                     cudaMemcpyDefault, c->stream),
+                  WS3D_EPEER);
+    if (c->hi_base[0])
+        WS3D_CUDA(c, cudaMemcpyAsync(c->hi_base[c->cur], P + (size_t)c->nz * c->plane, bytes,
+                                     cudaMemcpyDefault, c->stream),
+                  WS3D_EPEER);
+    WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EPEER);
+    c->halo_synced = true;
+    return WS3D_OK;
+}
+
+ws3d_status ws3d_step_group(ws3d_ctx* const* ctxs, uint32_t n, uint64_t steps) {
+    if (!ctxs || n == 0) return WS3D_EINVAL;
+    for (uint32_t k = 0; k < n; ++k) {
+        ws3d_ctx* c = ctxs[k];
+        if (!c) return WS3D_EINVAL;
+        if (c->desc.device != ctxs[0]->desc.device || c->stream != ctxs[0]->stream)
+            return fail(c, WS3D_EINVAL, "step_group: contexts must share one device and stream");
+        if (c->halo && !c->halo_synced)
+            return fail(c, WS3D_ECOMMAND, "step_group: fields changed since the last halo sync");
+        if (c->cur != ctxs[0]->cur || c->step != ctxs[0]->step)
+            return fail(c, WS3D_ECOMMAND, "step_group: contexts are at different steps");
+    }
+    DeviceGuard g(ctxs[0]->desc.device);
+    for (uint64_t s = 0; s < steps; ++s) {
+        // All sources first (they touch neighbours' ghost copies), then all steps.
+        for (uint32_t k = 0; k < n; ++k) {
+            ws3d_status st = launch_sources(ctxs[k]);
+            if (st != WS3D_OK) return st;
+        }
+        for (uint32_t k = 0; k < n; ++k) {
+            ws3d_status st = launch_step(ctxs[k]);
+            if (st != WS3D_OK) return st;
+        }
+        for (uint32_t k = 0; k < n; ++k) {
+            ctxs[k]->cur ^= 1;
+            ctxs[k]->step++;
+            ctxs[k]->halo_steps++;
+        }
+    }
     return WS3D_OK;
 }
 

@@ -1,0 +1,98 @@
+// ws3d_index.h -- address arithmetic of the step kernels, shared by the device
+// code and by a host-side bounds check (tests/index_check.cpp), which walks
+// every CTA, thread and plane of a launch and verifies that each load and
+// store the kernel issues stays inside the slab allocation.
+//
+// All offsets are signed 64-bit element offsets relative to owned plane 0 of
+// a slab (ghost plane -1 starts at -plane).  Every intermediate is widened to
+// int64 before subtraction, so no unsigned wrap-around can occur.
+#pragma once
+
+#include <stdint.h>
+
+#if defined(__CUDACC__)
+#define WS3D_HD __host__ __device__ __forceinline__
+#else
+#define WS3D_HD inline
+#endif
+
+namespace ws3d {
+
+constexpr int kZsTileX = 128;  // cells per CTA row (32 lanes x float4)
+
+// Per-thread constants of the z-streaming kernel.
+struct ZsLane {
+    int64_t row;    // offset of this thread's float4 inside a plane
+    int64_t rowlo;  // halo row y0-1 (valid when ylo)
+    int64_t rowhi;  // halo row y0+TY (valid when yhi)
+    int64_t offxl;  // halo float x0-1 (valid when xl)
+    int64_t offxr;  // halo float x0+128 (valid when xr)
+    uint32_t x, y, x0, y0;
+    bool act, ylo, yhi, xl, xr;
+};
+
+template <int TY>
+WS3D_HD ZsLane zs_lane(uint32_t bx, uint32_t by, int lane, int w, uint32_t W, uint32_t H,
+                       uint32_t pitch) {
+    ZsLane L;
+    L.x0 = bx * (uint32_t)kZsTileX;
+    L.x = L.x0 + 4u * (uint32_t)lane;
+    L.y0 = by * (uint32_t)TY;
+    L.y = L.y0 + (uint32_t)w;
+    const bool xin = L.x < pitch;
+    const bool yin = L.y < H;
+    L.act = xin && yin;
+    L.ylo = (w == 0) && (L.y0 > 0) && xin;
+    L.yhi = (w == TY - 1) && (L.y0 + (uint32_t)TY < H) && xin;
+    L.xl = (lane == 0) && (L.x0 > 0) && yin;
+    L.xr = (lane == 31) && (L.x0 + (uint32_t)kZsTileX < W) && yin;
+    const int64_t P = (int64_t)pitch;
+    L.row = (int64_t)L.y * P + (int64_t)L.x;
+    L.rowlo = ((int64_t)L.y0 - 1) * P + (int64_t)L.x;
+    L.rowhi = ((int64_t)L.y0 + TY) * P + (int64_t)L.x;
+    L.offxl = (int64_t)L.y * P + (int64_t)L.x0 - 1;
+    L.offxr = (int64_t)L.y * P + (int64_t)L.x0 + kZsTileX;
+    return L;
+}
+
+// Offset of plane `z` (may be -1 or nz: the ghosts).
+WS3D_HD int64_t zs_plane(int64_t z, int64_t plane) { return z * plane; }
+
+// Order in which z-chunks are assigned to blockIdx.z.  With a halo exchange,
+// chunk 0 and the last chunk (the ones that wait for a neighbour) go last.
+WS3D_HD uint32_t zs_chunk_order(uint32_t bz, uint32_t gz, bool halo) {
+    return (halo && gz > 1) ? (bz + 1) % gz : bz;
+}
+
+// z-range of CTA `bz`: [zb, ze), empty when zb >= nz.
+WS3D_HD void zs_chunk(uint32_t bz, uint32_t zchunk, uint32_t nz, uint32_t* zb, uint32_t* ze) {
+    const uint64_t b = (uint64_t)bz * zchunk;
+    *zb = b < nz ? (uint32_t)b : nz;
+    const uint64_t e = b + zchunk;
+    *ze = e < nz ? (uint32_t)e : nz;
+}
+
+// Launch geometry of the z-streaming kernel (host side).
+template <int TY>
+inline uint32_t zs_zchunk(uint32_t pitch, uint32_t H, uint32_t nz, int sm_count) {
+    const uint32_t tiles = ((pitch + kZsTileX - 1) / kZsTileX) * ((H + TY - 1) / TY);
+    // Enough CTAs for ~8 resident waves over the SMs, but chunks of at least
+    // 16 planes so the two extra planes a chunk re-reads stay cheap.
+    const uint32_t want = (uint32_t)(sm_count > 0 ? sm_count : 1) * 3u * 8u;
+    uint32_t nchunks = (want + tiles - 1) / tiles;
+    if (nchunks < 1) nchunks = 1;
+    uint32_t chunk = (nz + nchunks - 1) / nchunks;
+    if (chunk < 16) chunk = 16;
+    const uint32_t cap = nz > 0 ? nz : 1;
+    return chunk < cap ? chunk : cap;
+}
+
+template <int TY>
+inline void zs_grid(uint32_t pitch, uint32_t H, uint32_t nz, uint32_t zchunk, uint32_t* gx,
+                    uint32_t* gy, uint32_t* gz) {
+    *gx = (pitch + kZsTileX - 1) / kZsTileX;
+    *gy = (H + TY - 1) / TY;
+    *gz = (nz + zchunk - 1) / zchunk;
+}
+
+}  // namespace ws3d

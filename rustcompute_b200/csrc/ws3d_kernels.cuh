@@ -17,6 +17,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "ws3d_index.h"
+
 namespace ws3d {
 
 constexpr uint8_t kNormal = 0, kAbsorber = 1, kReflector = 2, kObstacle = 3;
@@ -36,7 +38,56 @@ struct StepParams {
     uint64_t plane;         // H * pitch
     float c2, damping;
     uint32_t sponge_w;
+    // z-slab halo exchange (all null / zero on a single GPU)
+    float* peer_lo;                      // lower neighbour's upper ghost plane (new field)
+    float* peer_hi;                      // upper neighbour's lower ghost plane (new field)
+    const unsigned long long* wait_lo;   // flag the lower neighbour raises, or null
+    const unsigned long long* wait_hi;   // flag the upper neighbour raises, or null
+    unsigned long long wait_val;         // both flags must reach this value first
+    unsigned long long budget_ns;        // bounded wait
+    unsigned int* status;                // error word (bit 0: lower wait, bit 1: upper wait)
 };
+
+// ---------------------------------------------------------------------------
+// System-scope flag protocol for the z-slab exchange.  Every wait is bounded
+// by a %globaltimer budget and a hard iteration cap; when it gives up it
+// records the failure in the status word and returns, so a missing neighbour
+// never hangs the GPU.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __noinline__ bool wait_flag_geq(const unsigned long long* f, unsigned long long v,
+                                           unsigned long long budget_ns) {
+    if (ld_acquire_sys(f) >= v) return true;
+    const unsigned long long t0 = global_ns();
+    for (unsigned int it = 1; it < (1u << 26); ++it) {
+        __nanosleep(128);
+        if (ld_acquire_sys(f) >= v) return true;
+        if ((it & 31u) == 0 && global_ns() - t0 > budget_ns) return false;
+    }
+    return false;
+}
+
+// Raise the neighbours' flags after this GPU's step kernel has completed
+// (stream order) and its peer stores were fenced at system scope.
+__global__ void k_halo_signal(unsigned long long* flag_lo, unsigned long long* flag_hi,
+                              unsigned long long v) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    __threadfence_system();
+    if (flag_lo) st_release_sys(flag_lo, v);
+    if (flag_hi) st_release_sys(flag_hi, v);
+}
 
 __device__ __forceinline__ float4 ld4(const float* p) {
     return __ldg(reinterpret_cast<const float4*>(p));
@@ -47,6 +98,12 @@ __device__ __forceinline__ float4 ld4_stream(const float* p) {
 }
 __device__ __forceinline__ void st4(float* p, float4 v) {
     *reinterpret_cast<float4*>(p) = v;
+}
+// Ghost planes may be written by a peer GPU while this kernel runs (after
+// the flag wait): read them through L2 (coherent), never the non-coherent path.
+__device__ __forceinline__ float4 ld4_plane(const float* p, int64_t z, uint32_t nz) {
+    if (z < 0 || z >= (int64_t)nz) return __ldcg(reinterpret_cast<const float4*>(p));
+    return __ldg(reinterpret_cast<const float4*>(p));
 }
 
 // Reference update of one interior Normal cell (grid3d.rs:250-256), then the
@@ -113,71 +170,77 @@ __device__ __forceinline__ bool is_interior(uint32_t x, uint32_t y, uint32_t zg,
 template <bool kC2F, bool kCells, int TY>
 __global__ void __launch_bounds__(32 * TY, 3)
 k_step_zstream(StepParams a, uint32_t zchunk) {
+    static_assert(TY >= 2, "the y-halo rows need two distinct warps");
     __shared__ float4 srow[2][TY + 2][32];
     __shared__ float shl[2][TY], shr[2][TY];
 
     const int lane = threadIdx.x, w = threadIdx.y;
-    const uint32_t x0 = blockIdx.x * 128u;
-    const uint32_t x = x0 + 4u * lane;
-    const uint32_t y0 = blockIdx.y * TY;
-    const uint32_t y = y0 + w;
-    const uint32_t zb = blockIdx.z * zchunk;
-    const uint32_t ze = min(zb + zchunk, a.nz);
-    if (zb >= ze) return;  // uniform over the CTA
+    const bool halo_wait = a.wait_lo != nullptr || a.wait_hi != nullptr;
+    uint32_t zb, ze;
+    zs_chunk(zs_chunk_order(blockIdx.z, gridDim.z, halo_wait), zchunk, a.nz, &zb, &ze);
+    if (zb >= ze) return;  // uniform over the CTA, before any barrier
 
-    const bool xin = x < a.pitch;
-    const bool yin = y < a.H;
-    const bool act = xin && yin;
-    const bool ylo = (w == 0) && (y0 > 0) && xin;
-    const bool yhi = (w == TY - 1) && (y0 + TY < a.H) && xin;
-    const bool xl = (lane == 0) && (x0 > 0) && yin;
-    const bool xr = (lane == 31) && (x0 + 128u < a.W) && yin;
-
-    const long long P = (long long)a.plane;
-    const long long row = (long long)y * a.pitch + x;
-    const long long rowlo = (long long)(y0 - 1) * a.pitch + x;       // valid when ylo
-    const long long rowhi = (long long)(y0 + TY) * a.pitch + x;      // valid when yhi
-    const long long offxl = (long long)y * a.pitch + (long long)x0 - 1;   // valid when xl
-    const long long offxr = (long long)y * a.pitch + x0 + 128;            // valid when xr
+    // Boundary chunks read ghost planes that a neighbour GPU writes: wait
+    // (bounded) for its flag.  Interior chunks never wait and are scheduled
+    // first, so they overlap the exchange.
+    if (halo_wait) {
+        const bool need_lo = a.wait_lo && zb == 0;
+        const bool need_hi = a.wait_hi && ze == a.nz;
+        if (need_lo || need_hi) {
+            if (threadIdx.x == 0 && threadIdx.y == 0) {
+                unsigned int bad = 0;
+                if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns)) bad |= 1u;
+                if (need_hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns)) bad |= 2u;
+                if (bad) atomicOr(a.status, bad);
+            }
+            __syncthreads();
+        }
+    }
+    const ZsLane L = zs_lane<TY>(blockIdx.x, blockIdx.y, lane, w, a.W, a.H, a.pitch);
+    const bool act = L.act, ylo = L.ylo, yhi = L.yhi, xl = L.xl, xr = L.xr;
+    const uint32_t x = L.x, y = L.y;
+    const int64_t P = (int64_t)a.plane;
+    const int64_t row = L.row;
 
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
     const float* __restrict__ p = a.p;
     float* __restrict__ pp = a.pp;
 
     // Prologue: planes zb-1, zb in registers; plane zb staged in smem.
-    float4 pm = act ? ld4(p + (long long)(zb - 1) * P + row) : z4;
-    float4 pc = act ? ld4(p + (long long)zb * P + row) : z4;
+    const int64_t ozb = zs_plane((int64_t)zb, P);
+    float4 pm = act ? ld4_plane(p + zs_plane((int64_t)zb - 1, P) + row, (int64_t)zb - 1, a.nz) : z4;
+    float4 pc = act ? ld4(p + ozb + row) : z4;
     srow[0][w + 1][lane] = pc;
-    if (ylo) srow[0][0][lane] = ld4(p + (long long)zb * P + rowlo);
-    if (yhi) srow[0][TY + 1][lane] = ld4(p + (long long)zb * P + rowhi);
-    if (xl) shl[0][w] = __ldg(p + (long long)zb * P + offxl);
-    if (xr) shr[0][w] = __ldg(p + (long long)zb * P + offxr);
-    float4 pn = act ? ld4(p + (long long)(zb + 1) * P + row) : z4;
-    float4 vpp = act ? ld4_stream(pp + (long long)zb * P + row) : z4;
-    float4 vc2 = (kC2F && act) ? ld4_stream(a.c2f + (long long)zb * P + row) : z4;
+    if (ylo) srow[0][0][lane] = ld4(p + ozb + L.rowlo);
+    if (yhi) srow[0][TY + 1][lane] = ld4(p + ozb + L.rowhi);
+    if (xl) shl[0][w] = __ldg(p + ozb + L.offxl);
+    if (xr) shr[0][w] = __ldg(p + ozb + L.offxr);
+    float4 pn = act ? ld4_plane(p + zs_plane((int64_t)zb + 1, P) + row, (int64_t)zb + 1, a.nz) : z4;
+    float4 vpp = act ? ld4_stream(pp + ozb + row) : z4;
+    float4 vc2 = (kC2F && act) ? ld4_stream(a.c2f + ozb + row) : z4;
     uchar4 vt = make_uchar4(0, 0, 0, 0);
-    if (kCells && act) vt = *reinterpret_cast<const uchar4*>(a.types + (long long)zb * P + row);
+    if (kCells && act) vt = *reinterpret_cast<const uchar4*>(a.types + ozb + row);
     __syncthreads();
 
     int cur = 0;
     for (uint32_t zl = zb; zl < ze; ++zl) {
         const bool more = zl + 1 < ze;
-        // Prefetch for plane zl+1.
+        // Prefetch for plane zl+1 (and the front plane zl+2).
         float4 pn2 = z4, vpp2 = z4, vc22 = z4, hy = z4;
         float hx = 0.f;
         uchar4 vt2 = make_uchar4(0, 0, 0, 0);
         if (more) {
-            const long long zo1 = (long long)(zl + 1) * P;
+            const int64_t zo1 = zs_plane((int64_t)zl + 1, P);
             if (act) {
-                pn2 = ld4(p + zo1 + P + row);
+                pn2 = ld4_plane(p + zs_plane((int64_t)zl + 2, P) + row, (int64_t)zl + 2, a.nz);
                 vpp2 = ld4_stream(pp + zo1 + row);
                 if (kC2F) vc22 = ld4_stream(a.c2f + zo1 + row);
                 if (kCells) vt2 = *reinterpret_cast<const uchar4*>(a.types + zo1 + row);
             }
-            if (ylo) hy = ld4(p + zo1 + rowlo);
-            else if (yhi) hy = ld4(p + zo1 + rowhi);
-            if (xl) hx = __ldg(p + zo1 + offxl);
-            else if (xr) hx = __ldg(p + zo1 + offxr);
+            if (ylo) hy = ld4(p + zo1 + L.rowlo);
+            else if (yhi) hy = ld4(p + zo1 + L.rowhi);
+            if (xl) hx = __ldg(p + zo1 + L.offxl);
+            else if (xr) hx = __ldg(p + zo1 + L.offxr);
         }
 
         // Compute plane zl.
@@ -190,12 +253,12 @@ k_step_zstream(StepParams a, uint32_t zchunk) {
 
         if (act) {
             const uint32_t zg = a.z0 + zl;
+            const int64_t o = zs_plane((int64_t)zl, P) + row;
             float4 out;
             float c2x = kC2F ? vc2.x : a.c2, c2y = kC2F ? vc2.y : a.c2;
             float c2z = kC2F ? vc2.z : a.c2, c2w = kC2F ? vc2.w : a.c2;
             float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
             if (kCells) {
-                const long long o = (long long)zl * P + row;
                 if (vt.x == kAbsorber || vt.x == kObstacle) r0 = __ldg(a.refl + o + 0);
                 if (vt.y == kAbsorber || vt.y == kObstacle) r1 = __ldg(a.refl + o + 1);
                 if (vt.z == kAbsorber || vt.z == kObstacle) r2 = __ldg(a.refl + o + 2);
@@ -209,7 +272,9 @@ k_step_zstream(StepParams a, uint32_t zchunk) {
                                       S.z, N.z, pm.z, pn.z, pc.z, vpp.z, c2z, vt.z, r2, a);
             out.w = cell_rule<kCells>(x + 3, y, zg, is_interior(x + 3, y, zg, a), pc.z, er, S.w,
                                       N.w, pm.w, pn.w, pc.w, vpp.w, c2w, vt.w, r3, a);
-            st4(pp + (long long)zl * P + row, out);
+            st4(pp + o, out);
+            if (zl == 0 && a.peer_lo) st4(a.peer_lo + row, out);
+            if (zl + 1 == a.nz && a.peer_hi) st4(a.peer_hi + row, out);
         }
 
         if (more) {
@@ -224,6 +289,8 @@ k_step_zstream(StepParams a, uint32_t zchunk) {
             cur = nxt;
         }
     }
+    // Order this thread's peer stores before the flag the signal kernel raises.
+    if ((a.peer_lo && zb == 0) || (a.peer_hi && ze == a.nz)) __threadfence_system();
 }
 
 // ---------------------------------------------------------------------------
@@ -296,15 +363,32 @@ __global__ void __launch_bounds__(256) k_ref_boundary(float* pp, const uint8_t* 
 // ---------------------------------------------------------------------------
 
 // Per-step point sources, applied in source order by one thread so that
-// coinciding sources add in the same order as the reference loop.
+// coinciding sources add in the same order as the reference loop.  A source
+// on a slab's first or last plane is also added to the neighbour's ghost copy
+// of that plane (ghost_row >= 0, side 0 = lower neighbour, 1 = upper).
 __global__ void k_inject_sources(float* p, float* pp, const uint64_t* off, const float* wavelet,
-                                 uint32_t n, uint64_t len, uint64_t step) {
+                                 uint32_t n, uint64_t len, uint64_t step,
+                                 const long long* ghost_row, float* ghost_lo, float* ghost_hi) {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     for (uint32_t k = 0; k < n; ++k) {
         const float amp = step < len ? wavelet[(uint64_t)k * len + step] : 0.0f;
         p[off[k]] = __fadd_rn(p[off[k]], amp);
         pp[off[k]] = __fadd_rn(pp[off[k]], __fmul_rn(amp, 0.5f));
+        if (ghost_row) {
+            const long long g = ghost_row[2 * k], side = ghost_row[2 * k + 1];
+            float* gp = side == 0 ? ghost_lo : ghost_hi;
+            if (g >= 0 && gp) gp[g] = __fadd_rn(gp[g], amp);
+        }
     }
+}
+
+// Impulse factors applied to a neighbour's ghost copy of a boundary plane
+// (pressure only: ghost planes hold no p_prev).
+__global__ void k_inject_ghost(float* ghost, const uint64_t* row, const float* factor, uint32_t n,
+                               float amp) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    ghost[row[i]] = __fadd_rn(ghost[row[i]], __fmul_rn(amp, factor[i]));
 }
 
 // grid3d.rs:146-152 / gpu_backend.rs:118-131 (offset precomputed on the host).

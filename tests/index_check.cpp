@@ -1,0 +1,136 @@
+// Host-side bounds check of the z-streaming kernel's addressing.
+//
+// Replays, for every CTA (or for the corner CTAs of very large launches),
+// every thread and every plane, the loads and stores k_step_zstream issues,
+// using the same helpers (rustcompute_b200/csrc/ws3d_index.h), and verifies
+// that each access lies inside its allocation, is 16-byte aligned for float4
+// accesses and does not straddle a row.  Exit code 0 = all accesses in bounds.
+//
+// Usage: index_check W H nz sm_count [TY [halo]]
+#include <cstdio>
+#include <cstdlib>
+#include <vector>
+
+#include "ws3d_index.h"
+
+using namespace ws3d;
+
+static long long g_checked = 0;
+static int g_bad = 0;
+
+struct Field {
+    const char* name;
+    bool ghosts;  // p: ghost planes -1 and nz are readable
+};
+
+static void check(const Field& f, int64_t o, int n, uint32_t pitch, uint32_t nz, int64_t plane,
+                  const char* what, uint32_t bx, uint32_t by, uint32_t bz, int lane, int w) {
+    ++g_checked;
+    const int64_t lo = f.ghosts ? -plane : 0;
+    const int64_t hi = f.ghosts ? (int64_t)(nz + 1) * plane : (int64_t)nz * plane;
+    int64_t in_row = ((o % (int64_t)pitch) + pitch) % (int64_t)pitch;
+    bool ok = o >= lo && o + n <= hi && in_row + n <= (int64_t)pitch;
+    if (n == 4 && (o % 4) != 0) ok = false;
+    if (!ok && g_bad < 20) {
+        fprintf(stderr, "OUT OF BOUNDS %s %s: off=%lld n=%d [%lld,%lld) block=(%u,%u,%u) lane=%d w=%d\n",
+                f.name, what, (long long)o, n, (long long)lo, (long long)hi, bx, by, bz, lane, w);
+    }
+    if (!ok) ++g_bad;
+}
+
+template <int TY>
+static void run(uint32_t W, uint32_t H, uint32_t nz, int sms, bool halo) {
+    const uint32_t pitch = (W + 31u) & ~31u;
+    const int64_t P = (int64_t)H * pitch;
+    const uint32_t chunk = zs_zchunk<TY>(pitch, H, nz, sms);
+    uint32_t gx, gy, gz;
+    zs_grid<TY>(pitch, H, nz, chunk, &gx, &gy, &gz);
+    const Field fp{"p", true}, fpp{"pp", false}, fc2{"c2", false}, fty{"types", false},
+        frf{"refl", false};
+    const bool sample = (uint64_t)gx * gy * gz * 32 * TY * (chunk + 2) > 30000000ull;
+    auto pick = [&](uint32_t n) {
+        std::vector<uint32_t> v;
+        if (!sample || n <= 4) {
+            for (uint32_t i = 0; i < n; ++i) v.push_back(i);
+        } else {
+            v = {0, 1, n / 2, n - 2, n - 1};
+        }
+        return v;
+    };
+    for (uint32_t bz : pick(gz))
+        for (uint32_t by : pick(gy))
+            for (uint32_t bx : pick(gx)) {
+                uint32_t zb, ze;
+                zs_chunk(zs_chunk_order(bz, gz, halo), chunk, nz, &zb, &ze);
+                if (zb >= ze) continue;
+                for (int w = 0; w < TY; ++w)
+                    for (int lane = 0; lane < 32; ++lane) {
+                        const ZsLane L = zs_lane<TY>(bx, by, lane, w, W, H, pitch);
+                        auto C = [&](const Field& f, int64_t z, int64_t off, int n, const char* what) {
+                            check(f, zs_plane(z, P) + off, n, pitch, nz, P, what, bx, by, bz, lane, w);
+                        };
+                        if (L.act) {
+                            C(fp, (int64_t)zb - 1, L.row, 4, "prologue pm");
+                            C(fp, zb, L.row, 4, "prologue pc");
+                        }
+                        if (L.ylo) C(fp, zb, L.rowlo, 4, "prologue ylo");
+                        if (L.yhi) C(fp, zb, L.rowhi, 4, "prologue yhi");
+                        if (L.xl) C(fp, zb, L.offxl, 1, "prologue xl");
+                        if (L.xr) C(fp, zb, L.offxr, 1, "prologue xr");
+                        if (L.act) {
+                            C(fp, (int64_t)zb + 1, L.row, 4, "prologue pn");
+                            C(fpp, zb, L.row, 4, "prologue pp");
+                            C(fc2, zb, L.row, 4, "prologue c2");
+                            C(fty, zb, L.row, 4, "prologue types");
+                        }
+                        for (uint32_t zl = zb; zl < ze; ++zl) {
+                            const bool more = zl + 1 < ze;
+                            if (more) {
+                                if (L.act) {
+                                    C(fp, (int64_t)zl + 2, L.row, 4, "loop pn2");
+                                    C(fpp, (int64_t)zl + 1, L.row, 4, "loop pp");
+                                    C(fc2, (int64_t)zl + 1, L.row, 4, "loop c2");
+                                    C(fty, (int64_t)zl + 1, L.row, 4, "loop types");
+                                }
+                                if (L.ylo) C(fp, (int64_t)zl + 1, L.rowlo, 4, "loop ylo");
+                                else if (L.yhi) C(fp, (int64_t)zl + 1, L.rowhi, 4, "loop yhi");
+                                if (L.xl) C(fp, (int64_t)zl + 1, L.offxl, 1, "loop xl");
+                                else if (L.xr) C(fp, (int64_t)zl + 1, L.offxr, 1, "loop xr");
+                            }
+                            if (L.act) {
+                                for (int k = 0; k < 4; ++k) C(frf, zl, L.row + k, 1, "refl");
+                                C(fpp, zl, L.row, 4, "store");
+                                // peer stores into a neighbour's ghost plane (one plane)
+                                if (halo && (zl == 0 || zl + 1 == nz)) {
+                                    ++g_checked;
+                                    if (!(L.row >= 0 && L.row + 4 <= P && L.row % 4 == 0)) {
+                                        ++g_bad;
+                                        fprintf(stderr, "OUT OF BOUNDS peer store row=%lld\n",
+                                                (long long)L.row);
+                                    }
+                                }
+                            }
+                        }
+                    }
+            }
+}
+
+int main(int argc, char** argv) {
+    if (argc < 5) {
+        fprintf(stderr, "usage: %s W H nz sm_count [TY]\n", argv[0]);
+        return 2;
+    }
+    const uint32_t W = (uint32_t)atoi(argv[1]), H = (uint32_t)atoi(argv[2]),
+                   nz = (uint32_t)atoi(argv[3]);
+    const int sms = atoi(argv[4]);
+    const int ty = argc > 5 ? atoi(argv[5]) : 8;
+    const bool halo = argc > 6 && atoi(argv[6]) != 0;
+    switch (ty) {
+        case 4: run<4>(W, H, nz, sms, halo); break;
+        case 8: run<8>(W, H, nz, sms, halo); break;
+        case 16: run<16>(W, H, nz, sms, halo); break;
+        default: fprintf(stderr, "TY must be 4, 8 or 16\n"); return 2;
+    }
+    printf("checked %lld accesses, %d out of bounds\n", g_checked, g_bad);
+    return g_bad == 0 ? 0 : 1;
+}

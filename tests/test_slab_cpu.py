@@ -1,0 +1,167 @@
+"""Multi-GPU host logic on CPU: z-slab bounds, the handle exchange over
+torch.distributed (gloo, world sizes 2 and 3), and a slab-split emulation
+of the step with explicit ghost-plane exchange that must equal the
+single-domain oracle bit for bit.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from rustcompute_b200 import configs
+from rustcompute_b200.slab import gather_handles, neighbours, slab_bounds
+
+f32 = np.float32
+
+
+def test_slab_bounds_cover_the_grid():
+    for D in (2, 7, 64, 512, 1023):
+        for world in (1, 2, 3, 4, 8):
+            if D < world:
+                with pytest.raises(ValueError):
+                    slab_bounds(D, world, 0)
+                continue
+            spans = [slab_bounds(D, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == D
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [e - b for b, e in spans]
+            assert max(sizes) - min(sizes) <= 1 and min(sizes) >= 1
+
+
+def test_neighbours():
+    assert neighbours(0, 1) == (None, None)
+    assert neighbours(0, 3) == (None, 1)
+    assert neighbours(1, 3) == (0, 2)
+    assert neighbours(2, 3) == (1, None)
+
+
+def slab_step(Pext, PP, c2, damping, sponge, z0, Dg):
+    """One step on a slab: Pext has nz+2 planes (ghosts at both ends), PP nz
+    planes; returns the new owned planes.  Same op order as the reference
+    (grid3d.rs:250-256), vectorised in float32 (no contraction)."""
+    nz, H, W = PP.shape
+    out = PP.copy()
+    if W >= 3 and H >= 3:
+        C = Pext[1:-1, 1:-1, 1:-1]
+        lap = (Pext[1:-1, 1:-1, :-2] + Pext[1:-1, 1:-1, 2:])
+        lap = lap + Pext[1:-1, :-2, 1:-1]
+        lap = lap + Pext[1:-1, 2:, 1:-1]
+        lap = lap + Pext[:-2, 1:-1, 1:-1]
+        lap = lap + Pext[2:, 1:-1, 1:-1]
+        lap = lap - f32(6.0) * C
+        c2i = c2[:, 1:-1, 1:-1] if c2.ndim == 3 else c2
+        pn = (f32(2.0) * C - PP[:, 1:-1, 1:-1]) + c2i * lap
+        v = pn * f32(damping)
+        if len(sponge):
+            zg = np.arange(z0, z0 + nz)[:, None, None]
+            y = np.arange(1, H - 1)[None, :, None]
+            x = np.arange(1, W - 1)[None, None, :]
+            d = np.minimum.reduce([np.broadcast_to(a, v.shape) for a in
+                                   (x, W - 1 - x, y, H - 1 - y, zg, Dg - 1 - zg)])
+            m = d < len(sponge)
+            v = np.where(m, v * sponge[np.minimum(d, len(sponge) - 1)], v).astype(np.float32)
+        zg = np.arange(z0, z0 + nz)
+        planes = (zg >= 1) & (zg <= Dg - 2)
+        out[planes, 1:-1, 1:-1] = v[planes]
+    # reference faces: absorber with reflection 0.1
+    zg = np.arange(z0, z0 + nz)
+    face_plane = (zg == 0) | (zg == Dg - 1)
+    out[face_plane] *= f32(0.1)
+    rest = ~face_plane
+    out[rest, 0, :] *= f32(0.1)
+    out[rest, -1, :] *= f32(0.1)
+    if H > 2:
+        out[rest, 1:-1, 0] *= f32(0.1)
+        out[rest, 1:-1, -1] *= f32(0.1)
+    return out
+
+
+def _rank_main(rank, world, port, wl_args, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import torch
+
+    import oracle
+    name, W, H, D, steps = wl_args
+    wl = configs.build(name, W, H, D, steps=steps)
+    zb, ze = slab_bounds(D, world, rank)
+    nz = ze - zb
+    # handle exchange: fake blobs stand in for the IPC handle structs
+    blobs = gather_handles(f"rank{rank}:{zb}-{ze}".encode(), rank, world, dist.all_gather_object)
+    assert blobs == [f"rank{r}:{slab_bounds(D, world, r)[0]}-{slab_bounds(D, world, r)[1]}".encode()
+                     for r in range(world)]
+    p, pp = wl.initial_fields(zb, ze)
+    P = p.reshape(nz, H, W).copy()
+    PP = pp.reshape(nz, H, W).copy()
+    c2 = wl.c2_field(zb, ze)
+    c2 = f32(wl.c_squared) if c2 is None else c2.reshape(nz, H, W)
+    sponge = oracle.sponge_table(wl.sponge_width, wl.sponge_max) if wl.sponge_width \
+        else np.zeros(0, np.float32)
+    lo, hi = neighbours(rank, world)
+    for s in range(steps):
+        for k, (x, y, z) in enumerate(wl.sources):
+            if zb <= z < ze:
+                a = wl.wavelet[k, s] if s < wl.wavelet.shape[1] else f32(0)
+                P[z - zb, y, x] = P[z - zb, y, x] + a
+                PP[z - zb, y, x] = PP[z - zb, y, x] + a * f32(0.5)
+        Pext = np.zeros((nz + 2, H, W), np.float32)
+        Pext[1:-1] = P
+        # exchange boundary planes with the neighbours (gloo point-to-point)
+        reqs = []
+        if lo is not None:
+            reqs.append(dist.isend(torch.from_numpy(P[0].copy()), lo))
+        if hi is not None:
+            reqs.append(dist.isend(torch.from_numpy(P[-1].copy()), hi))
+        if lo is not None:
+            t = torch.empty(H, W)
+            dist.recv(t, lo)
+            Pext[0] = t.numpy()
+        if hi is not None:
+            t = torch.empty(H, W)
+            dist.recv(t, hi)
+            Pext[-1] = t.numpy()
+        for r in reqs:
+            r.wait()
+        new = slab_step(Pext, PP, c2, wl.damping, sponge, zb, D)
+        P, PP = new, P
+    out = [None] * world
+    dist.all_gather_object(out, (zb, P.copy(), PP.copy()))
+    if rank == 0:
+        full_p = np.concatenate([o[1] for o in sorted(out, key=lambda t: t[0])]).reshape(-1)
+        full_pp = np.concatenate([o[2] for o in sorted(out, key=lambda t: t[0])]).reshape(-1)
+        ref = oracle.from_workload(wl)
+        ref.run(steps, 1)
+        result_q.put((bool(np.array_equal(full_p, ref.pressure)),
+                      bool(np.array_equal(full_pp, ref.pressure_prev))))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world,wl_args", [
+    (2, ("c3", 40, 36, 30, 25)),     # heterogeneous + sponge + centred source
+    (3, ("c2", 34, 30, 33, 40)),     # sources + sponge
+    (2, ("c1", 24, 20, 2, 5)),       # one plane per slab: both planes are faces
+])
+def test_gloo_slab_emulation_matches_oracle(world, wl_args):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, wl_args, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    codes = [p.exitcode for p in procs]
+    assert codes == [0] * world, codes
+    assert q.get(timeout=5) == (True, True)

@@ -1,0 +1,135 @@
+"""z-slab decomposition on the GPU.
+
+- Same-device slab groups (2-4 slabs, stream-ordered exchange) equal one
+  context bit for bit, with sources and impulses on slab boundary planes.
+- The bounded device wait gives up with WS3D_ETIMEOUT when a neighbour never
+  raises its flag (a child process exports a slab that never steps), and the
+  context stays usable.
+- On a box with >= 2 GPUs: one process per GPU with the in-kernel NVLink
+  exchange equals one GPU bit for bit.
+"""
+import multiprocessing as mpm
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+import pytest
+
+from rustcompute_b200 import GpuBackend3D, TimeoutError_, configs
+from rustcompute_b200.slab import LocalSlabGroup, attach, export_handles, slab_bounds
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def make(wl, zb, ze, device=0, budget_ns=0):
+    whole = (zb, ze) == (0, wl.D)
+    b = GpuBackend3D.create(wl.W, wl.H, wl.D, c_squared=wl.c_squared, damping=wl.damping,
+                            device=device, sponge_width=wl.sponge_width,
+                            sponge_max=wl.sponge_max, z_begin=0 if whole else zb,
+                            z_end=0 if whole else ze, spin_budget_ns=budget_ns)
+    p, pp = wl.initial_fields(zb, ze)
+    b.upload_fields(p, pp)
+    c2 = wl.c2_field(zb, ze)
+    if c2 is not None:
+        b.set_c2_field(c2)
+    if len(wl.sources):
+        b.set_sources(wl.sources, wl.wavelet)
+    return b
+
+
+@pytest.mark.parametrize("nslab", [2, 3, 4])
+@pytest.mark.parametrize("name,grid,steps", [("c3", (96, 72, 64), 50), ("c2", (48, 40, 37), 60)])
+def test_local_slab_group_equals_single_context(nslab, name, grid, steps):
+    W, H, D = grid
+    wl = configs.build(name, W, H, D, steps=steps)
+    bounds = [slab_bounds(D, nslab, r) for r in range(nslab)]
+    # put extra sources exactly on slab boundary planes (both sides)
+    extra = [[W // 2, H // 2, bounds[1][0]], [W // 3, H // 3, bounds[0][1] - 1]]
+    src = np.concatenate([wl.sources, np.array(extra, np.uint32)])
+    wav = np.concatenate([wl.wavelet, np.tile(wl.wavelet[:1], (2, 1))])
+    wl.sources, wl.wavelet = src, wav
+    full = make(wl, 0, D)
+    slabs = [make(wl, zb, ze) for zb, ze in bounds]
+    grp = LocalSlabGroup(slabs)
+    full.step_n(None, steps // 2)
+    grp.step_n(steps // 2)
+    for b in [full] + slabs:   # impulses on boundary planes
+        b.inject_impulse(W // 4, H // 4, bounds[1][0], 0.5)
+        b.inject_spherical_impulse(W // 2, H // 2, bounds[-1][0], 0.2, 2.5)
+    grp.sync()                  # impulses changed boundary planes: re-sync ghosts
+    full.step_n(None, steps - steps // 2)
+    grp.step_n(steps - steps // 2)
+    fp, fpp = full.download_field(with_prev=True)
+    gp = np.concatenate([b.download_field() for b in slabs])
+    gpp = np.concatenate([b.download_field(with_prev=True)[1] for b in slabs])
+    assert np.array_equal(gp.view(np.uint32), fp.view(np.uint32))
+    assert np.array_equal(gpp.view(np.uint32), fpp.view(np.uint32))
+    grp.close()
+    full.close()
+
+
+def _idle_lower_neighbour(conn, grid, zb, ze):
+    """Child process: owns the lower slab, exports it, never steps."""
+    sys.path.insert(0, ROOT)
+    from rustcompute_b200 import configs as cfg
+    from rustcompute_b200.slab import export_handles as exp
+    W, H, D = grid
+    wl = cfg.build("c1", W, H, D, steps=4)
+    b = make(wl, zb, ze)
+    conn.send(exp(b))
+    conn.recv()   # wait until the parent is done
+    b.close()
+
+
+def test_bounded_wait_times_out_and_context_stays_usable():
+    grid = (64, 40, 48)
+    W, H, D = grid
+    wl = configs.build("c1", W, H, D, steps=4)
+    ctx = mpm.get_context("spawn")
+    parent, child = ctx.Pipe()
+    proc = ctx.Process(target=_idle_lower_neighbour, args=(child, grid, 0, 24))
+    proc.start()
+    try:
+        lower = parent.recv()
+        b = make(wl, 24, 48, budget_ns=200_000_000)   # 0.2 s budget
+        attach(b, lower, None)
+        b._chk(b._lib.ws3d_halo_sync(b._ctx, 0), "sync0")
+        b._chk(b._lib.ws3d_halo_sync(b._ctx, 1), "sync1")
+        t0 = time.time()
+        b.step_n(None, 1)
+        with pytest.raises(TimeoutError_):
+            b.sync()
+        assert time.time() - t0 < 30
+        # the status was reported and cleared; the context still works
+        b.sync()
+        assert np.isfinite(b.energy())
+        b.close()
+    finally:
+        parent.send("done")
+        proc.join(timeout=60)
+    assert proc.exitcode == 0
+
+
+def _gpu_count():
+    import torch
+    return torch.cuda.device_count()
+
+
+@pytest.mark.multigpu
+@pytest.mark.parametrize("name,grid,steps", [("c3", "96x80x64", 60), ("c2", "64x48x45", 50)])
+def test_multi_process_nvlink_slabs_equal_one_gpu(name, grid, steps):
+    n = _gpu_count()
+    if n < 2:
+        pytest.skip("needs 2 or more GPUs")
+    n = min(n, 4)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr", "127.0.0.1", "--master-port", str(29400 + os.getpid() % 1000),
+           os.path.join(ROOT, "tests", "mp_slab_check.py"), "--workload", name, "--grid", grid,
+           "--steps", str(steps)]
+    r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, capture_output=True, text=True,
+                       env=env)
+    assert r.returncode == 0 and "SLAB-CHECK OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
