@@ -142,37 +142,33 @@ class ClockSampler:
 
 
 def cpu_sample_run(wl, target_s: float = 12.0, nthreads: int = 0):
-    """Time the oracle (CPU port of the reference step) on a bounded sample of
-    the workload: full-grid steps when they fit in ~target_s, else a z-slab."""
+    """Time the oracle (CPU port of the reference step, OpenMP over z-planes
+    like step_parallel) on a bounded sample of the workload: full-grid steps
+    filling ~target_s when one step takes < target_s/3, else a z-slab of the
+    same recipe."""
     import oracle
     nthreads = nthreads or oracle.max_threads()
-    # Probe one step on a small slab to size the sample.
-    probe_d = min(wl.D, max(8, int(4e6 // (wl.W * wl.H)) + 2))
-    sub = wl.scaled(wl.W, wl.H, probe_d, steps=4) if probe_d < wl.D else wl
-    g = oracle.from_workload(sub)
+    g = oracle.from_workload(wl)
+    g.run(1, nthreads)                     # warm-up (first touch)
     t0 = time.perf_counter()
-    g.run(1, nthreads)
+    g.run(1, nthreads)                     # calibration
     t1 = time.perf_counter() - t0
-    rate = sub.cells / max(t1, 1e-9)  # cells/s
-    full_step_s = wl.cells / rate
-    if full_step_s * 2 <= target_s:
-        steps = max(2, int(target_s / full_step_s))
-        sample = wl
-        g = oracle.from_workload(sample)
-        g.run(1, nthreads)  # warm-up step
-        desc = f"{steps} full {wl.W}x{wl.H}x{wl.D} steps after 1 warm-up step"
+    if t1 * 3 <= target_s:
+        steps = max(2, int(target_s / max(t1, 1e-6)))
+        sample = f"{steps} full {wl.W}x{wl.H}x{wl.D} steps after 2 untimed steps"
+        cells = wl.cells
     else:
-        planes = max(8, min(wl.D, int(target_s / 2 * rate / (wl.W * wl.H))))
-        sample = wl.scaled(wl.W, wl.H, planes, steps=4)
-        steps = 2
-        g = oracle.from_workload(sample)
+        planes = max(8, min(wl.D, int(wl.D * target_s / 3 / t1)))
+        sub = wl.scaled(wl.W, wl.H, planes, steps=4)
+        g = oracle.from_workload(sub)
         g.run(1, nthreads)
-        desc = (f"{steps} steps of a {wl.W}x{wl.H}x{planes} slab of the {wl.name} recipe "
-                f"(same per-cell work) after 1 warm-up step")
+        steps, cells = 2, sub.cells
+        sample = (f"2 steps of a {wl.W}x{wl.H}x{planes} slab of the {wl.name} recipe "
+                  "(same per-cell work) after 1 untimed step")
     t0 = time.perf_counter()
     g.run(steps, nthreads)
     dt = time.perf_counter() - t0
-    return sample.cells * steps / dt / 1e6, nthreads, desc, dt
+    return cells * steps / dt / 1e6, nthreads, sample, dt
 
 
 def run_reference(args, wl):

@@ -187,7 +187,9 @@ WS3D_API size_t ws3d_memory_usage(const ws3d_ctx *ctx);
 WS3D_API ws3d_status ws3d_sync(ws3d_ctx *ctx);
 
 /* Use a caller-owned cudaStream_t (passed as void*) for every later launch;
- * NULL returns to the context's own stream. */
+ * NULL returns to the context's own stream (the stream in use is synchronised
+ * first, so it must still be alive).  ws3d_destroy never touches a caller's
+ * stream: with one set, it synchronises the device instead. */
 WS3D_API ws3d_status ws3d_set_stream(ws3d_ctx *ctx, void *cuda_stream);
 WS3D_API ws3d_status ws3d_get_stream(const ws3d_ctx *ctx, void **cuda_stream);
 

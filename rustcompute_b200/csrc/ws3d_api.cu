@@ -480,7 +480,13 @@ void ws3d_destroy(ws3d_ctx* c) {
     if (!c) return;
     {
         DeviceGuard g(c->desc.device);
-        if (c->stream) cudaStreamSynchronize(c->stream);
+        // Never dereference a caller's stream here (it may already be gone):
+        // wait for our own stream, or for the device when an external one is set.
+        if (c->stream == c->own_stream) {
+            if (c->own_stream) cudaStreamSynchronize(c->own_stream);
+        } else {
+            cudaDeviceSynchronize();
+        }
         for (int b = 0; b < 2; ++b) dfree(c, c->buf[b], c->slab);
         dfree(c, c->c2f, c->slab);
         dfree(c, c->types, c->slab);

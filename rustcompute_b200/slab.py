@@ -106,5 +106,10 @@ class LocalSlabGroup:
         b0._chk(b0._lib.ws3d_step_group(arr, len(self.backends), int(n)), "step_group")
 
     def close(self) -> None:
+        # The group shares the first context's stream: give every context its
+        # own stream back before any of them (and that stream) is destroyed.
+        for b in self.backends:
+            if b._ctx:
+                b.set_stream(None)
         for b in self.backends:
             b.close()
