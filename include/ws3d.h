@@ -175,6 +175,33 @@ WS3D_API ws3d_status ws3d_inject_spherical_impulse(ws3d_ctx *ctx, uint32_t cx, u
  * the device over the owned cells.  Synchronous. */
 WS3D_API ws3d_status ws3d_energy(ws3d_ctx *ctx, double *sum_sq);
 
+/* Energy (sum of p^2, accumulated in f64) of a caller-owned device field,
+ * for callers that cannot allocate device memory when they need it: work
+ * being recorded into a CUDA graph (stream capture rejects cudaMalloc),
+ * real-time loops that must not block on the device synchronisation that
+ * cudaMalloc/cudaFree imply, and host applications that own all device memory
+ * and forbid libraries from allocating.  No counterpart in the reference.
+ *
+ * field:  device pointer, nz planes of height rows, row pitch `pitch` floats
+ *         (pitch >= width; pitch == width for a dense z-major array).
+ * result: device pointer to one double, written by the call.
+ * stream: cudaStream_t to launch on (NULL = the legacy default stream).
+ * errbuf: optional buffer for a one-line message on failure.
+ * Runs on the calling thread's current device, allocates nothing and
+ * returns without synchronising.  Its scratch is a fixed array of
+ * WS3D_STATIC_ENERGY_MAX_PLANES doubles (one per plane, 64 KiB) that every
+ * GPU loading this library holds until exit; nz above that limit is
+ * rejected with WS3D_EINVAL.  The first call on a device resolves the
+ * array's device address: make that first call outside any stream capture.
+ * All calls on a device share the array, so calls that overlap on the GPU
+ * (different streams, no ordering between them) race; each call writes every
+ * entry it reads, so nothing carries over from an earlier call. */
+#define WS3D_STATIC_ENERGY_MAX_PLANES 8192u
+WS3D_API ws3d_status ws3d_field_energy_static(const float *field, uint32_t width,
+                                              uint32_t height, uint32_t nz, uint32_t pitch,
+                                              double *result, void *stream, char *errbuf,
+                                              size_t errlen);
+
 /* SimulationGrid3D::max_pressure (grid3d.rs:450-455).  Synchronous. */
 WS3D_API ws3d_status ws3d_max_pressure(ws3d_ctx *ctx, float *max_abs);
 

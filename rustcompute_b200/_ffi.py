@@ -24,6 +24,8 @@ WS3D_EINVAL = 8
 WS3D_ETIMEOUT = 9
 WS3D_EPEER = 10
 
+WS3D_STATIC_ENERGY_MAX_PLANES = 8192   # include/ws3d.h
+
 WS3D_VARIANT_ZSTREAM = 0
 WS3D_VARIANT_NAIVE = 1
 WS3D_VARIANT_REFSHAPE = 2
@@ -108,6 +110,8 @@ SIGNATURES = {
         C.c_int, [_CTX, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float]),
     "ws3d_energy": (C.c_int, [_CTX, C.POINTER(C.c_double)]),
     "ws3d_max_pressure": (C.c_int, [_CTX, _F]),
+    "ws3d_field_energy_static": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                           _P, _P, C.c_char_p, C.c_size_t]),
     "ws3d_memory_usage": (C.c_size_t, [_CTX]),
     "ws3d_sync": (C.c_int, [_CTX]),
     "ws3d_set_stream": (C.c_int, [_CTX, _P]),

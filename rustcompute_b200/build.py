@@ -30,7 +30,7 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC,-O3,-fvisibility=hidden",
     "-shared",
 ]
-SOURCES = ["ws3d_api.cu"]
+SOURCES = ["ws3d_api.cu", "ws3d_noalloc.cu"]
 
 
 def nvcc_path() -> str:
