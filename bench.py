@@ -50,7 +50,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c3")
-    ap.add_argument("--variant", default="zstream")
+    ap.add_argument("--variant", default="auto",
+                    help="auto (TMA pipeline on one GPU, z-stream for z-slabs), tma, zstream, "
+                         "naive, refshape")
     ap.add_argument("--grid", default=None,
                     help="WxHxD: the workload's recipe at another size (profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -76,14 +78,15 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def ncu_traffic(workload: str, variant: str):
-    """DRAM bytes per launch of the step kernel from a committed ncu summary."""
+def ncu_traffic(wl, kernel: str):
+    """DRAM bytes per launch of the step kernel from a committed ncu summary
+    (profiles/traffic.json, keyed by workload, grid and kernel), or None."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(path):
         return None
     with open(path) as f:
         d = json.load(f)
-    e = d.get(f"{workload}/{variant}")
+    e = d.get(f"{wl.name}/{wl.W}x{wl.H}x{wl.D}/{kernel}")
     return None if e is None else e.get("dram_bytes_per_launch")
 
 
@@ -241,6 +244,13 @@ def pinned(a):
     return t.numpy()
 
 
+def kernel_name(variant, wl, world):
+    if variant == "auto":
+        variant = "tma" if (world == 1 and wl.W > 128 and wl.H >= 16) else "zstream"
+    return {"tma": "k_step_tma", "zstream": "k_step_zstream", "naive": "k_step_naive",
+            "refshape": "k_ref_stencil+k_ref_boundary"}[variant]
+
+
 def run_ours(args, wl):
     import datetime
 
@@ -310,13 +320,13 @@ def run_ours(args, wl):
     achieved = alg_bytes / (avg_kernel_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"],
-                "traffic": ncu_traffic(wl.name, args.variant),
+                "traffic": ncu_traffic(wl, kernel_name(args.variant, wl, world)),
                 "algorithmic_bytes_per_launch": alg_bytes,
                 "bytes_per_cell_step": bpc,
                 "kernel_avg_ms": avg_kernel_ms,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"
                                if peaks["source"] == "measured" else "fallback",
-                "kernel": "k_step_zstream" if args.variant == "zstream" else args.variant,
+                "kernel": kernel_name(args.variant, wl, world),
                 "rank": rank}
 
     result = {
@@ -365,7 +375,7 @@ def run_ours(args, wl):
 
     if args.comparators and world == 1:
         comps = {}
-        for v in ("naive", "refshape"):
+        for v in ("zstream", "naive", "refshape"):
             bc = make_backend(wl, v, local, zb, ze)
             bc.set_stream(stream.cuda_stream)
             upload_inputs(bc, wl, p0, pp0, c20)

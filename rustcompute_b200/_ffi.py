@@ -26,9 +26,11 @@ WS3D_EPEER = 10
 
 WS3D_STATIC_ENERGY_MAX_PLANES = 8192   # include/ws3d.h
 
-WS3D_VARIANT_ZSTREAM = 0
-WS3D_VARIANT_NAIVE = 1
-WS3D_VARIANT_REFSHAPE = 2
+WS3D_VARIANT_AUTO = 0
+WS3D_VARIANT_ZSTREAM = 1
+WS3D_VARIANT_NAIVE = 2
+WS3D_VARIANT_REFSHAPE = 3
+WS3D_VARIANT_TMA = 4
 
 
 class ws3d_desc(C.Structure):

@@ -91,14 +91,15 @@ def _f32c(a, n: int, name: str) -> np.ndarray:
     return arr
 
 
-VARIANTS = {"zstream": _ffi.WS3D_VARIANT_ZSTREAM, "naive": _ffi.WS3D_VARIANT_NAIVE,
-            "refshape": _ffi.WS3D_VARIANT_REFSHAPE}
+VARIANTS = {"auto": _ffi.WS3D_VARIANT_AUTO, "zstream": _ffi.WS3D_VARIANT_ZSTREAM,
+            "naive": _ffi.WS3D_VARIANT_NAIVE, "refshape": _ffi.WS3D_VARIANT_REFSHAPE,
+            "tma": _ffi.WS3D_VARIANT_TMA}
 
 
 class GpuBackend3D:
     """GPU backend for one grid, or for one z-slab [z_begin, z_end) of it."""
 
-    def __init__(self, grid: SimulationGrid3D, *, device: int = 0, variant: str = "zstream",
+    def __init__(self, grid: SimulationGrid3D, *, device: int = 0, variant: str = "auto",
                  sponge_width: int = 0, sponge_max: float = 0.0,
                  z_begin: int = 0, z_end: int = 0, upload: bool = True):
         """GpuBackend3D::new (gpu_backend.rs:204-311): device state for `grid`
@@ -115,7 +116,7 @@ class GpuBackend3D:
 
     @classmethod
     def create(cls, width: int, height: int, depth: int, *, c_squared: float = 0.25,
-               damping: float = 1.0, device: int = 0, variant: str = "zstream",
+               damping: float = 1.0, device: int = 0, variant: str = "auto",
                sponge_width: int = 0, sponge_max: float = 0.0, z_begin: int = 0,
                z_end: int = 0, spin_budget_ns: int = 0) -> "GpuBackend3D":
         """A backend without a host grid (fields start at zero).  z_begin/z_end

@@ -6,14 +6,17 @@
 // instead of copying, exactly like gpu_backend.rs:372.
 #include "ws3d.h"
 #include "ws3d_kernels.cuh"
+#include "ws3d_tma.cuh"
 
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -65,6 +68,13 @@ struct ws3d_ctx {
 
     // optional per-launch timing of the step kernel (ws3d_step_timed)
     std::vector<cudaEvent_t> tev;
+
+    // TMA kernel: tensor maps of both field buffers in both roles and of c2
+    CUtensorMap mapP[2];   // pressure role: box 136 x (TY+2) x 1
+    CUtensorMap mapT[2];   // p_prev role:   box 128 x TY x 1
+    CUtensorMap mapC2;     // c2:            box 128 x TY x 1
+    bool tma_maps = false, tma_c2_map = false;
+    int tma_grid[2] = {0, 0};  // persistent grid size without / with c2
 };
 
 namespace {
@@ -168,8 +178,8 @@ StepParams make_params(const ws3d_ctx* c) {
         // and after its sources of step s reached our ghost planes).
         a.wait_val = c->halo_steps + 1;
         a.budget_ns = c->budget_ns;
-        a.status = reinterpret_cast<unsigned int*>(c->flags + 2);
     }
+    a.status = reinterpret_cast<unsigned int*>(c->flags + 2);
     return a;
 }
 
@@ -207,6 +217,87 @@ void launch_zstream(const ws3d_ctx* c, const StepParams& a) {
     k_step_zstream<kC2F, kCells, kTY><<<dim3(gx, gy, gz), dim3(32, kTY, 1), 0, c->stream>>>(a, chunk);
 }
 
+// ---- TMA kernel (single GPU, default face layout) --------------------------
+constexpr int kTmaTY = 8;
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// 3-D map over a slab-shaped buffer: dims {pitch, H, nz+2}, fp32, zero fill.
+bool encode_slab_map(const ws3d_ctx* c, CUtensorMap* m, const float* base, uint32_t box_x,
+                     uint32_t box_y) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {c->pitch, c->H, (cuuint64_t)c->nz + 2};
+    const cuuint64_t strides[2] = {(cuuint64_t)c->pitch * 4, (cuuint64_t)c->plane * 4};
+    const cuuint32_t box[3] = {box_x, box_y, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+void build_tma_maps(ws3d_ctx* c) {
+    c->tma_maps = false;
+    if (c->pitch < 160 || c->H < 16) return;   // the kernel's boxes need W > 128, H >= 16
+    bool ok = true;
+    for (int b = 0; b < 2; ++b) {
+        ok = ok && encode_slab_map(c, &c->mapP[b], c->buf[b], TmaLayout<kTmaTY, true>::kPRow,
+                                   kTmaTY + 2);
+        ok = ok && encode_slab_map(c, &c->mapT[b], c->buf[b], 128, kTmaTY);
+    }
+    c->tma_maps = ok;
+}
+
+void build_tma_c2_map(ws3d_ctx* c) {
+    c->tma_c2_map = c->c2f && c->tma_maps && encode_slab_map(c, &c->mapC2, c->c2f, 128, kTmaTY);
+}
+
+bool tma_eligible(const ws3d_ctx* c) {
+    return !c->halo && c->cells_default && c->tma_maps && (!c->c2f || c->tma_c2_map);
+}
+
+template <bool kC2F>
+ws3d_status launch_tma(ws3d_ctx* c, const StepParams& a) {
+    using L = TmaLayout<kTmaTY, kC2F>;
+    constexpr int kThreads = 32 * (kTmaTY + 1);
+    const int smem = L::smem_bytes(kTmaStages);
+    int& grid = c->tma_grid[kC2F ? 1 : 0];
+    if (grid == 0) {
+        cudaError_t e = cudaFuncSetAttribute(k_step_tma<kC2F, kTmaTY>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return cuda_fail(c, WS3D_ELAUNCH, e, "cudaFuncSetAttribute(tma)");
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step_tma<kC2F, kTmaTY>,
+                                                          kThreads, smem);
+        if (e != cudaSuccess || per_sm < 1)
+            return cuda_fail(c, WS3D_ELAUNCH, e, "occupancy(tma)");
+        grid = per_sm * std::max(1, c->sm_count);
+    }
+    const uint32_t tiles_x = (c->pitch + 127) / 128;
+    const uint32_t tiles = tiles_x * ((c->H + kTmaTY - 1) / kTmaTY);
+    const uint64_t total = (uint64_t)tiles * c->nz;
+    const uint32_t g = (uint32_t)std::min<uint64_t>((uint64_t)grid, total);
+    const int P = c->cur, T = c->cur ^ 1;
+    k_step_tma<kC2F, kTmaTY><<<g, kThreads, smem, c->stream>>>(c->mapP[P], c->mapT[T], c->mapC2,
+                                                                a, tiles_x, total);
+    return check_launch(c, "k_step_tma");
+}
+
 template <bool kC2F, bool kCells>
 void launch_naive(const ws3d_ctx* c, const StepParams& a) {
     dim3 block(32, 4, 2);
@@ -220,7 +311,16 @@ ws3d_status launch_step(ws3d_ctx* c) {
     StepParams a = make_params(c);
     const bool f = a.c2f != nullptr;
     const bool cells = a.types != nullptr;
-    switch (c->desc.variant) {
+    uint32_t v = c->desc.variant;
+    if (v == WS3D_VARIANT_AUTO) v = tma_eligible(c) ? WS3D_VARIANT_TMA : WS3D_VARIANT_ZSTREAM;
+    if (v == WS3D_VARIANT_TMA) {
+        if (!tma_eligible(c))
+            return fail(c, WS3D_EINVAL,
+                        "the TMA kernel needs one GPU, the default face layout, W > 128 and "
+                        "H >= 16; use the auto or zstream variant");
+        return f ? launch_tma<true>(c, a) : launch_tma<false>(c, a);
+    }
+    switch (v) {
         case WS3D_VARIANT_NAIVE:
             if (f && cells) launch_naive<true, true>(c, a);
             else if (f) launch_naive<true, false>(c, a);
@@ -329,18 +429,23 @@ ws3d_status launch_sources(ws3d_ctx* c) {
     return check_launch(c, "k_inject_sources");
 }
 
-// Read (and clear) the device status word the bounded waits write.
+// Read (and clear) the device status word the bounded waits write:
+// bit 0 / 1 = wait for the lower / upper neighbour's flag, bit 2 = a stage
+// wait of the TMA pipeline.
 ws3d_status check_device_status(ws3d_ctx* c) {
-    if (!c->halo || c->host_ordered) return WS3D_OK;
     unsigned int st = 0;
     WS3D_CUDA(c, cudaMemcpy(&st, c->flags + 2, sizeof st, cudaMemcpyDeviceToHost), WS3D_EDEVICE);
     if (!st) return WS3D_OK;
     WS3D_CUDA(c, cudaMemset(c->flags + 2, 0, sizeof(unsigned long long)), WS3D_EDEVICE);
+    if (st & 3u)
+        return fail(c, WS3D_ETIMEOUT,
+                    "a step gave up waiting for the %s%s%s neighbour after %.3f s (its flag "
+                    "never reached the step); the field of that step is not valid",
+                    (st & 1u) ? "lower" : "", (st & 3u) == 3u ? " and " : "",
+                    (st & 2u) ? "upper" : "", c->budget_ns * 1e-9);
     return fail(c, WS3D_ETIMEOUT,
-                "a step gave up waiting for the %s%s%s neighbour after %.3f s (its flag never "
-                "reached the step); the field of that step is not valid",
-                (st & 1u) ? "lower" : "", (st & 3u) == 3u ? " and " : "",
-                (st & 2u) ? "upper" : "", c->budget_ns * 1e-9);
+                "a TMA pipeline stage wait gave up (status 0x%x); the field of that step is "
+                "not valid", st);
 }
 
 bool desc_ok(const ws3d_desc* d, std::string* why) {
@@ -353,7 +458,7 @@ bool desc_ok(const ws3d_desc* d, std::string* why) {
     if (!(zb == 0 && ze == 0) && !(zb < ze && ze <= d->depth)) {
         *why = "z_begin/z_end outside [0, depth]"; return false;
     }
-    if (d->variant > WS3D_VARIANT_REFSHAPE) { *why = "unknown variant"; return false; }
+    if (d->variant > WS3D_VARIANT_TMA) { *why = "unknown variant"; return false; }
     if (d->sponge_width > 4096) { *why = "sponge_width above 4096"; return false; }
     return true;
 }
@@ -467,6 +572,7 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
     e = cudaMemsetAsync(c->flags, 0, kFlagWords * sizeof(unsigned long long), c->stream);
     if (e != cudaSuccess) return bail(cuda_fail(c, WS3D_EMEMORY, e, "cudaMemsetAsync(flags)"));
     if (desc->spin_budget) c->budget_ns = desc->spin_budget;
+    build_tma_maps(c);
     c->red_blocks = (uint32_t)std::max(1, c->sm_count) * 4u;
     if ((s = dalloc(c, &c->red_scratch, (size_t)c->red_blocks + 1, "reduction")) != WS3D_OK)
         return bail(s);
@@ -590,7 +696,9 @@ ws3d_status ws3d_set_c2_field(ws3d_ctx* c, const float* c2) {
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     if (!c2) {
+        WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
         dfree(c, c->c2f, c->slab);
+        c->tma_c2_map = false;
         return WS3D_OK;
     }
     ws3d_status s;
@@ -601,6 +709,7 @@ ws3d_status ws3d_set_c2_field(ws3d_ctx* c, const float* c2) {
     }
     if ((s = h2d_pitched(c, c->c2f, c2)) != WS3D_OK) return s;
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EMEMORY);
+    build_tma_c2_map(c);
     return WS3D_OK;
 }
 
@@ -894,8 +1003,8 @@ ws3d_status attach_common(ws3d_ctx* c, bool has_lo, uint32_t lo_nz, bool has_hi)
     c->halo_synced = false;
     c->halo_steps = 0;
     c->lo_ghost_off = has_lo ? (uint64_t)(lo_nz + 1) * c->plane : 0;
-    if (c->desc.variant != WS3D_VARIANT_ZSTREAM && c->halo)
-        return fail(c, WS3D_EINVAL, "halo exchange needs the zstream variant");
+    if (c->halo && c->desc.variant != WS3D_VARIANT_ZSTREAM && c->desc.variant != WS3D_VARIANT_AUTO)
+        return fail(c, WS3D_EINVAL, "halo exchange needs the auto or zstream variant");
     return rebuild_source_ghosts(c);
 }
 

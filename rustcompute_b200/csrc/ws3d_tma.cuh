@@ -1,0 +1,249 @@
+// ws3d_tma.cuh -- TMA-fed step kernel for one GPU (sm_100a).
+//
+// Same cell rule and arithmetic as k_step_zstream, different data movement:
+//
+//  * persistent grid: CTA c owns an equal share [c*T/G, (c+1)*T/G) of the
+//    T = tiles x nz "plane-tiles", walked tile-major / z-minor, so the work
+//    is balanced to one plane-tile and there is no tail wave;
+//  * one elected producer thread issues cp.async.bulk.tensor 3-D box loads
+//    (no multicast, local memory only) into a ring of kStages shared-memory
+//    stages: per plane the front pressure plane z+1 as a 136 x (TY+2) box
+//    (x from x0-4 so the start stays 16-byte aligned, one halo row above and
+//    below; out-of-range rows/columns arrive as zeros), and the 128 x TY
+//    boxes of p_prev and c2 for plane z;
+//  * TY consumer warps (one row each, a float4 per lane) keep the three-plane
+//    register queue along z and read their y / x neighbours from the staged
+//    plane; full/empty mbarriers hand stages between producer and consumers.
+//
+// Every mbarrier wait is bounded (try_wait with a suspend hint, iteration
+// cap); a wait that gives up sets the status word, the CTA stops consuming,
+// and the producer waits (bounded) for the copies it issued before exiting.
+#pragma once
+
+#include <cuda.h>
+
+#include "ws3d_kernels.cuh"
+
+namespace ws3d {
+
+template <int TY, bool kC2F>
+struct TmaLayout {
+    // dynamic shared memory: stages, 2*S mbarriers, abort flag, alignment slack
+    static constexpr int smem_bytes(int stages);
+    static constexpr int kPRow = 136;                        // floats per staged P row
+    static constexpr int kPBytes = kPRow * (TY + 2) * 4;
+    static constexpr int kPBytesPad = (kPBytes + 127) / 128 * 128;
+    static constexpr int kTBytes = 128 * TY * 4;             // p_prev / c2 tile
+    static constexpr int kStage = kPBytesPad + kTBytes * (kC2F ? 2 : 1);
+    static constexpr int kTxFull = kPBytes + kTBytes * (kC2F ? 2 : 1);
+};
+
+template <int TY, bool kC2F>
+constexpr int TmaLayout<TY, kC2F>::smem_bytes(int stages) {
+    return stages * kStage + 2 * stages * 8 + 16 + 128;
+}
+
+constexpr int kTmaStages = 4;
+constexpr uint32_t kMbarSpins = 1u << 22;  // x ~0.5 us suspend hint: bounded to about 2 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait for the phase with parity `parity` to complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t it = 0; it < kMbarSpins; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n"
+            " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity), "r"(500u)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// The run of plane-tiles a CTA walks: tile-major, z-minor.
+struct TmaRun {
+    uint32_t tile, zs, ze;  // planes [zs, ze) of tile `tile`
+};
+__device__ __forceinline__ bool next_run(uint64_t& k, uint64_t kend, uint32_t nz, TmaRun& r) {
+    if (k >= kend) return false;
+    r.tile = (uint32_t)(k / nz);
+    r.zs = (uint32_t)(k - (uint64_t)r.tile * nz);
+    const uint64_t left_in_tile = nz - r.zs;
+    const uint64_t take = (kend - k) < left_in_tile ? (kend - k) : left_in_tile;
+    r.ze = r.zs + (uint32_t)take;
+    k += take;
+    return true;
+}
+
+template <bool kC2F, int TY>
+__global__ void __launch_bounds__(32 * (TY + 1), 3)
+k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmPP,
+           const __grid_constant__ CUtensorMap tmC2, StepParams a, uint32_t tiles_x,
+           uint64_t total) {
+    using L = TmaLayout<TY, kC2F>;
+    constexpr int S = kTmaStages;
+    // Dynamic shared memory only (no static __shared__), rounded up to 128 B:
+    // TMA destinations must be 128-byte aligned.
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * L::kStage);
+    uint64_t* empty = full + S;
+    int& abort_flag = *reinterpret_cast<int*>(empty + S);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t G = gridDim.x;
+    const uint64_t kbeg = total * blockIdx.x / G, kend = total * (blockIdx.x + 1) / G;
+    if (kbeg >= kend) return;  // uniform over the CTA, before any barrier
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], TY);
+        }
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == TY) {
+        // ------------------------------------------------------------ producer
+        if (lane != 0) return;
+        uint64_t j = 0;  // items issued
+        uint64_t k = kbeg;
+        TmaRun r;
+        bool ok = true;
+        while (ok && next_run(k, kend, a.nz, r)) {
+            const int x0 = (int)((r.tile % tiles_x) * 128u), y0 = (int)((r.tile / tiles_x) * TY);
+            for (uint32_t i = 0; ok && i <= r.ze - r.zs; ++i, ++j) {
+                const int s = (int)(j % S);
+                if (j >= S && !mbar_wait(&empty[s], (uint32_t)((j / S - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                unsigned char* st = smem + s * L::kStage;
+                if (i == 0) {  // prologue item: pressure plane zs
+                    mbar_expect_tx(&full[s], L::kPBytes);
+                    tma_load_3d(st, &tmP, x0 - 4, y0 - 1, (int)r.zs + 1, &full[s]);
+                } else {       // plane z = zs + i - 1: pressure z+1, p_prev z, c2 z
+                    const int z = (int)r.zs + (int)i - 1;
+                    mbar_expect_tx(&full[s], L::kTxFull);
+                    tma_load_3d(st, &tmP, x0 - 4, y0 - 1, z + 2, &full[s]);
+                    tma_load_3d(st + L::kPBytesPad, &tmPP, x0, y0, z + 1, &full[s]);
+                    if (kC2F)
+                        tma_load_3d(st + L::kPBytesPad + L::kTBytes, &tmC2, x0, y0, z + 1,
+                                    &full[s]);
+                }
+            }
+        }
+        if (!ok) {
+            atomicOr(a.status, 4u);
+            atomicExch(&abort_flag, 1);
+        }
+        // Do not leave while copies this thread issued may still be landing.
+        const uint64_t first = j > (uint64_t)S ? j - S : 0;
+        for (uint64_t q = first; q < j; ++q) mbar_wait(&full[q % S], (uint32_t)((q / S) & 1));
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    const int w = warp;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int64_t P = (int64_t)a.plane;
+    uint64_t j = 0;  // items consumed
+    uint64_t k = kbeg;
+    TmaRun r;
+    while (next_run(k, kend, a.nz, r)) {
+        const uint32_t x0 = (r.tile % tiles_x) * 128u, y0 = (r.tile / tiles_x) * TY;
+        const uint32_t x = x0 + 4u * lane, y = y0 + w;
+        const bool act = x < a.pitch && y < a.H;
+        const int64_t row = (int64_t)y * a.pitch + x;
+        float4 pm = act ? ld4(a.p + zs_plane((int64_t)r.zs - 1, P) + row) : z4;
+        // prologue item
+        {
+            const int s = (int)(j % S);
+            if (!mbar_wait(&full[s], (uint32_t)((j / S) & 1))) {
+                atomicOr(a.status, 4u);
+                return;
+            }
+        }
+        const float* Pz = reinterpret_cast<const float*>(smem + (j % S) * L::kStage);
+        float4 pc = *reinterpret_cast<const float4*>(Pz + (w + 1) * L::kPRow + 4 + 4 * lane);
+        ++j;
+        for (uint32_t z = r.zs; z < r.ze; ++z, ++j) {
+            const int s = (int)(j % S);
+            if (!mbar_wait(&full[s], (uint32_t)((j / S) & 1)) || abort_flag) {
+                atomicOr(a.status, 4u);
+                return;
+            }
+            const unsigned char* st = smem + s * L::kStage;
+            const float* Pz1 = reinterpret_cast<const float*>(st);
+            const float* tPP = reinterpret_cast<const float*>(st + L::kPBytesPad);
+            const float* tC2 = reinterpret_cast<const float*>(st + L::kPBytesPad + L::kTBytes);
+            const float4 pn =
+                *reinterpret_cast<const float4*>(Pz1 + (w + 1) * L::kPRow + 4 + 4 * lane);
+            const float4 Sv = *reinterpret_cast<const float4*>(Pz + w * L::kPRow + 4 + 4 * lane);
+            const float4 Nv =
+                *reinterpret_cast<const float4*>(Pz + (w + 2) * L::kPRow + 4 + 4 * lane);
+            const float4 vpp = *reinterpret_cast<const float4*>(tPP + w * 128 + 4 * lane);
+            float4 vc2 = z4;
+            if (kC2F) vc2 = *reinterpret_cast<const float4*>(tC2 + w * 128 + 4 * lane);
+            float wl = __shfl_up_sync(0xffffffffu, pc.w, 1);
+            float er = __shfl_down_sync(0xffffffffu, pc.x, 1);
+            if (lane == 0) wl = Pz[(w + 1) * L::kPRow + 3];
+            if (lane == 31) er = Pz[(w + 1) * L::kPRow + 4 + 128];
+            if (act) {
+                const uint32_t zg = a.z0 + z;
+                const float c2x = kC2F ? vc2.x : a.c2, c2y = kC2F ? vc2.y : a.c2;
+                const float c2z = kC2F ? vc2.z : a.c2, c2w = kC2F ? vc2.w : a.c2;
+                float4 out;
+                out.x = cell_rule<false>(x + 0, y, zg, is_interior(x + 0, y, zg, a), wl, pc.y,
+                                         Sv.x, Nv.x, pm.x, pn.x, pc.x, vpp.x, c2x, 0, 0.f, a);
+                out.y = cell_rule<false>(x + 1, y, zg, is_interior(x + 1, y, zg, a), pc.x, pc.z,
+                                         Sv.y, Nv.y, pm.y, pn.y, pc.y, vpp.y, c2y, 0, 0.f, a);
+                out.z = cell_rule<false>(x + 2, y, zg, is_interior(x + 2, y, zg, a), pc.y, pc.w,
+                                         Sv.z, Nv.z, pm.z, pn.z, pc.z, vpp.z, c2z, 0, 0.f, a);
+                out.w = cell_rule<false>(x + 3, y, zg, is_interior(x + 3, y, zg, a), pc.z, er,
+                                         Sv.w, Nv.w, pm.w, pn.w, pc.w, vpp.w, c2w, 0, 0.f, a);
+                st4(a.pp + zs_plane((int64_t)z, P) + row, out);
+            }
+            // The previous stage (plane z: neighbours, and this row's centre) is done.
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[(j - 1) % S]);
+            pm = pc;
+            pc = pn;
+            Pz = Pz1;
+        }
+        // The last item of the run (plane ze) is consumed too.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[(j - 1) % S]);
+    }
+}
+
+}  // namespace ws3d

@@ -51,6 +51,8 @@ CASES = [
     ("c3_96x72x64_90", "c3", (96, 72, 64, 90)),
     ("c4_64x64x48_40", "c4", (64, 64, 48, 40)),
     ("c5_48x48x48_300", "c5", (48, 48, 48, 300)),
+    ("c3_160x64x40_40", "c3", (160, 64, 40, 40)),    # wide enough for the TMA kernel
+    ("c2_144x40x36_50", "c2", (144, 40, 36, 50)),
 ]
 
 

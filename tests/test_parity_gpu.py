@@ -15,7 +15,17 @@ pytestmark = pytest.mark.gpu
 
 REL_L2 = 1e-5
 MAX_ABS_FRAC = 1e-4
-VARIANTS = ["zstream", "naive", "refshape"]
+VARIANTS = ["auto", "zstream", "naive", "refshape", "tma"]
+
+
+def tma_ok(W, H, cells=False):
+    """Shapes the TMA kernel takes (one GPU, default faces, W > 128, H >= 16)."""
+    return W > 128 and H >= 16 and not cells
+
+
+def skip_unless_applicable(variant, W, H, cells=False):
+    if variant == "tma" and not tma_ok(W, H, cells):
+        pytest.skip("TMA kernel needs W > 128, H >= 16 and the default face layout")
 
 
 def assert_parity(got, want, what=""):
@@ -53,6 +63,7 @@ def gpu_for(wl, variant="zstream", grid=None):
 def test_c1_full_config_matches_oracle(variant):
     """BASELINE config 1 exactly: 64^3, Gaussian sigma 3, 200 steps."""
     wl = configs.build("c1")
+    skip_unless_applicable(variant, wl.W, wl.H)
     ref = oracle.from_workload(wl)
     ref.run(wl.steps, 1)
     g, b = gpu_for(wl, variant)
@@ -65,10 +76,12 @@ def test_c1_full_config_matches_oracle(variant):
 
 @pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("shape", [(13, 7, 5), (33, 17, 9), (130, 9, 20), (257, 11, 6),
-                                   (3, 3, 3), (4, 40, 3), (160, 70, 37)])
+                                   (3, 3, 3), (4, 40, 3), (160, 70, 37), (129, 16, 3),
+                                   (200, 33, 21), (520, 17, 12)])
 @pytest.mark.parametrize("c2f,sponge", [(False, 0), (True, 3)])
 def test_ragged_grids_random_fields(variant, shape, c2f, sponge):
     W, H, D = shape
+    skip_unless_applicable(variant, W, H)
     rng = np.random.default_rng(W * 1000 + H * 10 + D)
     n = W * H * D
     prm = AcousticParams3D(c_squared=0.2, simple_damping=0.9995)
@@ -93,7 +106,8 @@ def test_ragged_grids_random_fields(variant, shape, c2f, sponge):
 @pytest.mark.parametrize("variant", VARIANTS)
 def test_cell_types_obstacles_reflectors(variant):
     """Full reference cell semantics (grid3d.rs:193-219, :353-370)."""
-    W, H, D = 70, 33, 21
+    W, H, D = 150, 33, 21
+    skip_unless_applicable(variant, W, H, cells=True)
     prm = AcousticParams3D(c_squared=0.25, simple_damping=0.999)
     ref = oracle.OracleGrid(W, H, D, prm)
     ref.inject_impulse_c(35, 16, 10, 1.0)
@@ -117,9 +131,9 @@ def test_cell_types_obstacles_reflectors(variant):
     assert_parity(g.pressure_prev, ref.pressure_prev, f"cells-prev/{variant}")
 
 
-@pytest.mark.parametrize("variant", ["zstream", "naive"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma"])
 def test_c2_scaled_sources_and_sponge(variant):
-    wl = configs.build("c2", 48, 44, 40, steps=120)
+    wl = configs.build("c2", 144, 44, 40, steps=120)
     ref = oracle.from_workload(wl)
     ref.run(wl.steps, 1)
     g, b = gpu_for(wl, variant)
@@ -129,9 +143,9 @@ def test_c2_scaled_sources_and_sponge(variant):
     assert_parity(g.pressure, ref.pressure, f"c2s/{variant}")
 
 
-@pytest.mark.parametrize("variant", ["zstream", "naive"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma"])
 def test_c3_scaled_heterogeneous(variant):
-    wl = configs.build("c3", 96, 72, 64, steps=90)
+    wl = configs.build("c3", 160, 72, 64, steps=90)
     ref = oracle.from_workload(wl)
     ref.run(wl.steps, 1)
     g, b = gpu_for(wl, variant)
@@ -217,6 +231,21 @@ def test_reset_and_memory_usage():
     assert b.memory_usage() >= 2 * 24 * 24 * 24 * 4
 
 
+def test_tma_variant_rejects_shapes_it_cannot_take():
+    g = SimulationGrid3D(64, 64, 16)
+    b = GpuBackend3D(g, variant="tma")
+    with pytest.raises(InvalidArgument):
+        b.step_n(None, 1)
+    g2 = SimulationGrid3D(160, 40, 16)
+    g2.set_cell_type(50, 20, 8, CellType.OBSTACLE)
+    b2 = GpuBackend3D(g2, variant="tma")
+    with pytest.raises(InvalidArgument):
+        b2.step_n(None, 1)
+    b3 = GpuBackend3D(g2)            # auto takes the z-stream kernel for cell arrays
+    b3.step_n(None, 2)
+    b3.sync()
+
+
 def test_errors_are_raised_not_swallowed():
     g = SimulationGrid3D(16, 16, 16)
     b = GpuBackend3D(g)
@@ -230,22 +259,25 @@ def test_errors_are_raised_not_swallowed():
         GpuBackend3D(g, variant="nope")
 
 
-def test_full_size_c3_zstream_equals_naive_and_oracle():
+def test_full_size_c3_kernels_agree_and_match_oracle():
     """BASELINE config 3 at full size (512^3, heterogeneous, sponge, source):
-    size-independent checks -- two independent kernels agree bit for bit after
-    20 steps, and both agree with the oracle (all host threads) after 2."""
+    size-independent checks -- three independent kernels (TMA pipeline,
+    z-stream, one thread per cell) agree bit for bit after 20 steps, and the
+    TMA kernel agrees with the oracle (all host threads) after 2."""
     wl = configs.build("c3")
-    g1, b1 = gpu_for(wl, "zstream")
-    g2, b2 = gpu_for(wl, "naive")
-    b1.step_n(g1, 2)
-    b1.download_pressure(g1)
+    gt, bt = gpu_for(wl, "tma")
+    bt.step_n(gt, 2)
+    bt.download_pressure(gt)
     ref = oracle.from_workload(wl)
     ref.run(2, oracle.max_threads())
-    assert_parity(g1.pressure, ref.pressure, "c3-full-vs-oracle")
-    b1.step_n(g1, 18)
-    b2.step_n(g2, 20)
-    p1 = b1.download_field()
-    p2 = b2.download_field()
-    assert np.array_equal(p1, p2)
-    e = b1.energy()
-    assert np.isfinite(e) and e > 0
+    assert_parity(gt.pressure, ref.pressure, "c3-full-vs-oracle")
+    del ref
+    bt.step_n(gt, 18)
+    pt = bt.download_field()
+    bt.close()
+    for v in ("zstream", "naive"):
+        g, b = gpu_for(wl, v)
+        b.step_n(g, 20)
+        assert np.array_equal(b.download_field().view(np.uint32), pt.view(np.uint32)), v
+        b.close()
+    assert float(np.max(np.abs(pt))) > 0
