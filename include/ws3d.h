@@ -163,6 +163,15 @@ WS3D_API ws3d_status ws3d_step(ws3d_ctx *ctx, uint64_t n);
  * without a synchronise, this measures on the device).  n <= 2^20. */
 WS3D_API ws3d_status ws3d_step_timed(ws3d_ctx *ctx, uint64_t n, double *kernel_ms);
 
+/* PersistentBackend::step (persistent_backend.rs:269-336): n steps inside ONE
+ * cooperative launch (the reference's persistent kernel, generated by
+ * ringkernel-cuda-codegen persistent_fdtd.rs:713-978).  All CTAs are
+ * co-resident and meet at a bounded software grid barrier after each step
+ * (two barriers when point sources are set).  Asynchronous; ws3d_sync reports
+ * WS3D_ETIMEOUT if a barrier or neighbour wait gave up.  Same results, bit for
+ * bit, as ws3d_step(ctx, n); works on z-slabs (ws3d_halo_attach) too. */
+WS3D_API ws3d_status ws3d_step_persistent(ws3d_ctx *ctx, uint64_t n);
+
 /* GpuBackend3D::inject_impulse (gpu_backend.rs:411-442). Out-of-range
  * coordinates are ignored like grid3d.rs:147. */
 WS3D_API ws3d_status ws3d_inject_impulse(ws3d_ctx *ctx, uint32_t x, uint32_t y, uint32_t z,

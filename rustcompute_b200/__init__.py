@@ -9,11 +9,15 @@ from .backend import (  # noqa: F401
     CommandError, CompileError, DeviceError, GpuBackend3D, GpuError, InvalidArgument,
     LaunchError, MemoryError_, PeerError, ReadbackError, SimulationError, TimeoutError_,
 )
+from .persistent import (  # noqa: F401
+    PersistentBackend, PersistentBackendConfig, PersistentBackendStats, ResponseType,
+)
 from . import configs  # noqa: F401
 
 __all__ = [
     "AcousticParams3D", "CellType", "SimulationGrid3D", "GpuBackend3D", "GpuError",
     "DeviceError", "CompileError", "LaunchError", "MemoryError_", "SimulationError",
     "CommandError", "ReadbackError", "InvalidArgument", "TimeoutError_", "PeerError",
+    "PersistentBackend", "PersistentBackendConfig", "PersistentBackendStats", "ResponseType",
     "configs",
 ]

@@ -107,6 +107,7 @@ SIGNATURES = {
     "ws3d_set_sources": (C.c_int, [_CTX, C.c_uint32, _U32, _F, C.c_uint64]),
     "ws3d_step": (C.c_int, [_CTX, C.c_uint64]),
     "ws3d_step_timed": (C.c_int, [_CTX, C.c_uint64, C.POINTER(C.c_double)]),
+    "ws3d_step_persistent": (C.c_int, [_CTX, C.c_uint64]),
     "ws3d_inject_impulse": (C.c_int, [_CTX, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float]),
     "ws3d_inject_spherical_impulse": (
         C.c_int, [_CTX, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float]),

@@ -191,6 +191,10 @@ class GpuBackend3D:
         if grid is not None:
             grid.advance_clock(n)
 
+    def step_persistent(self, n: int) -> None:
+        """`n` steps in one cooperative launch (bit-identical to step_n)."""
+        self._chk(self._lib.ws3d_step_persistent(self._ctx, int(n)), "step_persistent")
+
     def step_timed(self, n: int) -> float:
         """`n` steps; returns the summed device time of the step-kernel launches
         in ms (CUDA events on the launch stream).  Synchronises."""

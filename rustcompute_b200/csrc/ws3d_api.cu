@@ -6,6 +6,7 @@
 // instead of copying, exactly like gpu_backend.rs:372.
 #include "ws3d.h"
 #include "ws3d_kernels.cuh"
+#include "ws3d_persistent.cuh"
 #include "ws3d_tma.cuh"
 
 #include <cuda_runtime.h>
@@ -15,6 +16,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -74,7 +76,12 @@ struct ws3d_ctx {
     CUtensorMap mapT[2];   // p_prev role:   box 128 x TY x 1
     CUtensorMap mapC2;     // c2:            box 128 x TY x 1
     bool tma_maps = false, tma_c2_map = false;
-    int tma_grid[2] = {0, 0};  // persistent grid size without / with c2
+    int tma_grid[2] = {0, 0};  // co-resident CTAs without / with c2
+    uint32_t tma_min_chunk = 32;  // WS3D_TMA_MIN_CHUNK (schedule tuning), read at create
+
+    // persistent mode: co-resident CTAs of k_persistent per instantiation
+    int pers_resident[4] = {0, 0, 0, 0};
+    uint64_t persistent_launches = 0;
 };
 
 namespace {
@@ -290,11 +297,10 @@ ws3d_status launch_tma(ws3d_ctx* c, const StepParams& a) {
     }
     const uint32_t tiles_x = (c->pitch + 127) / 128;
     const uint32_t tiles = tiles_x * ((c->H + kTmaTY - 1) / kTmaTY);
-    const uint64_t total = (uint64_t)tiles * c->nz;
-    const uint32_t g = (uint32_t)std::min<uint64_t>((uint64_t)grid, total);
+    const TmaSchedule sch = tma_schedule(tiles, c->nz, (uint32_t)grid, c->tma_min_chunk);
     const int P = c->cur, T = c->cur ^ 1;
-    k_step_tma<kC2F, kTmaTY><<<g, kThreads, smem, c->stream>>>(c->mapP[P], c->mapT[T], c->mapC2,
-                                                                a, tiles_x, total);
+    k_step_tma<kC2F, kTmaTY><<<sch.grid, kThreads, smem, c->stream>>>(
+        c->mapP[P], c->mapT[T], c->mapC2, a, tiles_x, tiles, sch.clen, sch.nitems);
     return check_launch(c, "k_step_tma");
 }
 
@@ -306,6 +312,61 @@ void launch_naive(const ws3d_ctx* c, const StepParams& a) {
 }
 
 ws3d_status ensure_cell_arrays(ws3d_ctx* c);
+
+// ---- persistent mode --------------------------------------------------------
+constexpr int kPersTY = 8;
+
+template <bool kC2F, bool kCells>
+ws3d_status launch_persistent(ws3d_ctx* c, uint64_t n) {
+    auto kern = k_persistent<kC2F, kCells, kPersTY>;
+    const int threads = 32 * kPersTY;
+    int& resident = c->pers_resident[(kC2F ? 2 : 0) + (kCells ? 1 : 0)];
+    if (resident == 0) {
+        int per_sm = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0);
+        if (e != cudaSuccess || per_sm < 1)
+            return cuda_fail(c, WS3D_ELAUNCH, e, "occupancy(persistent)");
+        resident = per_sm * std::max(1, c->sm_count);
+    }
+    PersistentArgs q{};
+    q.a = make_params(c);
+    for (int b = 0; b < 2; ++b) {
+        q.buf[b] = c->buf[b];
+        q.lo_base[b] = c->lo_base[b];
+        q.hi_base[b] = c->hi_base[b];
+    }
+    q.lo_ghost_off = c->lo_ghost_off;
+    q.lo_flag = c->halo ? c->lo_flag : nullptr;
+    q.hi_flag = c->halo ? c->hi_flag : nullptr;
+    q.halo_base = c->halo_steps;
+    q.bar_count = reinterpret_cast<unsigned int*>(c->flags + 4);
+    q.bar_gen = reinterpret_cast<unsigned int*>(c->flags + 5);
+    q.src_off = c->src_off;
+    q.wavelet = c->wavelet;
+    q.src_ghost = c->src_ghost;
+    q.n_src = c->n_src;
+    q.wl_len = c->wl_len;
+    q.step0 = c->step;
+    q.nsteps = n;
+    q.cur0 = (uint32_t)c->cur;
+    q.tiles_x = (c->pitch + kZsTileX - 1) / kZsTileX;
+    q.tiles = q.tiles_x * ((c->H + kPersTY - 1) / kPersTY);
+    const TmaSchedule sch = tma_schedule(q.tiles, c->nz, (uint32_t)resident, 8);
+    q.clen = sch.clen;
+    q.nitems = sch.nitems;
+    void* args[] = {&q};
+    cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, dim3(sch.grid),
+                                                dim3(32, kPersTY, 1), args, 0, c->stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(c, e == cudaErrorCooperativeLaunchTooLarge ? WS3D_ELAUNCH : WS3D_ELAUNCH,
+                         e, "cudaLaunchCooperativeKernel(k_persistent)");
+    }
+    c->launches++;
+    c->persistent_launches++;
+    return WS3D_OK;
+}
+
 
 ws3d_status launch_step(ws3d_ctx* c) {
     StepParams a = make_params(c);
@@ -572,6 +633,10 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
     e = cudaMemsetAsync(c->flags, 0, kFlagWords * sizeof(unsigned long long), c->stream);
     if (e != cudaSuccess) return bail(cuda_fail(c, WS3D_EMEMORY, e, "cudaMemsetAsync(flags)"));
     if (desc->spin_budget) c->budget_ns = desc->spin_budget;
+    if (const char* mc = getenv("WS3D_TMA_MIN_CHUNK")) {
+        const long v = strtol(mc, nullptr, 10);
+        if (v >= 1 && v <= (1 << 20)) c->tma_min_chunk = (uint32_t)v;
+    }
     build_tma_maps(c);
     c->red_blocks = (uint32_t)std::max(1, c->sm_count) * 4u;
     if ((s = dalloc(c, &c->red_scratch, (size_t)c->red_blocks + 1, "reduction")) != WS3D_OK)
@@ -993,6 +1058,28 @@ ws3d_status ws3d_stats_get(const ws3d_ctx* c, ws3d_stats* o) {
     return WS3D_OK;
 }
 
+
+ws3d_status ws3d_step_persistent(ws3d_ctx* c, uint64_t n) {
+    if (!c) return WS3D_EINVAL;
+    if (c->halo && c->host_ordered)
+        return fail(c, WS3D_ECOMMAND, "step_persistent: same-device slab groups step through "
+                                      "ws3d_step_group");
+    if (c->halo && !c->halo_synced)
+        return fail(c, WS3D_ECOMMAND, "step_persistent: fields changed since the last halo sync");
+    if (n == 0) return WS3D_OK;
+    DeviceGuard g(c->desc.device);
+    const bool f = c->c2f != nullptr, cells = !c->cells_default;
+    ws3d_status s;
+    if (f && cells) s = launch_persistent<true, true>(c, n);
+    else if (f) s = launch_persistent<true, false>(c, n);
+    else if (cells) s = launch_persistent<false, true>(c, n);
+    else s = launch_persistent<false, false>(c, n);
+    if (s != WS3D_OK) return s;
+    if (n & 1u) c->cur ^= 1;
+    c->step += n;
+    c->halo_steps += n;
+    return WS3D_OK;
+}
 
 // ---------------------------------------------------------------------------
 // z-slab halo exchange.

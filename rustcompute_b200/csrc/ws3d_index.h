@@ -95,4 +95,40 @@ inline void zs_grid(uint32_t pitch, uint32_t H, uint32_t nz, uint32_t zchunk, ui
     *gz = (nz + zchunk - 1) / zchunk;
 }
 
+// Schedule of the TMA kernel: (grid, chunk length, items) for `tiles` tiles
+// of nz planes on `resident` co-resident CTAs.  z is cut into chunks of at
+// least `min_chunk` planes (whole columns when nz < 2 * min_chunk); the chunk count maximises the
+// use of the resident CTA slots, items / (rounds * resident), preferring
+// fewer chunks on ties (fewer re-read boundary planes).
+struct TmaSchedule {
+    uint32_t grid, clen, nitems;
+};
+inline TmaSchedule tma_schedule(uint32_t tiles, uint32_t nz, uint32_t resident,
+                                uint32_t min_chunk = 32) {
+    TmaSchedule s;
+    if (resident < 1) resident = 1;
+    if (tiles < 1) tiles = 1;
+    if (min_chunk < 1) min_chunk = 1;
+    uint32_t best_k = 1;
+    double best = -1.0;
+    const uint32_t kmax = nz / min_chunk > 1 ? nz / min_chunk : 1;
+    for (uint32_t k = 1; k <= kmax && k <= 1024; ++k) {
+        const uint32_t clen = (nz + k - 1) / k;
+        const uint32_t chunks = (nz + clen - 1) / clen;
+        const uint64_t items = (uint64_t)chunks * tiles;
+        const uint64_t rounds = (items + resident - 1) / resident;
+        const double use = (double)items / ((double)rounds * resident);
+        if (use > best + 1e-9) {
+            best = use;
+            best_k = k;
+        }
+    }
+    s.clen = (nz + best_k - 1) / best_k;
+    if (s.clen < 1) s.clen = 1;
+    const uint32_t chunks = (nz + s.clen - 1) / s.clen;
+    s.nitems = chunks * tiles;
+    s.grid = s.nitems < resident ? s.nitems : resident;
+    return s;
+}
+
 }  // namespace ws3d

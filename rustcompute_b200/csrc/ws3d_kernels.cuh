@@ -167,18 +167,23 @@ __device__ __forceinline__ bool is_interior(uint32_t x, uint32_t y, uint32_t zg,
 // current plane staged in shared memory with one halo row above and below.
 // Loads for plane z+1 are issued one iteration ahead.
 // ---------------------------------------------------------------------------
-template <bool kC2F, bool kCells, int TY>
-__global__ void __launch_bounds__(32 * TY, 3)
-k_step_zstream(StepParams a, uint32_t zchunk) {
-    static_assert(TY >= 2, "the y-halo rows need two distinct warps");
-    __shared__ float4 srow[2][TY + 2][32];
-    __shared__ float shl[2][TY], shr[2][TY];
+template <int TY>
+struct ZsSmem {
+    float4 srow[2][TY + 2][32];
+    float shl[2][TY], shr[2][TY];
+};
 
+// One CTA (32 x TY threads) computes planes [zb, ze) of tile (bx, by).  Ends
+// with a CTA barrier so it can be called again on the same shared memory.
+template <bool kC2F, bool kCells, int TY>
+__device__ __forceinline__ void zs_tile(const StepParams& a, uint32_t bx, uint32_t by,
+                                        uint32_t zb, uint32_t ze, ZsSmem<TY>& sm) {
+    static_assert(TY >= 2, "the y-halo rows need two distinct warps");
+    auto& srow = sm.srow;
+    auto& shl = sm.shl;
+    auto& shr = sm.shr;
     const int lane = threadIdx.x, w = threadIdx.y;
     const bool halo_wait = a.wait_lo != nullptr || a.wait_hi != nullptr;
-    uint32_t zb, ze;
-    zs_chunk(zs_chunk_order(blockIdx.z, gridDim.z, halo_wait), zchunk, a.nz, &zb, &ze);
-    if (zb >= ze) return;  // uniform over the CTA, before any barrier
 
     // Boundary chunks read ghost planes that a neighbour GPU writes: wait
     // (bounded) for its flag.  Interior chunks never wait and are scheduled
@@ -196,7 +201,7 @@ k_step_zstream(StepParams a, uint32_t zchunk) {
             __syncthreads();
         }
     }
-    const ZsLane L = zs_lane<TY>(blockIdx.x, blockIdx.y, lane, w, a.W, a.H, a.pitch);
+    const ZsLane L = zs_lane<TY>(bx, by, lane, w, a.W, a.H, a.pitch);
     const bool act = L.act, ylo = L.ylo, yhi = L.yhi, xl = L.xl, xr = L.xr;
     const uint32_t x = L.x, y = L.y;
     const int64_t P = (int64_t)a.plane;
@@ -289,8 +294,20 @@ k_step_zstream(StepParams a, uint32_t zchunk) {
             cur = nxt;
         }
     }
-    // Order this thread's peer stores before the flag the signal kernel raises.
+    // Order this thread's peer stores before the flag the signal raises.
     if ((a.peer_lo && zb == 0) || (a.peer_hi && ze == a.nz)) __threadfence_system();
+    __syncthreads();
+}
+
+template <bool kC2F, bool kCells, int TY>
+__global__ void __launch_bounds__(32 * TY, 3)
+k_step_zstream(StepParams a, uint32_t zchunk) {
+    __shared__ ZsSmem<TY> sm;
+    const bool halo_wait = a.wait_lo != nullptr || a.wait_hi != nullptr;
+    uint32_t zb, ze;
+    zs_chunk(zs_chunk_order(blockIdx.z, gridDim.z, halo_wait), zchunk, a.nz, &zb, &ze);
+    if (zb >= ze) return;  // uniform over the CTA, before any barrier
+    zs_tile<kC2F, kCells, TY>(a, blockIdx.x, blockIdx.y, zb, ze, sm);
 }
 
 // ---------------------------------------------------------------------------
@@ -366,10 +383,10 @@ __global__ void __launch_bounds__(256) k_ref_boundary(float* pp, const uint8_t* 
 // coinciding sources add in the same order as the reference loop.  A source
 // on a slab's first or last plane is also added to the neighbour's ghost copy
 // of that plane (ghost_row >= 0, side 0 = lower neighbour, 1 = upper).
-__global__ void k_inject_sources(float* p, float* pp, const uint64_t* off, const float* wavelet,
-                                 uint32_t n, uint64_t len, uint64_t step,
-                                 const long long* ghost_row, float* ghost_lo, float* ghost_hi) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+__device__ __forceinline__ void inject_sources_dev(float* p, float* pp, const uint64_t* off,
+                                                   const float* wavelet, uint32_t n, uint64_t len,
+                                                   uint64_t step, const long long* ghost_row,
+                                                   float* ghost_lo, float* ghost_hi) {
     for (uint32_t k = 0; k < n; ++k) {
         const float amp = step < len ? wavelet[(uint64_t)k * len + step] : 0.0f;
         p[off[k]] = __fadd_rn(p[off[k]], amp);
@@ -380,6 +397,13 @@ __global__ void k_inject_sources(float* p, float* pp, const uint64_t* off, const
             if (g >= 0 && gp) gp[g] = __fadd_rn(gp[g], amp);
         }
     }
+}
+
+__global__ void k_inject_sources(float* p, float* pp, const uint64_t* off, const float* wavelet,
+                                 uint32_t n, uint64_t len, uint64_t step,
+                                 const long long* ghost_row, float* ghost_lo, float* ghost_hi) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    inject_sources_dev(p, pp, off, wavelet, n, len, step, ghost_row, ghost_lo, ghost_hi);
 }
 
 // Impulse factors applied to a neighbour's ghost copy of a boundary plane

@@ -2,9 +2,11 @@
 //
 // Same cell rule and arithmetic as k_step_zstream, different data movement:
 //
-//  * persistent grid: CTA c owns an equal share [c*T/G, (c+1)*T/G) of the
-//    T = tiles x nz "plane-tiles", walked tile-major / z-minor, so the work
-//    is balanced to one plane-tile and there is no tail wave;
+//  * persistent grid over (z-chunk, tile) items in chunk-major order: tiles
+//    that run together are neighbours in the same z-chunk and stream through
+//    z in lockstep, so the halo rows a tile stages from its neighbours hit L2
+//    (a tile-major balanced split re-read them from DRAM: +30 % traffic at
+//    512^3); the chunk length is chosen so items divide evenly over the CTAs;
 //  * one elected producer thread issues cp.async.bulk.tensor 3-D box loads
 //    (no multicast, local memory only) into a ring of kStages shared-memory
 //    stages: per plane the front pressure plane z+1 as a 136 x (TY+2) box
@@ -86,18 +88,23 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
-// The run of plane-tiles a CTA walks: tile-major, z-minor.
+// Work items: item = chunk * tiles + tile (chunk-major, tile x fastest),
+// covering planes [chunk * clen, min(nz, (chunk + 1) * clen)) of the tile.
+// CTA c takes items c, c + G, c + 2G, ...  Items that run at the same time are
+// neighbouring tiles of the same z-chunk, so the tiles advance through z in
+// lockstep and the halo rows one tile stages from its neighbours are still in
+// L2 when it needs them.
 struct TmaRun {
     uint32_t tile, zs, ze;  // planes [zs, ze) of tile `tile`
 };
-__device__ __forceinline__ bool next_run(uint64_t& k, uint64_t kend, uint32_t nz, TmaRun& r) {
-    if (k >= kend) return false;
-    r.tile = (uint32_t)(k / nz);
-    r.zs = (uint32_t)(k - (uint64_t)r.tile * nz);
-    const uint64_t left_in_tile = nz - r.zs;
-    const uint64_t take = (kend - k) < left_in_tile ? (kend - k) : left_in_tile;
-    r.ze = r.zs + (uint32_t)take;
-    k += take;
+__device__ __forceinline__ bool next_run(uint32_t& item, uint32_t nitems, uint32_t tiles,
+                                         uint32_t clen, uint32_t nz, TmaRun& r) {
+    if (item >= nitems) return false;
+    const uint32_t chunk = item / tiles;
+    r.tile = item - chunk * tiles;
+    r.zs = chunk * clen;
+    r.ze = min(nz, r.zs + clen);
+    item += gridDim.x;
     return true;
 }
 
@@ -105,7 +112,7 @@ template <bool kC2F, int TY>
 __global__ void __launch_bounds__(32 * (TY + 1), 3)
 k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmPP,
            const __grid_constant__ CUtensorMap tmC2, StepParams a, uint32_t tiles_x,
-           uint64_t total) {
+           uint32_t tiles, uint32_t clen, uint32_t nitems) {
     using L = TmaLayout<TY, kC2F>;
     constexpr int S = kTmaStages;
     // Dynamic shared memory only (no static __shared__), rounded up to 128 B:
@@ -118,9 +125,7 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
     int& abort_flag = *reinterpret_cast<int*>(empty + S);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t G = gridDim.x;
-    const uint64_t kbeg = total * blockIdx.x / G, kend = total * (blockIdx.x + 1) / G;
-    if (kbeg >= kend) return;  // uniform over the CTA, before any barrier
+    if (blockIdx.x >= nitems) return;  // uniform over the CTA, before any barrier
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -135,11 +140,11 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
     if (warp == TY) {
         // ------------------------------------------------------------ producer
         if (lane != 0) return;
-        uint64_t j = 0;  // items issued
-        uint64_t k = kbeg;
+        uint64_t j = 0;  // stage items issued
+        uint32_t item = blockIdx.x;
         TmaRun r;
         bool ok = true;
-        while (ok && next_run(k, kend, a.nz, r)) {
+        while (ok && next_run(item, nitems, tiles, clen, a.nz, r)) {
             const int x0 = (int)((r.tile % tiles_x) * 128u), y0 = (int)((r.tile / tiles_x) * TY);
             for (uint32_t i = 0; ok && i <= r.ze - r.zs; ++i, ++j) {
                 const int s = (int)(j % S);
@@ -176,10 +181,10 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
     const int w = warp;
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
     const int64_t P = (int64_t)a.plane;
-    uint64_t j = 0;  // items consumed
-    uint64_t k = kbeg;
+    uint64_t j = 0;  // stage items consumed
+    uint32_t item = blockIdx.x;
     TmaRun r;
-    while (next_run(k, kend, a.nz, r)) {
+    while (next_run(item, nitems, tiles, clen, a.nz, r)) {
         const uint32_t x0 = (r.tile % tiles_x) * 128u, y0 = (r.tile / tiles_x) * TY;
         const uint32_t x = x0 + 4u * lane, y = y0 + w;
         const bool act = x < a.pitch && y < a.H;

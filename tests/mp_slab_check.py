@@ -22,6 +22,8 @@ def main():
     ap.add_argument("--workload", default="c3")
     ap.add_argument("--grid", default="96x80x64")
     ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--persistent", action="store_true",
+                    help="advance the slabs with ws3d_step_persistent")
     args = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -59,9 +61,10 @@ def main():
         zc = slab_bounds(D, world, r)[0]
         b.inject_impulse(W // 3, H // 2, zc, 0.25)
         b.inject_impulse(W // 2, H // 3, zc - 1, -0.5)
-    b.step_n(None, 7)
+    adv = b.step_persistent if args.persistent else (lambda n: b.step_n(None, n))
+    adv(7)
     b.inject_spherical_impulse(W // 2, H // 2, slab_bounds(D, world, world // 2)[0], 0.3, 3.0)
-    b.step_n(None, args.steps - 7)
+    adv(args.steps - 7)
     b.sync()
     p, pp = b.download_field(with_prev=True)
     parts = [None] * world

@@ -206,3 +206,20 @@ def test_sponge_table_values(oracle_lib):
     assert np.all(np.diff(t) > 0) and t[-1] < 1.0
     d = 5
     assert t[d] == np.float32(1.0 - np.float64(np.float32(0.1)) * ((16 - d) / 16) ** 2)
+
+
+def test_persistent_config_restated():
+    """persistent_backend.rs:495-513 (config defaults and builder)."""
+    from rustcompute_b200 import PersistentBackendConfig
+    c = PersistentBackendConfig()
+    assert c.tile_size == (8, 8, 8) and c.use_cooperative and c.progress_interval == 100
+    c = PersistentBackendConfig().with_tile_size(4, 4, 4).with_cooperative(False) \
+        .with_progress_interval(50)
+    assert c.tile_size == (4, 4, 4) and not c.use_cooperative and c.progress_interval == 50
+
+
+def test_error_display_restated():
+    """persistent_backend.rs:515-522 / gpu_backend.rs:13-23: error kinds and messages."""
+    from rustcompute_b200 import CompileError, DeviceError, GpuError
+    assert issubclass(DeviceError, GpuError) and issubclass(CompileError, GpuError)
+    assert "device" in str(DeviceError("GpuBackend3D::new: GPU device error: x")).lower()

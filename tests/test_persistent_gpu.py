@@ -1,0 +1,153 @@
+"""Persistent mode (many steps in one cooperative launch) on the GPU.
+
+Bit-identical to the per-step path and to the oracle; mixes with per-step
+calls; the PersistentBackend mirror of the reference API; and the bounded
+neighbour wait inside a persistent launch (a child process exports a slab
+that never steps).
+"""
+import multiprocessing as mpm
+import os
+import sys
+import time
+
+import numpy as np
+import pytest
+
+import oracle
+from rustcompute_b200 import (CellType, GpuBackend3D, PersistentBackend, PersistentBackendConfig,
+                              ResponseType, SimulationGrid3D, TimeoutError_, configs)
+from rustcompute_b200.grid import AcousticParams3D
+from rustcompute_b200.slab import attach
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def backend_for(wl, variant="auto", cells=None):
+    g = SimulationGrid3D(wl.W, wl.H, wl.D, AcousticParams3D(c_squared=wl.c_squared,
+                                                            simple_damping=wl.damping))
+    g.pressure[:], g.pressure_prev[:] = wl.initial_fields()
+    if cells is not None:
+        g.cell_types[:], g.reflection_coeff[:] = cells
+    b = GpuBackend3D(g, variant=variant, sponge_width=wl.sponge_width, sponge_max=wl.sponge_max)
+    c2 = wl.c2_field()
+    if c2 is not None:
+        b.set_c2_field(c2)
+    if len(wl.sources):
+        b.set_sources(wl.sources, wl.wavelet)
+    return g, b
+
+
+@pytest.mark.parametrize("name,grid,steps", [("c5", (64, 64, 64), 300),
+                                             ("c3", (160, 72, 64), 90),
+                                             ("c2", (96, 40, 37), 120),
+                                             ("c1", (13, 7, 5), 9)])
+def test_persistent_equals_step_and_oracle(name, grid, steps):
+    wl = configs.build(name, *grid, steps=steps)
+    _, bp = backend_for(wl)
+    bp.step_persistent(steps)
+    bp.sync()
+    pp_, ppp = bp.download_field(with_prev=True)
+    _, bs = backend_for(wl)
+    bs.step_n(None, steps)
+    sp, spp = bs.download_field(with_prev=True)
+    assert np.array_equal(pp_.view(np.uint32), sp.view(np.uint32))
+    assert np.array_equal(ppp.view(np.uint32), spp.view(np.uint32))
+    ref = oracle.from_workload(wl)
+    ref.run(steps, 1)
+    assert np.array_equal(pp_.view(np.uint32), ref.pressure.view(np.uint32))
+
+
+def test_persistent_with_cell_arrays():
+    wl = configs.build("c1", 100, 40, 30, steps=60)
+    g = SimulationGrid3D(wl.W, wl.H, wl.D)
+    g.create_obstacle(20, 5, 4, 30, 12, 9, CellType.OBSTACLE)
+    g.create_obstacle(60, 20, 10, 64, 25, 15, CellType.REFLECTOR)
+    cells = (g.cell_types.copy(), g.reflection_coeff.copy())
+    _, bp = backend_for(wl, cells=cells)
+    bp.step_persistent(60)
+    _, bs = backend_for(wl, cells=cells)
+    bs.step_n(None, 60)
+    assert np.array_equal(bp.download_field(), bs.download_field())
+
+
+def test_persistent_mixes_with_per_step_calls():
+    wl = configs.build("c2", 70, 50, 41, steps=100)
+    _, a = backend_for(wl)
+    a.step_persistent(37)
+    a.step_n(None, 13)
+    a.step_persistent(49)
+    a.step_n(None, 1)
+    _, b = backend_for(wl)
+    b.step_n(None, 100)
+    assert np.array_equal(a.download_field(), b.download_field())
+    assert a.stats()["step"] == 100
+
+
+def test_persistent_backend_api_restated():
+    """persistent_backend.rs:253-446 behaviour through the mirror."""
+    prm = AcousticParams3D.new(343.0, 0.1)
+    grid = SimulationGrid3D(48, 48, 48, prm)
+    grid.inject_impulse(24, 24, 24, 1.0)
+    pb = PersistentBackend(grid, PersistentBackendConfig().with_progress_interval(25))
+    assert not pb.is_running()
+    copy = SimulationGrid3D(48, 48, 48, prm)
+    pb.download_pressure(copy)                  # before start: nothing downloaded
+    assert copy.total_energy() == 0.0
+    pb.step(grid, 60)
+    assert pb.is_running() and grid.step == 60
+    st = pb.stats()
+    assert st.current_step == 60 and st.steps_remaining == 0 and st.total_energy > 0
+    resp = pb.poll_responses()
+    assert (ResponseType.ENERGY in [r[0] for r in resp]) and pb.poll_responses() == []
+    pb.inject_impulse(10, 10, 10, 0.5)
+    pb.step(grid, 10)
+    pb.download_pressure(grid)
+    ref = SimulationGrid3D(48, 48, 48, prm)
+    ref.inject_impulse(24, 24, 24, 1.0)
+    gb = GpuBackend3D(ref)
+    gb.step_n(ref, 60)
+    gb.inject_impulse(10, 10, 10, 0.5)
+    gb.step_n(ref, 10)
+    gb.download_pressure(ref)
+    assert np.array_equal(grid.pressure, ref.pressure)
+    pb.shutdown()
+    assert not pb.is_running() and pb.stats().has_terminated
+    pb.close()
+
+
+def _idle_lower_neighbour(conn, grid, zb, ze):
+    sys.path.insert(0, ROOT)
+    from rustcompute_b200 import GpuBackend3D as B
+    from rustcompute_b200.slab import export_handles as exp
+    W, H, D = grid
+    b = B.create(W, H, D, z_begin=zb, z_end=ze)
+    conn.send(exp(b))
+    conn.recv()
+    b.close()
+
+
+def test_persistent_neighbour_wait_times_out():
+    grid = (64, 40, 48)
+    W, H, D = grid
+    ctx = mpm.get_context("spawn")
+    parent, child = ctx.Pipe()
+    proc = ctx.Process(target=_idle_lower_neighbour, args=(child, grid, 0, 24))
+    proc.start()
+    try:
+        lower = parent.recv()
+        b = GpuBackend3D.create(W, H, D, z_begin=24, z_end=48, spin_budget_ns=200_000_000)
+        attach(b, lower, None)
+        b._chk(b._lib.ws3d_halo_sync(b._ctx, 0), "sync0")
+        b._chk(b._lib.ws3d_halo_sync(b._ctx, 1), "sync1")
+        t0 = time.time()
+        b.step_persistent(50)
+        with pytest.raises(TimeoutError_):
+            b.sync()
+        assert time.time() - t0 < 30
+        b.sync()
+        b.close()
+    finally:
+        parent.send("done")
+        proc.join(timeout=60)
+    assert proc.exitcode == 0

@@ -119,8 +119,11 @@ def _gpu_count():
 
 
 @pytest.mark.multigpu
-@pytest.mark.parametrize("name,grid,steps", [("c3", "96x80x64", 60), ("c2", "64x48x45", 50)])
-def test_multi_process_nvlink_slabs_equal_one_gpu(name, grid, steps):
+@pytest.mark.parametrize("name,grid,steps,persistent", [("c3", "96x80x64", 60, False),
+                                                        ("c2", "64x48x45", 50, False),
+                                                        ("c5", "128x128x128", 200, True),
+                                                        ("c3", "160x64x64", 40, True)])
+def test_multi_process_nvlink_slabs_equal_one_gpu(name, grid, steps, persistent):
     n = _gpu_count()
     if n < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -129,7 +132,7 @@ def test_multi_process_nvlink_slabs_equal_one_gpu(name, grid, steps):
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", "--master-port", str(29400 + os.getpid() % 1000),
            os.path.join(ROOT, "tests", "mp_slab_check.py"), "--workload", name, "--grid", grid,
-           "--steps", str(steps)]
+           "--steps", str(steps)] + (["--persistent"] if persistent else [])
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, capture_output=True, text=True,
                        env=env)
     assert r.returncode == 0 and "SLAB-CHECK OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
