@@ -153,7 +153,7 @@ def cpu_sample_run(wl, target_s: float = 12.0, nthreads: int = 0):
     filling ~target_s when one step takes < target_s/3, else a z-slab of the
     same recipe."""
     import oracle
-    nthreads = nthreads or oracle.max_threads()
+    nthreads = nthreads or host_threads()
     g = oracle.from_workload(wl)
     g.run(1, nthreads)                     # warm-up (first touch)
     t0 = time.perf_counter()
@@ -183,7 +183,7 @@ def run_reference(args, wl):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    nthreads = oracle.max_threads()
+    nthreads = host_threads()
     # One timed step = one full-grid step when affordable, else a z-slab sample.
     probe = wl.scaled(wl.W, wl.H, min(wl.D, 34), steps=2)
     g = oracle.from_workload(probe)
@@ -217,7 +217,7 @@ def run_reference(args, wl):
         "note": "the reference Rust crate cannot be built in this image (no cargo, wgpu "
                 "dependency); this arm times its CPU step restated in C (oracle/)",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def make_backend(wl, variant, device, zb, ze):
@@ -410,10 +410,36 @@ def run_ours(args, wl):
         pg.barrier()
         pg.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(result)
+
+
+def host_threads() -> int:
+    """Host cores this process may use (torchrun sets OMP_NUM_THREADS=1 for
+    its ranks; the CPU legs use every core they are allowed to run on)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Write the result line to the real stdout (libraries such as NCCL may
+    print banners to fd 1; main() points fd 1 at stderr for them)."""
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 
 def main():
+    global _JSON_OUT
+    # Keep stdout for the one JSON line: anything else written to fd 1
+    # (NCCL's version banner, library chatter) goes to stderr.
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse()
     from rustcompute_b200 import configs
     if args.grid:

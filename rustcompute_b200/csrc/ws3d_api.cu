@@ -351,7 +351,9 @@ ws3d_status launch_persistent(ws3d_ctx* c, uint64_t n) {
     q.cur0 = (uint32_t)c->cur;
     q.tiles_x = (c->pitch + kZsTileX - 1) / kZsTileX;
     q.tiles = q.tiles_x * ((c->H + kPersTY - 1) / kPersTY);
-    const TmaSchedule sch = tma_schedule(q.tiles, c->nz, (uint32_t)resident, 8);
+    // Persistent launches are latency-bound per plane (small, L2-resident
+    // grids): chunks down to 4 planes give every resident CTA work each step.
+    const TmaSchedule sch = tma_schedule(q.tiles, c->nz, (uint32_t)resident, 4);
     q.clen = sch.clen;
     q.nitems = sch.nitems;
     void* args[] = {&q};

@@ -72,17 +72,21 @@ WS3D_HD void zs_chunk(uint32_t bz, uint32_t zchunk, uint32_t nz, uint32_t* zb, u
     *ze = e < nz ? (uint32_t)e : nz;
 }
 
-// Launch geometry of the z-streaming kernel (host side).
+// Launch geometry of the z-streaming kernel (host side): enough CTAs for ~8
+// resident waves over the SMs.  Each chunk re-reads two extra planes, so
+// chunks stay >= 16 planes when the slab streams from HBM; a slab whose
+// three fields fit in L2 (<= 64 MiB) uses chunks down to 4 planes, since
+// there the re-reads are L2 hits and the per-plane latency dominates.
 template <int TY>
 inline uint32_t zs_zchunk(uint32_t pitch, uint32_t H, uint32_t nz, int sm_count) {
     const uint32_t tiles = ((pitch + kZsTileX - 1) / kZsTileX) * ((H + TY - 1) / TY);
-    // Enough CTAs for ~8 resident waves over the SMs, but chunks of at least
-    // 16 planes so the two extra planes a chunk re-reads stay cheap.
     const uint32_t want = (uint32_t)(sm_count > 0 ? sm_count : 1) * 3u * 8u;
     uint32_t nchunks = (want + tiles - 1) / tiles;
     if (nchunks < 1) nchunks = 1;
     uint32_t chunk = (nz + nchunks - 1) / nchunks;
-    if (chunk < 16) chunk = 16;
+    const uint64_t field_bytes = (uint64_t)pitch * H * nz * 4u * 3u;
+    const uint32_t min_chunk = field_bytes <= (64ull << 20) ? 4u : 16u;
+    if (chunk < min_chunk) chunk = min_chunk;
     const uint32_t cap = nz > 0 ? nz : 1;
     return chunk < cap ? chunk : cap;
 }
