@@ -65,13 +65,15 @@ typedef enum ws3d_status {
 /* Step-kernel variants (all run on the GPU; none falls back to the CPU). */
 enum {
     WS3D_VARIANT_AUTO = 0,     /* default: TMA on one GPU with the default face layout
-                                  and W > 128, H >= 16; ZSTREAM otherwise */
+                                  and W > 128, H >= 16; else ASYNC with the default face
+                                  layout (z-slabs included); ZSTREAM with cell arrays */
     WS3D_VARIANT_ZSTREAM = 1,  /* 2-D tile streaming along z, 128-bit loads, register
                                   prefetch; the kernel used for z-slabs and cell arrays */
     WS3D_VARIANT_NAIVE = 2,    /* one thread per cell, fused boundary (comparator) */
     WS3D_VARIANT_REFSHAPE = 3, /* the reference's launch shape: 8x8x4 stencil launch
                                   plus a separate full-grid boundary launch (comparator) */
-    WS3D_VARIANT_TMA = 4       /* persistent, TMA-fed 4-stage shared-memory pipeline */
+    WS3D_VARIANT_TMA = 4,      /* persistent, TMA-fed 4-stage shared-memory pipeline (one GPU) */
+    WS3D_VARIANT_ASYNC = 5     /* persistent, cp.async-fed 5-stage pipeline (one GPU or z-slabs) */
 };
 
 typedef struct ws3d_desc {

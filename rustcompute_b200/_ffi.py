@@ -31,6 +31,7 @@ WS3D_VARIANT_ZSTREAM = 1
 WS3D_VARIANT_NAIVE = 2
 WS3D_VARIANT_REFSHAPE = 3
 WS3D_VARIANT_TMA = 4
+WS3D_VARIANT_ASYNC = 5
 
 
 class ws3d_desc(C.Structure):

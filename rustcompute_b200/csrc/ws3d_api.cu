@@ -6,6 +6,7 @@
 // instead of copying, exactly like gpu_backend.rs:372.
 #include "ws3d.h"
 #include "ws3d_kernels.cuh"
+#include "ws3d_async.cuh"
 #include "ws3d_persistent.cuh"
 #include "ws3d_tma.cuh"
 
@@ -77,6 +78,7 @@ struct ws3d_ctx {
     CUtensorMap mapC2;     // c2:            box 128 x TY x 1
     bool tma_maps = false, tma_c2_map = false;
     int tma_grid[2] = {0, 0};  // co-resident CTAs without / with c2
+    int async_grid[2] = {0, 0};
     uint32_t tma_min_chunk = 32;  // WS3D_TMA_MIN_CHUNK (schedule tuning), read at create
 
     // persistent mode: co-resident CTAs of k_persistent per instantiation
@@ -304,6 +306,39 @@ ws3d_status launch_tma(ws3d_ctx* c, const StepParams& a) {
     return check_launch(c, "k_step_tma");
 }
 
+// ---- cp.async kernel (one GPU or z-slabs, default face layout) -------------
+template <bool kC2F>
+ws3d_status launch_async(ws3d_ctx* c, const StepParams& a) {
+    using L = AsyncLayout<kC2F>;
+    constexpr int kThreads = 32 * kAsyncTY;
+    const int smem = L::smem_bytes();
+    int& resident = c->async_grid[kC2F ? 1 : 0];
+    if (resident == 0) {
+        cudaError_t e = cudaFuncSetAttribute(k_step_async<kC2F>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return cuda_fail(c, WS3D_ELAUNCH, e, "cudaFuncSetAttribute(async)");
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step_async<kC2F>, kThreads,
+                                                          smem);
+        if (e != cudaSuccess || per_sm < 1)
+            return cuda_fail(c, WS3D_ELAUNCH, e, "occupancy(async)");
+        resident = per_sm * std::max(1, c->sm_count);
+    }
+    AsyncSched sc{};
+    sc.tiles_x = (c->pitch + 127) / 128;
+    sc.tiles = sc.tiles_x * ((c->H + kAsyncTY - 1) / kAsyncTY);
+    sc.nz = c->nz;
+    sc.halo = a.wait_lo != nullptr || a.wait_hi != nullptr;
+    const uint64_t field_bytes = (uint64_t)c->plane * c->nz * 4u * 3u;
+    const uint32_t min_chunk = field_bytes <= (64ull << 20) ? 8u : c->tma_min_chunk;
+    const TmaSchedule sch = tma_schedule(sc.tiles, c->nz, (uint32_t)resident, min_chunk);
+    sc.clen = sch.clen;
+    sc.nchunks = (c->nz + sch.clen - 1) / sch.clen;
+    sc.nitems = sch.nitems;
+    k_step_async<kC2F><<<sch.grid, kThreads, smem, c->stream>>>(a, sc);
+    return check_launch(c, "k_step_async");
+}
+
 template <bool kC2F, bool kCells>
 void launch_naive(const ws3d_ctx* c, const StepParams& a) {
     dim3 block(32, 4, 2);
@@ -375,7 +410,16 @@ ws3d_status launch_step(ws3d_ctx* c) {
     const bool f = a.c2f != nullptr;
     const bool cells = a.types != nullptr;
     uint32_t v = c->desc.variant;
-    if (v == WS3D_VARIANT_AUTO) v = tma_eligible(c) ? WS3D_VARIANT_TMA : WS3D_VARIANT_ZSTREAM;
+    if (v == WS3D_VARIANT_AUTO)
+        v = tma_eligible(c) ? WS3D_VARIANT_TMA
+                            : (c->cells_default ? WS3D_VARIANT_ASYNC : WS3D_VARIANT_ZSTREAM);
+    if (v == WS3D_VARIANT_ASYNC) {
+        if (!c->cells_default)
+            return fail(c, WS3D_EINVAL,
+                        "the async kernel evaluates the default face layout only; use the auto "
+                        "or zstream variant for per-cell boundary arrays");
+        return f ? launch_async<true>(c, a) : launch_async<false>(c, a);
+    }
     if (v == WS3D_VARIANT_TMA) {
         if (!tma_eligible(c))
             return fail(c, WS3D_EINVAL,
@@ -521,7 +565,7 @@ bool desc_ok(const ws3d_desc* d, std::string* why) {
     if (!(zb == 0 && ze == 0) && !(zb < ze && ze <= d->depth)) {
         *why = "z_begin/z_end outside [0, depth]"; return false;
     }
-    if (d->variant > WS3D_VARIANT_TMA) { *why = "unknown variant"; return false; }
+    if (d->variant > WS3D_VARIANT_ASYNC) { *why = "unknown variant"; return false; }
     if (d->sponge_width > 4096) { *why = "sponge_width above 4096"; return false; }
     return true;
 }
@@ -1092,8 +1136,9 @@ ws3d_status attach_common(ws3d_ctx* c, bool has_lo, uint32_t lo_nz, bool has_hi)
     c->halo_synced = false;
     c->halo_steps = 0;
     c->lo_ghost_off = has_lo ? (uint64_t)(lo_nz + 1) * c->plane : 0;
-    if (c->halo && c->desc.variant != WS3D_VARIANT_ZSTREAM && c->desc.variant != WS3D_VARIANT_AUTO)
-        return fail(c, WS3D_EINVAL, "halo exchange needs the auto or zstream variant");
+    if (c->halo && c->desc.variant != WS3D_VARIANT_ZSTREAM &&
+        c->desc.variant != WS3D_VARIANT_AUTO && c->desc.variant != WS3D_VARIANT_ASYNC)
+        return fail(c, WS3D_EINVAL, "halo exchange needs the auto, async or zstream variant");
     return rebuild_source_ghosts(c);
 }
 

@@ -135,4 +135,49 @@ inline TmaSchedule tma_schedule(uint32_t tiles, uint32_t nz, uint32_t resident,
     return s;
 }
 
+// ---- cp.async pipeline (k_step_async): per-thread copy assignments --------
+// A stage holds the front pressure plane as 10 rows x 136 floats (x from
+// x0-4, rows y0-1 .. y0+8) = 340 float4 chunks, and p_prev / c2 as 8 x 128
+// floats = 256 float4 chunks each.  Thread t of 256 copies P chunks t and
+// t + 256 (< 340) and chunk t of p_prev and c2.  Chunks outside the grid are
+// zero-filled (no global access).
+constexpr int kAsyncTY = 8;
+constexpr int kAsyncPRow = 136;
+constexpr int kAsyncPChunks = kAsyncPRow / 4 * (kAsyncTY + 2);  // 340
+
+struct AsyncChunk {
+    bool valid;       // inside the grid: copy from global, else zero-fill
+    int64_t goff;     // in-plane global element offset (valid only)
+    int32_t soff;     // shared-memory element offset inside the tile
+};
+
+WS3D_HD AsyncChunk async_p_chunk(int c, uint32_t x0, uint32_t y0, uint32_t H, uint32_t pitch) {
+    AsyncChunk a;
+    const int r = c / (kAsyncPRow / 4), q = c - r * (kAsyncPRow / 4);
+    const int64_t y = (int64_t)y0 - 1 + r;
+    const int64_t x = (int64_t)x0 - 4 + 4 * q;
+    a.valid = y >= 0 && y < (int64_t)H && x >= 0 && x < (int64_t)pitch;
+    a.goff = a.valid ? y * (int64_t)pitch + x : 0;
+    a.soff = r * kAsyncPRow + 4 * q;
+    return a;
+}
+
+WS3D_HD AsyncChunk async_t_chunk(int c, uint32_t x0, uint32_t y0, uint32_t H, uint32_t pitch) {
+    AsyncChunk a;
+    const int r = c / 32, q = c - r * 32;
+    const int64_t y = (int64_t)y0 + r;
+    const int64_t x = (int64_t)x0 + 4 * q;
+    a.valid = y < (int64_t)H && x < (int64_t)pitch;
+    a.goff = a.valid ? y * (int64_t)pitch + x : 0;
+    a.soff = r * 128 + 4 * q;
+    return a;
+}
+
+// Item order for slabs: boundary z-chunks (the ones that wait for a
+// neighbour) after all interior chunks.
+WS3D_HD uint32_t async_chunk_of(uint32_t item, uint32_t tiles, uint32_t nchunks, bool halo) {
+    const uint32_t c = item / tiles;
+    return (halo && nchunks > 1) ? (c + 1) % nchunks : c;
+}
+
 }  // namespace ws3d

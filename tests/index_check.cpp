@@ -6,7 +6,7 @@
 // that each access lies inside its allocation, is 16-byte aligned for float4
 // accesses and does not straddle a row.  Exit code 0 = all accesses in bounds.
 //
-// Usage: index_check W H nz sm_count [TY [halo]]
+// Usage: index_check W H nz sm_count [TY [halo [kernel: 0 zstream, 1 async]]]
 #include <cstdio>
 #include <cstdlib>
 #include <vector>
@@ -115,6 +115,65 @@ static void run(uint32_t W, uint32_t H, uint32_t nz, int sms, bool halo) {
             }
 }
 
+// The cp.async kernel: replay every CTA's issue sequence (P / p_prev / c2
+// chunk copies of each stage-item) and its consumer's global loads / stores.
+static void run_async(uint32_t W, uint32_t H, uint32_t nz, int sms, bool halo) {
+    const uint32_t pitch = (W + 31u) & ~31u;
+    const int64_t P = (int64_t)H * pitch;
+    const uint32_t tiles_x = (pitch + 127) / 128;
+    const uint32_t tiles = tiles_x * ((H + kAsyncTY - 1) / kAsyncTY);
+    const uint32_t resident = (uint32_t)(sms > 0 ? sms : 1) * 3u;
+    const uint64_t field_bytes = (uint64_t)P * nz * 12u;
+    const TmaSchedule sch = tma_schedule(tiles, nz, resident, field_bytes <= (64ull << 20) ? 8u : 32u);
+    const uint32_t nchunks = (nz + sch.clen - 1) / sch.clen;
+    const Field fp{"p", true}, fpp{"pp", false}, fc2{"c2", false};
+    uint64_t covered = 0;
+    for (uint32_t b = 0; b < sch.grid; ++b) {
+        for (uint32_t item = b; item < sch.nitems; item += sch.grid) {
+            const uint32_t chunk = async_chunk_of(item, tiles, nchunks, halo);
+            const uint32_t tile = item % tiles;
+            const uint32_t zs = chunk * sch.clen, ze = zs + sch.clen < nz ? zs + sch.clen : nz;
+            covered += (uint64_t)(ze - zs);
+            const uint32_t x0 = (tile % tiles_x) * 128u, y0 = (tile / tiles_x) * kAsyncTY;
+            for (uint32_t i = 0; i <= ze - zs; ++i) {
+                for (int t = 0; t < 32 * kAsyncTY; ++t) {
+                    for (int c = t; c < kAsyncPChunks; c += 32 * kAsyncTY) {
+                        const AsyncChunk ch = async_p_chunk(c, x0, y0, H, pitch);
+                        if (ch.valid)
+                            check(fp, zs_plane((int64_t)zs + i, P) + ch.goff, 4, pitch, nz, P,
+                                  "async P copy", b, 0, 0, t, 0);
+                    }
+                    if (i > 0) {
+                        const AsyncChunk ch = async_t_chunk(t, x0, y0, H, pitch);
+                        if (ch.valid) {
+                            check(fpp, zs_plane((int64_t)zs + i - 1, P) + ch.goff, 4, pitch, nz,
+                                  P, "async pp copy", b, 0, 0, t, 0);
+                            check(fc2, zs_plane((int64_t)zs + i - 1, P) + ch.goff, 4, pitch, nz,
+                                  P, "async c2 copy", b, 0, 0, t, 0);
+                        }
+                    }
+                }
+            }
+            for (int w = 0; w < kAsyncTY; ++w)
+                for (int lane = 0; lane < 32; ++lane) {
+                    const uint32_t x = x0 + 4u * lane, y = y0 + w;
+                    if (!(x < pitch && y < H)) continue;
+                    const int64_t row = (int64_t)y * pitch + x;
+                    check(fp, zs_plane((int64_t)zs - 1, P) + row, 4, pitch, nz, P, "async pm", b,
+                          0, 0, lane, w);
+                    for (uint32_t z = zs; z < ze; ++z)
+                        check(fpp, zs_plane(z, P) + row, 4, pitch, nz, P, "async store", b, 0, 0,
+                              lane, w);
+                }
+        }
+    }
+    if (covered != (uint64_t)tiles * nz) {
+        ++g_bad;
+        fprintf(stderr, "async schedule covers %llu plane-tiles, expected %llu\n",
+                (unsigned long long)covered, (unsigned long long)tiles * nz);
+    }
+}
+
 int main(int argc, char** argv) {
     if (argc < 5) {
         fprintf(stderr, "usage: %s W H nz sm_count [TY]\n", argv[0]);
@@ -125,6 +184,11 @@ int main(int argc, char** argv) {
     const int sms = atoi(argv[4]);
     const int ty = argc > 5 ? atoi(argv[5]) : 8;
     const bool halo = argc > 6 && atoi(argv[6]) != 0;
+    if (argc > 7 && atoi(argv[7]) == 1) {
+        run_async(W, H, nz, sms, halo);
+        printf("checked %lld accesses, %d out of bounds\n", g_checked, g_bad);
+        return g_bad == 0 ? 0 : 1;
+    }
     switch (ty) {
         case 4: run<4>(W, H, nz, sms, halo); break;
         case 8: run<8>(W, H, nz, sms, halo); break;

@@ -54,7 +54,7 @@ def test_c1_slices_fixture_consistent():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "refshape", "tma"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "refshape", "tma", "async"])
 @pytest.mark.parametrize("key", CASES)
 def test_gpu_reproduces_golden(key, variant):
     wl = workload(key)

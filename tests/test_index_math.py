@@ -40,6 +40,19 @@ def test_zstream_accesses_in_bounds(checker, shape, sms, halo):
     assert r.returncode == 0, r.stderr + r.stdout
 
 
+ASYNC_SHAPES = [(13, 7, 5), (130, 9, 20), (257, 11, 6), (3, 3, 3), (160, 70, 37), (40, 36, 34),
+                (64, 64, 64), (512, 512, 64), (520, 17, 300), (256, 256, 256)]
+
+
+@pytest.mark.parametrize("shape", ASYNC_SHAPES)
+@pytest.mark.parametrize("halo", [0, 1])
+def test_async_kernel_accesses_in_bounds(checker, shape, halo):
+    W, H, nz = shape
+    r = subprocess.run([checker, str(W), str(H), str(nz), "148", "8", str(halo), "1"],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr + r.stdout
+
+
 def test_checker_catches_the_unsigned_wrap(checker, tmp_path):
     """The check must flag the bug class it exists for: a ghost-plane offset
     computed in uint32 (zb - 1 wrapping to 2^32 - 1)."""

@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 REL_L2 = 1e-5
 MAX_ABS_FRAC = 1e-4
-VARIANTS = ["auto", "zstream", "naive", "refshape", "tma"]
+VARIANTS = ["auto", "zstream", "naive", "refshape", "tma", "async"]
 
 
 def tma_ok(W, H, cells=False):
@@ -26,6 +26,8 @@ def tma_ok(W, H, cells=False):
 def skip_unless_applicable(variant, W, H, cells=False):
     if variant == "tma" and not tma_ok(W, H, cells):
         pytest.skip("TMA kernel needs W > 128, H >= 16 and the default face layout")
+    if variant == "async" and cells:
+        pytest.skip("the async kernel takes the default face layout only")
 
 
 def assert_parity(got, want, what=""):
@@ -131,7 +133,7 @@ def test_cell_types_obstacles_reflectors(variant):
     assert_parity(g.pressure_prev, ref.pressure_prev, f"cells-prev/{variant}")
 
 
-@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma", "async"])
 def test_c2_scaled_sources_and_sponge(variant):
     wl = configs.build("c2", 144, 44, 40, steps=120)
     ref = oracle.from_workload(wl)
@@ -143,7 +145,7 @@ def test_c2_scaled_sources_and_sponge(variant):
     assert_parity(g.pressure, ref.pressure, f"c2s/{variant}")
 
 
-@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma", "async"])
 def test_c3_scaled_heterogeneous(variant):
     wl = configs.build("c3", 160, 72, 64, steps=90)
     ref = oracle.from_workload(wl)
@@ -244,6 +246,9 @@ def test_tma_variant_rejects_shapes_it_cannot_take():
     b3 = GpuBackend3D(g2)            # auto takes the z-stream kernel for cell arrays
     b3.step_n(None, 2)
     b3.sync()
+    b4 = GpuBackend3D(g2, variant="async")
+    with pytest.raises(InvalidArgument):
+        b4.step_n(None, 1)
 
 
 def test_errors_are_raised_not_swallowed():
@@ -275,7 +280,7 @@ def test_full_size_c3_kernels_agree_and_match_oracle():
     bt.step_n(gt, 18)
     pt = bt.download_field()
     bt.close()
-    for v in ("zstream", "naive"):
+    for v in ("async", "zstream", "naive"):
         g, b = gpu_for(wl, v)
         b.step_n(g, 20)
         assert np.array_equal(b.download_field().view(np.uint32), pt.view(np.uint32)), v

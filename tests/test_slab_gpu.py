@@ -24,10 +24,10 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def make(wl, zb, ze, device=0, budget_ns=0):
+def make(wl, zb, ze, device=0, budget_ns=0, variant="auto"):
     whole = (zb, ze) == (0, wl.D)
     b = GpuBackend3D.create(wl.W, wl.H, wl.D, c_squared=wl.c_squared, damping=wl.damping,
-                            device=device, sponge_width=wl.sponge_width,
+                            device=device, variant=variant, sponge_width=wl.sponge_width,
                             sponge_max=wl.sponge_max, z_begin=0 if whole else zb,
                             z_end=0 if whole else ze, spin_budget_ns=budget_ns)
     p, pp = wl.initial_fields(zb, ze)
@@ -40,9 +40,11 @@ def make(wl, zb, ze, device=0, budget_ns=0):
     return b
 
 
+@pytest.mark.parametrize("variant", ["auto", "zstream"])
 @pytest.mark.parametrize("nslab", [2, 3, 4])
-@pytest.mark.parametrize("name,grid,steps", [("c3", (96, 72, 64), 50), ("c2", (48, 40, 37), 60)])
-def test_local_slab_group_equals_single_context(nslab, name, grid, steps):
+@pytest.mark.parametrize("name,grid,steps", [("c3", (96, 72, 64), 50), ("c2", (48, 40, 37), 60),
+                                             ("c3", (160, 40, 45), 30)])
+def test_local_slab_group_equals_single_context(nslab, name, grid, steps, variant):
     W, H, D = grid
     wl = configs.build(name, W, H, D, steps=steps)
     bounds = [slab_bounds(D, nslab, r) for r in range(nslab)]
@@ -52,7 +54,7 @@ def test_local_slab_group_equals_single_context(nslab, name, grid, steps):
     wav = np.concatenate([wl.wavelet, np.tile(wl.wavelet[:1], (2, 1))])
     wl.sources, wl.wavelet = src, wav
     full = make(wl, 0, D)
-    slabs = [make(wl, zb, ze) for zb, ze in bounds]
+    slabs = [make(wl, zb, ze, variant=variant) for zb, ze in bounds]
     grp = LocalSlabGroup(slabs)
     full.step_n(None, steps // 2)
     grp.step_n(steps // 2)
