@@ -250,10 +250,10 @@ def pinned(a):
 def kernel_name(variant, wl, world, mode="step"):
     if mode == "persistent":
         return "k_persistent"
-    if variant == "auto":
-        variant = "tma" if (world == 1 and wl.W > 128 and wl.H >= 16) else "zstream"
-    return {"tma": "k_step_tma", "zstream": "k_step_zstream", "naive": "k_step_naive",
-            "refshape": "k_ref_stencil+k_ref_boundary"}[variant]
+    if variant == "auto":   # mirrors launch_step's choice for the default face layout
+        variant = "tma" if (world == 1 and wl.W > 128 and wl.H >= 16) else "async"
+    return {"tma": "k_step_tma", "async": "k_step_async", "zstream": "k_step_zstream",
+            "naive": "k_step_naive", "refshape": "k_ref_stencil+k_ref_boundary"}[variant]
 
 
 def run_ours(args, wl):
@@ -390,7 +390,7 @@ def run_ours(args, wl):
 
     if args.comparators and world == 1:
         comps = {}
-        for v in ("zstream", "naive", "refshape"):
+        for v in ("async", "zstream", "naive", "refshape"):
             bc = make_backend(wl, v, local, zb, ze)
             bc.set_stream(stream.cuda_stream)
             upload_inputs(bc, wl, p0, pp0, c20)
