@@ -220,6 +220,21 @@ WS3D_API ws3d_status ws3d_field_energy_static(const float *field, uint32_t width
 /* SimulationGrid3D::max_pressure (grid3d.rs:450-455).  Synchronous. */
 WS3D_API ws3d_status ws3d_max_pressure(ws3d_ctx *ctx, float *max_abs);
 
+/* SimulationGrid3D::get_xy_slice / get_xz_slice / get_yz_slice
+ * (grid3d.rs:413-442) read straight from the device field.  axis 0: XY plane
+ * at z = index (W*H floats); 1: XZ at y = index (W*nz floats, owned planes);
+ * 2: YZ at x = index (H*nz floats, owned planes).  index is clamped to the
+ * grid like the reference.  Synchronous. */
+WS3D_API ws3d_status ws3d_get_slice(ws3d_ctx *ctx, uint32_t axis, uint32_t index, float *out);
+
+/* SimulationGrid3D::sample_pressure (grid3d.rs:373-411): trilinear samples
+ * of the current field at n positions (x, y, z triples in metres, cells of
+ * `cell_size` metres), f32 in the reference order, for the binaural
+ * microphone and other probes.  Positions must lie in the grid (and, on a
+ * z-slab, between its own planes).  Synchronous. */
+WS3D_API ws3d_status ws3d_sample_pressure(ws3d_ctx *ctx, uint32_t n, const float *pos_m,
+                                          float cell_size, float *out);
+
 /* GpuBackend3D::memory_usage (gpu_backend.rs:490-493): device bytes held. */
 WS3D_API size_t ws3d_memory_usage(const ws3d_ctx *ctx);
 

@@ -117,6 +117,8 @@ SIGNATURES = {
     "ws3d_field_energy_static": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                            _P, _P, C.c_char_p, C.c_size_t]),
     "ws3d_memory_usage": (C.c_size_t, [_CTX]),
+    "ws3d_get_slice": (C.c_int, [_CTX, C.c_uint32, C.c_uint32, _F]),
+    "ws3d_sample_pressure": (C.c_int, [_CTX, C.c_uint32, _F, C.c_float, _F]),
     "ws3d_sync": (C.c_int, [_CTX]),
     "ws3d_set_stream": (C.c_int, [_CTX, _P]),
     "ws3d_get_stream": (C.c_int, [_CTX, C.POINTER(_P)]),

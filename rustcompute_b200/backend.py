@@ -237,6 +237,33 @@ class GpuBackend3D:
             self._ctx, cx, cy, cz, np.float32(amplitude), np.float32(radius)),
             "GpuBackend3D::inject_spherical_impulse")
 
+    def get_xy_slice(self, z: int) -> np.ndarray:
+        """grid3d.rs:414-418, read from the device."""
+        out = np.empty(self.width * self.height, np.float32)
+        self._chk(self._lib.ws3d_get_slice(self._ctx, 0, int(z), _fptr(out)), "get_xy_slice")
+        return out
+
+    def get_xz_slice(self, y: int) -> np.ndarray:
+        """grid3d.rs:421-430 (owned planes), read from the device."""
+        out = np.empty(self.width * (self.z_end - self.z_begin), np.float32)
+        self._chk(self._lib.ws3d_get_slice(self._ctx, 1, int(y), _fptr(out)), "get_xz_slice")
+        return out
+
+    def get_yz_slice(self, x: int) -> np.ndarray:
+        """grid3d.rs:433-442 (owned planes), read from the device."""
+        out = np.empty(self.height * (self.z_end - self.z_begin), np.float32)
+        self._chk(self._lib.ws3d_get_slice(self._ctx, 2, int(x), _fptr(out)), "get_yz_slice")
+        return out
+
+    def sample_pressure(self, positions_m, cell_size: float) -> np.ndarray:
+        """grid3d.rs:373-411 at (n, 3) positions in metres; f32 samples."""
+        pos = np.ascontiguousarray(positions_m, dtype=np.float32).reshape(-1, 3)
+        out = np.empty(pos.shape[0], np.float32)
+        self._chk(self._lib.ws3d_sample_pressure(self._ctx, pos.shape[0], _fptr(pos),
+                                                 np.float32(cell_size), _fptr(out)),
+                  "sample_pressure")
+        return out
+
     def memory_usage(self) -> int:
         """gpu_backend.rs:490-493 (actual device bytes held)."""
         return int(self._lib.ws3d_memory_usage(self._ctx))

@@ -1127,6 +1127,73 @@ ws3d_status ws3d_step_persistent(ws3d_ctx* c, uint64_t n) {
     return WS3D_OK;
 }
 
+ws3d_status ws3d_get_slice(ws3d_ctx* c, uint32_t axis, uint32_t index, float* out) {
+    if (!c || !out) return c ? fail(c, WS3D_EINVAL, "get_slice: out is NULL") : WS3D_EINVAL;
+    DeviceGuard g(c->desc.device);
+    const float* P = owned0(c, c->buf[c->cur]);
+    cudaError_t e = cudaSuccess;
+    if (axis == 0) {  // XY at z (grid3d.rs:414-418)
+        const uint32_t z = std::min(index, c->Dg - 1);
+        if (z < c->z0 || z >= c->z0 + c->nz)
+            return fail(c, WS3D_EINVAL, "get_slice: plane z=%u is not owned by this slab", z);
+        e = cudaMemcpy2DAsync(out, c->W * 4, P + (size_t)(z - c->z0) * c->plane, c->pitch * 4,
+                              c->W * 4, c->H, cudaMemcpyDeviceToHost, c->stream);
+    } else if (axis == 1) {  // XZ at y (grid3d.rs:421-430): one row per owned plane
+        const uint32_t y = std::min(index, c->H - 1);
+        e = cudaMemcpy2DAsync(out, c->W * 4, P + (size_t)y * c->pitch, c->plane * 4, c->W * 4,
+                              c->nz, cudaMemcpyDeviceToHost, c->stream);
+    } else if (axis == 2) {  // YZ at x (grid3d.rs:433-442): one float per (z, y)
+        const uint32_t x = std::min(index, c->W - 1);
+        e = cudaMemcpy2DAsync(out, 4, P + x, c->pitch * 4, 4, (size_t)c->H * c->nz,
+                              cudaMemcpyDeviceToHost, c->stream);
+    } else {
+        return fail(c, WS3D_EINVAL, "get_slice: axis must be 0 (XY), 1 (XZ) or 2 (YZ)");
+    }
+    if (e != cudaSuccess) return cuda_fail(c, WS3D_EREADBACK, e, "get_slice copy");
+    WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EREADBACK);
+    return WS3D_OK;
+}
+
+ws3d_status ws3d_sample_pressure(ws3d_ctx* c, uint32_t n, const float* pos_m, float cell_size,
+                                 float* out) {
+    if (!c) return WS3D_EINVAL;
+    if (n == 0) return WS3D_OK;
+    if (!pos_m || !out || !(cell_size > 0.0f) || n > (1u << 24))
+        return fail(c, WS3D_EINVAL, "sample_pressure: bad arguments");
+    // Every sample's planes z0, z0+1 (clamped) must be readable by this context.
+    for (uint32_t i = 0; i < n; ++i) {
+        const float fz = pos_m[3 * i + 2] / cell_size;
+        const float flz = floorf(fz);
+        const uint32_t z0 = flz > 0.f ? (uint32_t)flz : 0u;
+        const uint32_t zz0 = std::min(z0, c->Dg - 1), z1 = std::min(z0 + 1u, c->Dg - 1);
+        const bool ok0 = zz0 >= c->z0 && zz0 < c->z0 + c->nz;
+        const bool ok1 = (z1 >= c->z0 && z1 < c->z0 + c->nz) ||
+                         (z1 == c->z0 + c->nz && c->halo && c->halo_synced && c->hi_base[0]);
+        if (!ok0 || !ok1 || !(pos_m[3 * i] >= 0.f) || !(pos_m[3 * i + 1] >= 0.f) ||
+            !(pos_m[3 * i + 2] >= 0.f) || pos_m[3 * i] / cell_size >= (float)c->W ||
+            pos_m[3 * i + 1] / cell_size >= (float)c->H || fz >= (float)c->Dg)
+            return fail(c, WS3D_EINVAL, "sample_pressure: sample %u is outside this context's cells", i);
+    }
+    DeviceGuard g(c->desc.device);
+    float* d = nullptr;
+    ws3d_status s = dalloc(c, &d, (size_t)n * 4, "samples");
+    if (s != WS3D_OK) return s;
+    cudaError_t e = cudaMemcpyAsync(d, pos_m, (size_t)n * 12, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) {
+        k_sample<<<(n + 127) / 128, 128, 0, c->stream>>>(owned0(c, c->buf[c->cur]), c->W, c->H,
+                                                         c->Dg, c->pitch, c->plane, c->z0, d,
+                                                         cell_size, n, d + 3 * (size_t)n);
+        s = check_launch(c, "k_sample");
+        if (s == WS3D_OK)
+            e = cudaMemcpyAsync(out, d + 3 * (size_t)n, (size_t)n * 4, cudaMemcpyDeviceToHost,
+                                c->stream);
+    }
+    if (s == WS3D_OK && e != cudaSuccess) s = cuda_fail(c, WS3D_EREADBACK, e, "sample copy");
+    cudaStreamSynchronize(c->stream);
+    dfree(c, d, (size_t)n * 4);
+    return s;
+}
+
 // ---------------------------------------------------------------------------
 // z-slab halo exchange.
 // ---------------------------------------------------------------------------

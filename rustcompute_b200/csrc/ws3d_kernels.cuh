@@ -167,21 +167,16 @@ __device__ __forceinline__ bool is_interior(uint32_t x, uint32_t y, uint32_t zg,
 // current plane staged in shared memory with one halo row above and below.
 // Loads for plane z+1 are issued one iteration ahead.
 // ---------------------------------------------------------------------------
-template <int TY>
-struct ZsSmem {
-    float4 srow[2][TY + 2][32];
-    float shl[2][TY], shr[2][TY];
-};
-
-// One CTA (32 x TY threads) computes planes [zb, ze) of tile (bx, by).  Ends
-// with a CTA barrier so it can be called again on the same shared memory.
+// One CTA (32 x TY threads) computes planes [zb, ze) of tile (bx, by).  Its
+// staging arrays are declared __shared__ here (one set per instantiation, so
+// the compiler addresses them as shared memory).  Ends with a CTA barrier so
+// it can be called again by a persistent loop.
 template <bool kC2F, bool kCells, int TY>
 __device__ __forceinline__ void zs_tile(const StepParams& a, uint32_t bx, uint32_t by,
-                                        uint32_t zb, uint32_t ze, ZsSmem<TY>& sm) {
+                                        uint32_t zb, uint32_t ze) {
     static_assert(TY >= 2, "the y-halo rows need two distinct warps");
-    auto& srow = sm.srow;
-    auto& shl = sm.shl;
-    auto& shr = sm.shr;
+    __shared__ float4 srow[2][TY + 2][32];
+    __shared__ float shl[2][TY], shr[2][TY];
     const int lane = threadIdx.x, w = threadIdx.y;
     const bool halo_wait = a.wait_lo != nullptr || a.wait_hi != nullptr;
 
@@ -302,12 +297,11 @@ __device__ __forceinline__ void zs_tile(const StepParams& a, uint32_t bx, uint32
 template <bool kC2F, bool kCells, int TY>
 __global__ void __launch_bounds__(32 * TY, 3)
 k_step_zstream(StepParams a, uint32_t zchunk) {
-    __shared__ ZsSmem<TY> sm;
     const bool halo_wait = a.wait_lo != nullptr || a.wait_hi != nullptr;
     uint32_t zb, ze;
     zs_chunk(zs_chunk_order(blockIdx.z, gridDim.z, halo_wait), zchunk, a.nz, &zb, &ze);
     if (zb >= ze) return;  // uniform over the CTA, before any barrier
-    zs_tile<kC2F, kCells, TY>(a, blockIdx.x, blockIdx.y, zb, ze, sm);
+    zs_tile<kC2F, kCells, TY>(a, blockIdx.x, blockIdx.y, zb, ze);
 }
 
 // ---------------------------------------------------------------------------
@@ -430,6 +424,43 @@ __global__ void k_inject_table(float* p, float* pp, const uint64_t* off, const f
     const float v = __fmul_rn(amp, factor[i]);
     p[off[i]] = __fadd_rn(p[off[i]], v);
     pp[off[i]] = __fadd_rn(pp[off[i]], __fmul_rn(v, 0.5f));
+}
+
+// ---------------------------------------------------------------------------
+// Trilinear sampling (grid3d.rs:373-411), f32 in the reference order.  pos
+// holds n (x, y, z) positions in metres; p addresses owned plane 0 of the
+// current field; samples need planes z0 and z0+1 inside [0, nz] (plane nz is
+// the upper ghost, valid on a synchronised slab).
+// ---------------------------------------------------------------------------
+__global__ void k_sample(const float* p, uint32_t W, uint32_t H, uint32_t Dg, uint32_t pitch,
+                         uint64_t plane, uint32_t z_first, const float* pos, float cell_size,
+                         uint32_t n, float* out) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float fx = __fdiv_rn(pos[3 * i + 0], cell_size);
+    const float fy = __fdiv_rn(pos[3 * i + 1], cell_size);
+    const float fz = __fdiv_rn(pos[3 * i + 2], cell_size);
+    // `as usize` saturates negative values to 0
+    const float flx = floorf(fx), fly = floorf(fy), flz = floorf(fz);
+    const uint32_t x0 = flx > 0.f ? (uint32_t)flx : 0u;
+    const uint32_t y0 = fly > 0.f ? (uint32_t)fly : 0u;
+    const uint32_t z0 = flz > 0.f ? (uint32_t)flz : 0u;
+    const uint32_t x1 = min(x0 + 1u, W - 1u), y1 = min(y0 + 1u, H - 1u), z1 = min(z0 + 1u, Dg - 1u);
+    const float tx = __fsub_rn(fx, (float)x0), ty = __fsub_rn(fy, (float)y0);
+    const float tz = __fsub_rn(fz, (float)z0);
+    auto at = [&](uint32_t x, uint32_t y, uint32_t z) {
+        return p[(int64_t)(z - z_first) * (int64_t)plane + (int64_t)y * pitch + x];
+    };
+    auto lerp = [](float a, float b, float t) {
+        return __fadd_rn(__fmul_rn(a, __fsub_rn(1.0f, t)), __fmul_rn(b, t));
+    };
+    const float c00 = lerp(at(x0, y0, z0), at(x1, y0, z0), tx);
+    const float c01 = lerp(at(x0, y0, z1), at(x1, y0, z1), tx);
+    const float c10 = lerp(at(x0, y1, z0), at(x1, y1, z0), tx);
+    const float c11 = lerp(at(x0, y1, z1), at(x1, y1, z1), tx);
+    const float c0 = lerp(c00, c10, ty);
+    const float c1 = lerp(c01, c11, ty);
+    out[i] = lerp(c0, c1, tz);
 }
 
 // ---------------------------------------------------------------------------

@@ -92,7 +92,6 @@ __device__ __forceinline__ bool grid_barrier(unsigned int* count, unsigned int* 
 
 template <bool kC2F, bool kCells, int TY>
 __global__ void __launch_bounds__(32 * TY, 3) k_persistent(PersistentArgs q) {
-    __shared__ ZsSmem<TY> sm;
     __shared__ int s_ok;
     const unsigned int nb = gridDim.x;
     const bool leader = blockIdx.x == 0 && threadIdx.x == 0 && threadIdx.y == 0;
@@ -121,7 +120,7 @@ __global__ void __launch_bounds__(32 * TY, 3) k_persistent(PersistentArgs q) {
         for (uint32_t item = blockIdx.x; item < q.nitems; item += nb) {
             const uint32_t chunk = item / q.tiles, tile = item - chunk * q.tiles;
             const uint32_t zs = chunk * q.clen, ze = min(a.nz, zs + q.clen);
-            zs_tile<kC2F, kCells, TY>(a, tile % q.tiles_x, tile / q.tiles_x, zs, ze, sm);
+            zs_tile<kC2F, kCells, TY>(a, tile % q.tiles_x, tile / q.tiles_x, zs, ze);
         }
         if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok)) return;
     }

@@ -286,3 +286,29 @@ def test_full_size_c3_kernels_agree_and_match_oracle():
         assert np.array_equal(b.download_field().view(np.uint32), pt.view(np.uint32)), v
         b.close()
     assert float(np.max(np.abs(pt))) > 0
+
+
+def test_device_slices_and_trilinear_samples():
+    """grid3d.rs:373-442 on the device: slices equal the downloaded field;
+    samples equal the reference arithmetic (host mirror, f32) bit for bit."""
+    wl = configs.build("c3", 70, 44, 36, steps=25)
+    g, b = gpu_for(wl)
+    b.step_n(g, 25)
+    b.download_pressure(g)
+    for z in (0, 17, 35, 99):
+        assert np.array_equal(b.get_xy_slice(z), g.get_xy_slice(z))
+    for y in (0, 21, 43):
+        assert np.array_equal(b.get_xz_slice(y), g.get_xz_slice(y))
+    for x in (0, 33, 69, 500):
+        assert np.array_equal(b.get_yz_slice(x), g.get_yz_slice(x))
+    cs = np.float32(0.1)
+    g.params.cell_size = float(cs)
+    rng = np.random.default_rng(3)
+    pos = (rng.uniform(0, 1, (200, 3)) * np.array([69.0, 43.0, 35.0]) * cs).astype(np.float32)
+    pos[0] = (0.0, 0.0, 0.0)
+    pos[1] = np.float32(np.array([69, 43, 35])) * cs * np.float32(0.999)
+    got = b.sample_pressure(pos, cs)
+    want = np.array([g.sample_pressure(*p) for p in pos], np.float32)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    with pytest.raises(InvalidArgument):
+        b.sample_pressure(np.array([[100.0, 0.0, 0.0]], np.float32), cs)
