@@ -100,6 +100,22 @@ k_step_async(StepParams a, AsyncSched sc) {
     cursor_run(is, sc);
     cursor_run(cs, sc);
 
+    // This thread's copy assignments for the issue cursor's current run (they
+    // depend on the tile only; per item only the plane offset changes).
+    AsyncChunk cp0{}, cp1{}, ct{};
+    bool has1 = false;
+    uint32_t table_tile = 0xffffffffu;
+    auto load_table = [&]() {
+        if (!is.have || is.tile == table_tile) return;
+        const uint32_t x0 = (is.tile % sc.tiles_x) * 128u;
+        const uint32_t y0 = (is.tile / sc.tiles_x) * kAsyncTY;
+        cp0 = async_p_chunk(t, x0, y0, a.H, a.pitch);
+        has1 = t + 32 * kAsyncTY < kAsyncPChunks;
+        if (has1) cp1 = async_p_chunk(t + 32 * kAsyncTY, x0, y0, a.H, a.pitch);
+        ct = async_t_chunk(t, x0, y0, a.H, a.pitch);
+        table_tile = is.tile;
+    };
+
     // Issue the copies of the issue cursor's stage-item into stage (j % S);
     // every thread calls this at the same point, and commits one group.
     auto issue = [&](uint64_t j) {
@@ -116,23 +132,18 @@ k_step_async(StepParams a, AsyncSched sc) {
                 }
                 __syncthreads();
             }
+            load_table();
             float* st = smem + (j % S) * L::kStageFloats;
-            const uint32_t x0 = (is.tile % sc.tiles_x) * 128u;
-            const uint32_t y0 = (is.tile / sc.tiles_x) * kAsyncTY;
             const int64_t zp = (int64_t)is.zs + is.i;  // pressure plane of this item
             const float* psrc = a.p + zs_plane(zp, P);
-            for (int c = t; c < kAsyncPChunks; c += 32 * kAsyncTY) {
-                const AsyncChunk ch = async_p_chunk(c, x0, y0, a.H, a.pitch);
-                cp_async16(st + ch.soff, ch.valid ? psrc + ch.goff : a.p, ch.valid);
-            }
+            cp_async16(st + cp0.soff, cp0.valid ? psrc + cp0.goff : a.p, cp0.valid);
+            if (has1) cp_async16(st + cp1.soff, cp1.valid ? psrc + cp1.goff : a.p, cp1.valid);
             if (is.i > 0) {
-                const int64_t z = (int64_t)is.zs + is.i - 1;
-                const AsyncChunk ch = async_t_chunk(t, x0, y0, a.H, a.pitch);
-                cp_async16(st + L::kPFloats + ch.soff,
-                           ch.valid ? a.pp + zs_plane(z, P) + ch.goff : a.pp, ch.valid);
+                const int64_t zo = zs_plane(zp - 1, P) + ct.goff;
+                cp_async16(st + L::kPFloats + ct.soff, ct.valid ? a.pp + zo : a.pp, ct.valid);
                 if (kC2F)
-                    cp_async16(st + L::kPFloats + L::kTFloats + ch.soff,
-                               ch.valid ? a.c2f + zs_plane(z, P) + ch.goff : a.c2f, ch.valid);
+                    cp_async16(st + L::kPFloats + L::kTFloats + ct.soff,
+                               ct.valid ? a.c2f + zo : a.c2f, ct.valid);
             }
             cursor_next(is, sc);
         }
@@ -147,6 +158,7 @@ k_step_async(StepParams a, AsyncSched sc) {
         const uint32_t x = x0 + 4u * lane, y = y0 + w;
         const bool act = x < a.pitch && y < a.H;
         const int64_t row = (int64_t)y * a.pitch + x;
+        const XYPre xy = make_xypre(x, y, a);
         // The issue cursor passed this run's first item (and its flag wait)
         // before we got here, so the ghost plane zs-1 may be read now.
         float4 pm = act ? ld4_plane(a.p + zs_plane((int64_t)cs.zs - 1, P) + row,
@@ -179,18 +191,9 @@ k_step_async(StepParams a, AsyncSched sc) {
             if (lane == 0) wl = Pz[(w + 1) * kAsyncPRow + 3];
             if (lane == 31) er = Pz[(w + 1) * kAsyncPRow + 4 + 128];
             if (act) {
-                const uint32_t zg = a.z0 + z;
-                const float c2x = kC2F ? vc2.x : a.c2, c2y = kC2F ? vc2.y : a.c2;
-                const float c2z = kC2F ? vc2.z : a.c2, c2w = kC2F ? vc2.w : a.c2;
-                float4 out;
-                out.x = cell_rule<false>(x + 0, y, zg, is_interior(x + 0, y, zg, a), wl, pc.y,
-                                         Sv.x, Nv.x, pm.x, pn.x, pc.x, vpp.x, c2x, 0, 0.f, a);
-                out.y = cell_rule<false>(x + 1, y, zg, is_interior(x + 1, y, zg, a), pc.x, pc.z,
-                                         Sv.y, Nv.y, pm.y, pn.y, pc.y, vpp.y, c2y, 0, 0.f, a);
-                out.z = cell_rule<false>(x + 2, y, zg, is_interior(x + 2, y, zg, a), pc.y, pc.w,
-                                         Sv.z, Nv.z, pm.z, pn.z, pc.z, vpp.z, c2z, 0, 0.f, a);
-                out.w = cell_rule<false>(x + 3, y, zg, is_interior(x + 3, y, zg, a), pc.z, er,
-                                         Sv.w, Nv.w, pm.w, pn.w, pc.w, vpp.w, c2w, 0, 0.f, a);
+                if (!kC2F) vc2 = make_float4(a.c2, a.c2, a.c2, a.c2);
+                const float4 out = cells4_default(xy, a.z0 + z, wl, er, Sv, Nv, pm, pc, pn, vpp,
+                                                  vc2, a);
                 st4(a.pp + zs_plane((int64_t)z, P) + row, out);
                 if (z == 0 && a.peer_lo) st4(a.peer_lo + row, out);
                 if (z + 1 == a.nz && a.peer_hi) st4(a.peer_hi + row, out);

@@ -149,6 +149,68 @@ __device__ __forceinline__ float cell_rule(uint32_t x, uint32_t y, uint32_t zg, 
     return v;
 }
 
+// x/y part of the default-face cell rule for one thread's float4 column,
+// computed once per (tile) run: which of the 4 cells are interior in x and y,
+// which are real cells (x < W, not row padding), and min(dx, dy) for the
+// sponge.  Per plane only the z part is added (cells4_default).
+struct XYPre {
+    uint32_t dxy[4];
+    uint32_t interior_xy;  // bit k: cell x+k interior in x and y
+    uint32_t real;         // bit k: x+k < W
+};
+
+__device__ __forceinline__ XYPre make_xypre(uint32_t x, uint32_t y, const StepParams& a) {
+    XYPre q;
+    q.interior_xy = 0;
+    q.real = 0;
+    const bool yin = y >= 1 && y + 1 < a.H;
+    const uint32_t dy = min(y, a.H - 1 - y);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t xk = x + k;
+        const bool xin = xk >= 1 && xk + 1 < a.W;
+        if (xin && yin) q.interior_xy |= 1u << k;
+        if (xk < a.W) q.real |= 1u << k;
+        q.dxy[k] = (xin && yin) ? min(min(xk, a.W - 1 - xk), dy) : 0u;
+    }
+    return q;
+}
+
+// The default-face cell rule for 4 cells at global plane zg; bit-identical to
+// cell_rule<false> (same operations in the same order).
+__device__ __forceinline__ float4 cells4_default(const XYPre& q, uint32_t zg, float wl, float er,
+                                                 float4 S, float4 N, float4 pm, float4 pc,
+                                                 float4 pn, float4 vpp, float4 c2,
+                                                 const StepParams& a) {
+    const bool zin = zg >= 1 && zg + 1 < a.Dg;
+    const uint32_t dz = min(zg, a.Dg - 1 - zg);
+    const float w[4] = {wl, pc.x, pc.y, pc.z};
+    const float e[4] = {pc.y, pc.z, pc.w, er};
+    const float s[4] = {S.x, S.y, S.z, S.w};
+    const float n[4] = {N.x, N.y, N.z, N.w};
+    const float d[4] = {pm.x, pm.y, pm.z, pm.w};
+    const float u[4] = {pn.x, pn.y, pn.z, pn.w};
+    const float c[4] = {pc.x, pc.y, pc.z, pc.w};
+    const float pv[4] = {vpp.x, vpp.y, vpp.z, vpp.w};
+    const float cc[4] = {c2.x, c2.y, c2.z, c2.w};
+    float o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float v = pv[k];
+        if (zin && ((q.interior_xy >> k) & 1u)) {
+            v = leapfrog(w[k], e[k], s[k], n[k], d[k], u[k], c[k], pv[k], cc[k], a.damping);
+            if (a.sponge_w) {
+                const uint32_t dist = min(q.dxy[k], dz);
+                if (dist < a.sponge_w) v = __fmul_rn(v, __ldg(a.sponge + dist));
+            }
+        } else if ((q.real >> k) & 1u) {
+            v = __fmul_rn(v, kFaceReflection);
+        }
+        o[k] = v;
+    }
+    return make_float4(o[0], o[1], o[2], o[3]);
+}
+
 __device__ __forceinline__ bool is_interior(uint32_t x, uint32_t y, uint32_t zg,
                                             const StepParams& a) {
     return x >= 1 && x + 1 < a.W && y >= 1 && y + 1 < a.H && zg >= 1 && zg + 1 < a.Dg;

@@ -189,6 +189,7 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
         const uint32_t x = x0 + 4u * lane, y = y0 + w;
         const bool act = x < a.pitch && y < a.H;
         const int64_t row = (int64_t)y * a.pitch + x;
+        const XYPre xy = make_xypre(x, y, a);
         float4 pm = act ? ld4(a.p + zs_plane((int64_t)r.zs - 1, P) + row) : z4;
         // prologue item
         {
@@ -224,18 +225,9 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
             if (lane == 0) wl = Pz[(w + 1) * L::kPRow + 3];
             if (lane == 31) er = Pz[(w + 1) * L::kPRow + 4 + 128];
             if (act) {
-                const uint32_t zg = a.z0 + z;
-                const float c2x = kC2F ? vc2.x : a.c2, c2y = kC2F ? vc2.y : a.c2;
-                const float c2z = kC2F ? vc2.z : a.c2, c2w = kC2F ? vc2.w : a.c2;
-                float4 out;
-                out.x = cell_rule<false>(x + 0, y, zg, is_interior(x + 0, y, zg, a), wl, pc.y,
-                                         Sv.x, Nv.x, pm.x, pn.x, pc.x, vpp.x, c2x, 0, 0.f, a);
-                out.y = cell_rule<false>(x + 1, y, zg, is_interior(x + 1, y, zg, a), pc.x, pc.z,
-                                         Sv.y, Nv.y, pm.y, pn.y, pc.y, vpp.y, c2y, 0, 0.f, a);
-                out.z = cell_rule<false>(x + 2, y, zg, is_interior(x + 2, y, zg, a), pc.y, pc.w,
-                                         Sv.z, Nv.z, pm.z, pn.z, pc.z, vpp.z, c2z, 0, 0.f, a);
-                out.w = cell_rule<false>(x + 3, y, zg, is_interior(x + 3, y, zg, a), pc.z, er,
-                                         Sv.w, Nv.w, pm.w, pn.w, pc.w, vpp.w, c2w, 0, 0.f, a);
+                if (!kC2F) vc2 = make_float4(a.c2, a.c2, a.c2, a.c2);
+                const float4 out = cells4_default(xy, a.z0 + z, wl, er, Sv, Nv, pm, pc, pn, vpp,
+                                                  vc2, a);
                 st4(a.pp + zs_plane((int64_t)z, P) + row, out);
             }
             // The previous stage (plane z: neighbours, and this row's centre) is done.
