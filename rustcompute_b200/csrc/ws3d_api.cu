@@ -310,7 +310,7 @@ ws3d_status launch_tma(ws3d_ctx* c, const StepParams& a) {
 template <bool kC2F>
 ws3d_status launch_async(ws3d_ctx* c, const StepParams& a) {
     using L = AsyncLayout<kC2F>;
-    constexpr int kThreads = 32 * kAsyncTY;
+    constexpr int kThreads = 32 * (kAsyncTY + 1);
     const int smem = L::smem_bytes();
     int& resident = c->async_grid[kC2F ? 1 : 0];
     if (resident == 0) {
