@@ -251,7 +251,7 @@ def kernel_name(variant, wl, world, mode="step"):
     if mode == "persistent":
         return "k_persistent"
     if variant == "auto":   # mirrors launch_step's choice for the default face layout
-        variant = "tma" if (world == 1 and wl.W > 128 and wl.H >= 16) else "async"
+        variant = "tma" if (world == 1 and wl.W > 128 and wl.H >= 16) else "zstream"
     return {"tma": "k_step_tma", "async": "k_step_async", "zstream": "k_step_zstream",
             "naive": "k_step_naive", "refshape": "k_ref_stencil+k_ref_boundary"}[variant]
 

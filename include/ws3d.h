@@ -65,8 +65,8 @@ typedef enum ws3d_status {
 /* Step-kernel variants (all run on the GPU; none falls back to the CPU). */
 enum {
     WS3D_VARIANT_AUTO = 0,     /* default: TMA on one GPU with the default face layout
-                                  and W > 128, H >= 16; else ASYNC with the default face
-                                  layout (z-slabs included); ZSTREAM with cell arrays */
+                                  and W > 128, H >= 16; ZSTREAM otherwise (z-slabs,
+                                  cell arrays, narrow grids) */
     WS3D_VARIANT_ZSTREAM = 1,  /* 2-D tile streaming along z, 128-bit loads, register
                                   prefetch; the kernel used for z-slabs and cell arrays */
     WS3D_VARIANT_NAIVE = 2,    /* one thread per cell, fused boundary (comparator) */

@@ -410,9 +410,10 @@ ws3d_status launch_step(ws3d_ctx* c) {
     const bool f = a.c2f != nullptr;
     const bool cells = a.types != nullptr;
     uint32_t v = c->desc.variant;
-    if (v == WS3D_VARIANT_AUTO)
-        v = tma_eligible(c) ? WS3D_VARIANT_TMA
-                            : (c->cells_default ? WS3D_VARIANT_ASYNC : WS3D_VARIANT_ZSTREAM);
+    // auto: the TMA pipeline on one GPU (0.91 of measured HBM peak at 512^3);
+    // z-slabs and cell arrays take the register-prefetch z-stream kernel
+    // (0.75), which measured ahead of the cp.async pipeline (0.73) on slabs.
+    if (v == WS3D_VARIANT_AUTO) v = tma_eligible(c) ? WS3D_VARIANT_TMA : WS3D_VARIANT_ZSTREAM;
     if (v == WS3D_VARIANT_ASYNC) {
         if (!c->cells_default)
             return fail(c, WS3D_EINVAL,

@@ -154,26 +154,32 @@ __device__ __forceinline__ float cell_rule(uint32_t x, uint32_t y, uint32_t zg, 
 // which are real cells (x < W, not row padding), and min(dx, dy) for the
 // sponge.  Per plane only the z part is added (cells4_default).
 struct XYPre {
-    uint32_t dxy[4];
-    uint32_t interior_xy;  // bit k: cell x+k interior in x and y
-    uint32_t real;         // bit k: x+k < W
+    uint32_t dxy01, dxy23;  // min(dx, dy) of cells 0..3, 16 bits each (clamped to 65535)
+    uint32_t bits;          // bit k: cell x+k interior in x and y; bit 4+k: x+k < W
 };
 
 __device__ __forceinline__ XYPre make_xypre(uint32_t x, uint32_t y, const StepParams& a) {
     XYPre q;
-    q.interior_xy = 0;
-    q.real = 0;
+    q.bits = 0;
     const bool yin = y >= 1 && y + 1 < a.H;
     const uint32_t dy = min(y, a.H - 1 - y);
+    uint32_t d[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const uint32_t xk = x + k;
         const bool xin = xk >= 1 && xk + 1 < a.W;
-        if (xin && yin) q.interior_xy |= 1u << k;
-        if (xk < a.W) q.real |= 1u << k;
-        q.dxy[k] = (xin && yin) ? min(min(xk, a.W - 1 - xk), dy) : 0u;
+        if (xin && yin) q.bits |= 1u << k;
+        if (xk < a.W) q.bits |= 16u << k;
+        d[k] = (xin && yin) ? min(min(min(xk, a.W - 1 - xk), dy), 65535u) : 0u;
     }
+    q.dxy01 = d[0] | (d[1] << 16);
+    q.dxy23 = d[2] | (d[3] << 16);
     return q;
+}
+
+__device__ __forceinline__ uint32_t xypre_dxy(const XYPre& q, int k) {
+    const uint32_t w = k < 2 ? q.dxy01 : q.dxy23;
+    return (k & 1) ? (w >> 16) : (w & 0xFFFFu);
 }
 
 // The default-face cell rule for 4 cells at global plane zg; bit-identical to
@@ -197,13 +203,14 @@ __device__ __forceinline__ float4 cells4_default(const XYPre& q, uint32_t zg, fl
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         float v = pv[k];
-        if (zin && ((q.interior_xy >> k) & 1u)) {
+        if (zin && ((q.bits >> k) & 1u)) {
             v = leapfrog(w[k], e[k], s[k], n[k], d[k], u[k], c[k], pv[k], cc[k], a.damping);
             if (a.sponge_w) {
-                const uint32_t dist = min(q.dxy[k], dz);
+                // dxy is clamped to 65535 >= any sponge width (<= 4096): same test
+                const uint32_t dist = min(xypre_dxy(q, k), dz);
                 if (dist < a.sponge_w) v = __fmul_rn(v, __ldg(a.sponge + dist));
             }
-        } else if ((q.real >> k) & 1u) {
+        } else if ((q.bits >> (4 + k)) & 1u) {
             v = __fmul_rn(v, kFaceReflection);
         }
         o[k] = v;
@@ -261,6 +268,8 @@ __device__ __forceinline__ void zs_tile(const StepParams& a, uint32_t bx, uint32
     const ZsLane L = zs_lane<TY>(bx, by, lane, w, a.W, a.H, a.pitch);
     const bool act = L.act, ylo = L.ylo, yhi = L.yhi, xl = L.xl, xr = L.xr;
     const uint32_t x = L.x, y = L.y;
+    XYPre xy{};
+    if (!kCells) xy = make_xypre(x, y, a);
     const int64_t P = (int64_t)a.plane;
     const int64_t row = L.row;
 
@@ -313,7 +322,14 @@ __device__ __forceinline__ void zs_tile(const StepParams& a, uint32_t bx, uint32
         if (lane == 0) wl = shl[cur][w];
         if (lane == 31) er = shr[cur][w];
 
-        if (act) {
+        if (act && !kCells) {
+            const int64_t o = zs_plane((int64_t)zl, P) + row;
+            const float4 c2v = kC2F ? vc2 : make_float4(a.c2, a.c2, a.c2, a.c2);
+            const float4 out = cells4_default(xy, a.z0 + zl, wl, er, S, N, pm, pc, pn, vpp, c2v, a);
+            st4(pp + o, out);
+            if (zl == 0 && a.peer_lo) st4(a.peer_lo + row, out);
+            if (zl + 1 == a.nz && a.peer_hi) st4(a.peer_hi + row, out);
+        } else if (act) {
             const uint32_t zg = a.z0 + zl;
             const int64_t o = zs_plane((int64_t)zl, P) + row;
             float4 out;
@@ -357,7 +373,7 @@ __device__ __forceinline__ void zs_tile(const StepParams& a, uint32_t bx, uint32
 }
 
 template <bool kC2F, bool kCells, int TY>
-__global__ void __launch_bounds__(32 * TY, 3)
+__global__ void __launch_bounds__(32 * TY, 4)
 k_step_zstream(StepParams a, uint32_t zchunk) {
     const bool halo_wait = a.wait_lo != nullptr || a.wait_hi != nullptr;
     uint32_t zb, ze;
