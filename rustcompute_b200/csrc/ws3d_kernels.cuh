@@ -373,7 +373,7 @@ __device__ __forceinline__ void zs_tile(const StepParams& a, uint32_t bx, uint32
 }
 
 template <bool kC2F, bool kCells, int TY>
-__global__ void __launch_bounds__(32 * TY, 4)
+__global__ void __launch_bounds__(32 * TY, 3)
 k_step_zstream(StepParams a, uint32_t zchunk) {
     const bool halo_wait = a.wait_lo != nullptr || a.wait_hi != nullptr;
     uint32_t zb, ze;
