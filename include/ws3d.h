@@ -133,6 +133,11 @@ WS3D_API ws3d_status ws3d_upload(ws3d_ctx *ctx, const float *pressure, const flo
  * field (and, when non-NULL, the previous field) to the host.  Synchronous. */
 WS3D_API ws3d_status ws3d_download(ws3d_ctx *ctx, float *pressure, float *pressure_prev);
 
+/* Set the step counter (SimulationGrid3D::step, grid3d.rs:57), which indexes
+ * the source wavelets; used to resume from a checkpoint
+ * (ringkernel-core checkpoint.rs CheckpointMetadata::current_step). */
+WS3D_API ws3d_status ws3d_set_step(ws3d_ctx *ctx, uint64_t step);
+
 /* GpuBackend3D::reset (gpu_backend.rs:404-408): upload both fields and set the
  * step counter to zero. */
 WS3D_API ws3d_status ws3d_reset(ws3d_ctx *ctx, const float *pressure, const float *pressure_prev);

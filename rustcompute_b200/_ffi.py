@@ -103,6 +103,7 @@ SIGNATURES = {
     "ws3d_upload": (C.c_int, [_CTX, _F, _F]),
     "ws3d_download": (C.c_int, [_CTX, _F, _F]),
     "ws3d_reset": (C.c_int, [_CTX, _F, _F]),
+    "ws3d_set_step": (C.c_int, [_CTX, C.c_uint64]),
     "ws3d_set_cells": (C.c_int, [_CTX, _U8, _F]),
     "ws3d_set_c2_field": (C.c_int, [_CTX, _F]),
     "ws3d_set_sources": (C.c_int, [_CTX, C.c_uint32, _U32, _F, C.c_uint64]),

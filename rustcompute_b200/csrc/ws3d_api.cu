@@ -1195,6 +1195,14 @@ ws3d_status ws3d_sample_pressure(ws3d_ctx* c, uint32_t n, const float* pos_m, fl
     return s;
 }
 
+ws3d_status ws3d_set_step(ws3d_ctx* c, uint64_t step) {
+    if (!c) return WS3D_EINVAL;
+    DeviceGuard g(c->desc.device);
+    WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
+    c->step = step;
+    return WS3D_OK;
+}
+
 // ---------------------------------------------------------------------------
 // z-slab halo exchange.
 // ---------------------------------------------------------------------------
