@@ -6,7 +6,9 @@
 
 One "step" is one FDTD time step of the whole grid.  Rank 0 prints one JSON
 line.  For N > 1 the script runs under torchrun, one rank per GPU, each rank
-owning a z-slab of the grid (strong scaling: the grid is fixed as N grows).
+owning a z-slab of the grid: by default one full-size slab of the recipe per
+GPU (weak scaling, grid W x H x D*N); --scaling strong splits the
+single-GPU grid instead.
 
 value     global cells x K / device time of the K timed steps (CUDA events on
           the launch stream, max over ranks), fields resident in HBM.
@@ -56,6 +58,10 @@ def parse():
     ap.add_argument("--mode", default="step", choices=["step", "persistent"],
                     help="step: one launch per step (library-timed); persistent: all K steps "
                          "in one cooperative launch (config 5)")
+    ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
+                    help="N > 1: weak (default) keeps one D-plane slab of the recipe per GPU "
+                         "(grid W x H x D*N, as BASELINE config 4's weak scaling); strong "
+                         "splits the single-GPU grid into N slabs")
     ap.add_argument("--grid", default=None,
                     help="WxHxD: the workload's recipe at another size (profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -206,7 +212,7 @@ def run_reference(args, wl):
     line = {
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded SplitMix64 medium and sources)",
         "config": {"workload": wl.name, "grid": [wl.W, wl.H, wl.D],
                    "heterogeneous": wl.heterogeneous, "sponge": wl.sponge_width,
@@ -345,7 +351,7 @@ def run_ours(args, wl):
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": total_ms / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded SplitMix64 medium and sources)",
         "config": {"workload": wl.name, "grid": [wl.W, wl.H, wl.D], "variant": args.variant,
                    "heterogeneous": wl.heterogeneous, "sponge": wl.sponge_width,
@@ -442,11 +448,17 @@ def main():
     os.dup2(2, 1)
     args = parse()
     from rustcompute_b200 import configs
+    _, world, _ = dist_env()
+    if args.scaling is None:
+        args.scaling = "weak" if world > 1 else "strong"
     if args.grid:
         W, H, D = (int(v) for v in args.grid.lower().split("x"))
-        wl = configs.build(args.workload, W, H, D)
     else:
-        wl = configs.build(args.workload)
+        base = configs.build(args.workload, steps=1)
+        W, H, D = base.W, base.H, base.D
+    if args.scaling == "weak" and world > 1:
+        D *= world          # one D-plane slab per GPU
+    wl = configs.build(args.workload, W, H, D)
     if args.impl == "reference":
         run_reference(args, wl)
         return
