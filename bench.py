@@ -15,8 +15,10 @@ value     global cells x K / device time of the K timed steps (CUDA events on
 e2e       the same metric for a whole job through the public API with pinned
           host buffers: upload p, p_prev, c2 and the source wavelets, K steps,
           download p -- all inside the timed region.
-roofline  algorithmic bytes (12 B/cell/step uniform, 16 B heterogeneous) per
-          step / the average step duration, against MEASURED_PEAKS.json.
+roofline  algorithmic bytes per step-kernel launch / its average duration,
+          against MEASURED_PEAKS.json: 12 B/cell (16 B with a c2 field) for a
+          one-step launch; read p, p_prev (+ c2) and write two fields, 16 B/cell
+          (20 B with c2), for a two-step launch (variant tma2).
 cpu_baseline  the C restatement of the reference CPU step (oracle/, "port")
           timed on this host's cores over a bounded sample (rank 0, N = 1).
 --impl reference  the reference's CPU implementation of the path (the same
@@ -256,9 +258,12 @@ def pinned(a):
 def kernel_name(variant, wl, world, mode="step"):
     if mode == "persistent":
         return "k_persistent"
-    if variant == "auto":   # mirrors launch_step's choice for the default face layout
-        variant = "tma" if (world == 1 and wl.W > 128 and wl.H >= 16) else "zstream"
-    return {"tma": "k_step_tma", "async": "k_step_async", "zstream": "k_step_zstream",
+    if variant == "auto":   # mirrors the library's choice for the default face layout
+        one_gpu_tma = world == 1 and wl.W > 128 and wl.H >= 16
+        two_step = one_gpu_tma and len(wl.sources) <= 32 and wl.sponge_width <= 64
+        variant = "tma2" if two_step else ("tma" if one_gpu_tma else "zstream")
+    return {"tma": "k_step_tma", "tma2": "k_step_tma2", "async": "k_step_async",
+            "zstream": "k_step_zstream",
             "naive": "k_step_naive", "refshape": "k_ref_stencil+k_ref_boundary"}[variant]
 
 
@@ -333,14 +338,24 @@ def run_ours(args, wl):
     if kernel_ms is None:   # persistent: the one launch is the whole timed region
         kernel_ms = e0.elapsed_time(e1)
     bpc = wl.bytes_per_cell_step
-    alg_bytes = bpc * local_cells
-    avg_kernel_ms = kernel_ms / args.steps
+    kname = kernel_name(args.variant, wl, world, args.mode)
+    if kname == "k_step_tma2" and args.mode == "step":
+        # K // 2 two-step launches (+ one single step for odd K)
+        n_launch = args.steps // 2 + args.steps % 2
+        total_bytes = ((args.steps // 2) * (bpc + 4) + (args.steps % 2) * bpc) * local_cells
+        alg_bytes = (bpc + 4) * local_cells
+    else:
+        n_launch = args.steps
+        total_bytes = bpc * local_cells * args.steps
+        alg_bytes = bpc * local_cells
+    avg_kernel_ms = kernel_ms / n_launch
     peaks = measured_peaks()
-    achieved = alg_bytes / (avg_kernel_ms * 1e-3) / 1e9
+    achieved = total_bytes / (kernel_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"],
                 "traffic": ncu_traffic(wl, kernel_name(args.variant, wl, world)),
                 "algorithmic_bytes_per_launch": alg_bytes,
+                "steps_per_launch": 2 if kname == "k_step_tma2" and args.mode == "step" else 1,
                 "bytes_per_cell_step": bpc,
                 "kernel_avg_ms": avg_kernel_ms,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"

@@ -64,16 +64,21 @@ typedef enum ws3d_status {
 
 /* Step-kernel variants (all run on the GPU; none falls back to the CPU). */
 enum {
-    WS3D_VARIANT_AUTO = 0,     /* default: TMA on one GPU with the default face layout
-                                  and W > 128, H >= 16; ZSTREAM otherwise (z-slabs,
-                                  cell arrays, narrow grids) */
+    WS3D_VARIANT_AUTO = 0,     /* default: on one GPU with the default face layout and
+                                  W > 128, H >= 16 the two-step kernel of TMA2 where it
+                                  applies, else single TMA steps; ZSTREAM otherwise
+                                  (z-slabs, cell arrays, narrow grids) */
     WS3D_VARIANT_ZSTREAM = 1,  /* 2-D tile streaming along z, 128-bit loads, register
                                   prefetch; the kernel used for z-slabs and cell arrays */
     WS3D_VARIANT_NAIVE = 2,    /* one thread per cell, fused boundary (comparator) */
     WS3D_VARIANT_REFSHAPE = 3, /* the reference's launch shape: 8x8x4 stencil launch
                                   plus a separate full-grid boundary launch (comparator) */
     WS3D_VARIANT_TMA = 4,      /* persistent, TMA-fed 4-stage shared-memory pipeline (one GPU) */
-    WS3D_VARIANT_ASYNC = 5     /* persistent, cp.async-fed 5-stage pipeline (one GPU or z-slabs) */
+    WS3D_VARIANT_ASYNC = 5,    /* persistent, cp.async-fed 4-stage pipeline (one GPU or z-slabs) */
+    WS3D_VARIANT_TMA2 = 6      /* two steps per launch (temporal blocking), TMA-fed, one GPU,
+                                  default face layout, <= 32 sources; allocates two more
+                                  field buffers on first use; an odd last step and contexts
+                                  it cannot serve run single TMA steps */
 };
 
 typedef struct ws3d_desc {

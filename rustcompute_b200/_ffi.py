@@ -32,6 +32,7 @@ WS3D_VARIANT_NAIVE = 2
 WS3D_VARIANT_REFSHAPE = 3
 WS3D_VARIANT_TMA = 4
 WS3D_VARIANT_ASYNC = 5
+WS3D_VARIANT_TMA2 = 6
 
 
 class ws3d_desc(C.Structure):

@@ -93,7 +93,8 @@ def _f32c(a, n: int, name: str) -> np.ndarray:
 
 VARIANTS = {"auto": _ffi.WS3D_VARIANT_AUTO, "zstream": _ffi.WS3D_VARIANT_ZSTREAM,
             "naive": _ffi.WS3D_VARIANT_NAIVE, "refshape": _ffi.WS3D_VARIANT_REFSHAPE,
-            "tma": _ffi.WS3D_VARIANT_TMA, "async": _ffi.WS3D_VARIANT_ASYNC}
+            "tma": _ffi.WS3D_VARIANT_TMA, "async": _ffi.WS3D_VARIANT_ASYNC,
+            "tma2": _ffi.WS3D_VARIANT_TMA2}
 
 
 class GpuBackend3D:

@@ -8,6 +8,7 @@
 #include "ws3d_kernels.cuh"
 #include "ws3d_async.cuh"
 #include "ws3d_persistent.cuh"
+#include "ws3d_tb.cuh"
 #include "ws3d_tma.cuh"
 
 #include <cuda_runtime.h>
@@ -30,8 +31,11 @@ struct ws3d_ctx {
     uint32_t W = 0, H = 0, Dg = 0, z0 = 0, nz = 0, pitch = 0;
     size_t plane = 0;       // H * pitch floats
     size_t slab = 0;        // (nz + 2) * plane floats (ghost below + owned + ghost above)
-    float* buf[2] = {nullptr, nullptr};
-    int cur = 0;            // buf[cur] = pressure, buf[cur ^ 1] = pressure_prev
+    // Field buffers: buf[ip] = pressure, buf[ipp] = pressure_prev.  Buffers 2
+    // and 3 are allocated on first use of the two-step (temporally blocked)
+    // pass, which writes both new fields into free buffers.
+    float* buf[4] = {nullptr, nullptr, nullptr, nullptr};
+    int ip = 0, ipp = 1;
     float* c2f = nullptr;   // slab-shaped, or nullptr
     uint8_t* types = nullptr;
     float* refl = nullptr;
@@ -39,6 +43,7 @@ struct ws3d_ctx {
     bool types_hold_default = false;  // types/refl arrays currently hold that default layout
     float* sponge = nullptr;
     uint32_t sponge_w = 0;
+    bool sponge_monotone = true;   // table non-decreasing and <= 1 (the lean cell rule's premise)
     uint64_t* src_off = nullptr;
     float* wavelet = nullptr;
     uint32_t n_src = 0;
@@ -72,12 +77,20 @@ struct ws3d_ctx {
     // optional per-launch timing of the step kernel (ws3d_step_timed)
     std::vector<cudaEvent_t> tev;
 
-    // TMA kernel: tensor maps of both field buffers in both roles and of c2
-    CUtensorMap mapP[2];   // pressure role: box 136 x (TY+2) x 1
-    CUtensorMap mapT[2];   // p_prev role:   box 128 x TY x 1
-    CUtensorMap mapC2;     // c2:            box 128 x TY x 1
+    // TMA kernels: tensor maps of every field buffer in every role and of c2
+    // (index = buffer; permuted together with buf[] after a two-step launch)
+    CUtensorMap mapP[4];   // one step, pressure role: box 136 x (TY+2) x 1
+    CUtensorMap mapT[4];   // one step, p_prev role:   box 128 x TY x 1
+    CUtensorMap mapC2;     // one step, c2:            box 128 x TY x 1
+    CUtensorMap mapA[4];   // two steps, pressure role: box 136 x (TY+4) x 1
+    CUtensorMap mapB[4];   // two steps, p_prev role:   box 136 x (TY+2) x 1
+    CUtensorMap mapC2b;    // two steps, c2:            box 136 x (TY+2) x 1
     bool tma_maps = false, tma_c2_map = false;
+    bool tb_buffers = false;   // buffers 2 and 3 allocated, their maps encoded
+    bool tb_failed = false;    // their allocation failed: run single steps
     int tma_grid[2] = {0, 0};  // co-resident CTAs without / with c2
+    int tb_grid[2] = {0, 0};
+    uint64_t tb_launches = 0;
     int async_grid[2] = {0, 0};
     uint32_t tma_min_chunk = 32;  // WS3D_TMA_MIN_CHUNK (schedule tuning), read at create
 
@@ -159,8 +172,8 @@ inline size_t owned_elems(const ws3d_ctx* c) { return (size_t)c->nz * c->plane; 
 
 StepParams make_params(const ws3d_ctx* c) {
     StepParams a{};
-    a.p = owned0(c, c->buf[c->cur]);
-    a.pp = owned0(c, c->buf[c->cur ^ 1]);
+    a.p = owned0(c, c->buf[c->ip]);
+    a.pp = owned0(c, c->buf[c->ipp]);
     a.c2f = c->c2f ? c->c2f + c->plane : nullptr;
     a.types = c->cells_default ? nullptr : c->types + c->plane;
     a.refl = c->cells_default ? nullptr : c->refl + c->plane;
@@ -176,7 +189,7 @@ StepParams make_params(const ws3d_ctx* c) {
     a.damping = c->desc.damping;
     a.sponge_w = c->sponge_w;
     if (c->halo) {
-        const int nxt = c->cur ^ 1;
+        const int nxt = c->ipp;   // the neighbour's buffer in the same role
         a.peer_lo = c->lo_base[nxt] ? c->lo_base[nxt] + c->lo_ghost_off : nullptr;
         a.peer_hi = c->hi_base[nxt];
         if (!c->host_ordered) {
@@ -260,20 +273,26 @@ bool encode_slab_map(const ws3d_ctx* c, CUtensorMap* m, const float* base, uint3
     return r == CUDA_SUCCESS;
 }
 
+bool encode_buffer_maps(ws3d_ctx* c, int b) {
+    return encode_slab_map(c, &c->mapP[b], c->buf[b], TmaLayout<kTmaTY, true>::kPRow,
+                           kTmaTY + 2) &&
+           encode_slab_map(c, &c->mapT[b], c->buf[b], 128, kTmaTY) &&
+           encode_slab_map(c, &c->mapA[b], c->buf[b], kTbRow, kTbTY + 4) &&
+           encode_slab_map(c, &c->mapB[b], c->buf[b], kTbRow, kTbTY + 2);
+}
+
 void build_tma_maps(ws3d_ctx* c) {
     c->tma_maps = false;
     if (c->pitch < 160 || c->H < 16) return;   // the kernel's boxes need W > 128, H >= 16
     bool ok = true;
-    for (int b = 0; b < 2; ++b) {
-        ok = ok && encode_slab_map(c, &c->mapP[b], c->buf[b], TmaLayout<kTmaTY, true>::kPRow,
-                                   kTmaTY + 2);
-        ok = ok && encode_slab_map(c, &c->mapT[b], c->buf[b], 128, kTmaTY);
-    }
+    for (int b = 0; b < 2; ++b) ok = ok && encode_buffer_maps(c, b);
     c->tma_maps = ok;
 }
 
 void build_tma_c2_map(ws3d_ctx* c) {
-    c->tma_c2_map = c->c2f && c->tma_maps && encode_slab_map(c, &c->mapC2, c->c2f, 128, kTmaTY);
+    c->tma_c2_map = c->c2f && c->tma_maps &&
+                    encode_slab_map(c, &c->mapC2, c->c2f, 128, kTmaTY) &&
+                    encode_slab_map(c, &c->mapC2b, c->c2f, kTbRow, kTbTY + 2);
 }
 
 bool tma_eligible(const ws3d_ctx* c) {
@@ -300,10 +319,101 @@ ws3d_status launch_tma(ws3d_ctx* c, const StepParams& a) {
     const uint32_t tiles_x = (c->pitch + 127) / 128;
     const uint32_t tiles = tiles_x * ((c->H + kTmaTY - 1) / kTmaTY);
     const TmaSchedule sch = tma_schedule(tiles, c->nz, (uint32_t)grid, c->tma_min_chunk);
-    const int P = c->cur, T = c->cur ^ 1;
+    const int P = c->ip, T = c->ipp;
     k_step_tma<kC2F, kTmaTY><<<sch.grid, kThreads, smem, c->stream>>>(
         c->mapP[P], c->mapT[T], c->mapC2, a, tiles_x, tiles, sch.clen, sch.nitems);
     return check_launch(c, "k_step_tma");
+}
+
+// ---- two steps per launch (one GPU, default face layout) --------------------
+// Buffers 2 and 3 hold no state between calls: a two-step launch writes
+// p_{t+1} and p_{t+2} into them, then buf[] and the maps are permuted so that
+// buffers 0 and 1 are again (pressure, pressure_prev).  Their ghost planes
+// stay zero (one GPU: nothing writes them).
+bool ensure_tb_buffers(ws3d_ctx* c) {
+    if (c->tb_buffers) return true;
+    if (c->tb_failed) return false;
+    for (int b = 2; b < 4; ++b) {
+        if (!c->buf[b] && dalloc(c, &c->buf[b], c->slab, "pressure (two-step)") != WS3D_OK) {
+            c->err.clear();
+            c->tb_failed = true;
+            return false;
+        }
+        if (cudaMemsetAsync(c->buf[b], 0, c->slab * sizeof(float), c->stream) != cudaSuccess ||
+            !encode_buffer_maps(c, b)) {
+            cudaGetLastError();
+            c->tb_failed = true;
+            return false;
+        }
+    }
+    c->tb_buffers = true;
+    return true;
+}
+
+bool tb_eligible(ws3d_ctx* c) {
+    return tma_eligible(c) && c->sponge_monotone && c->sponge_w <= (uint32_t)kTbSpongeMax &&
+           c->n_src <= (uint32_t)kTbMaxSrc &&
+           (!c->c2f || c->tma_c2_map) && ensure_tb_buffers(c);
+}
+
+template <bool kC2F>
+ws3d_status launch_tb(ws3d_ctx* c) {
+    using L = TbLayout<kC2F>;
+    constexpr int kThreads = 32 * (kTbTY + 3);
+    const int smem = L::smem_bytes();
+    int& grid = c->tb_grid[kC2F ? 1 : 0];
+    if (grid == 0) {
+        cudaError_t e = cudaFuncSetAttribute(k_step_tma2<kC2F>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return cuda_fail(c, WS3D_ELAUNCH, e, "cudaFuncSetAttribute(tma2)");
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step_tma2<kC2F>, kThreads,
+                                                          smem);
+        if (e != cudaSuccess || per_sm < 1)
+            return cuda_fail(c, WS3D_ELAUNCH, e, "occupancy(tma2)");
+        grid = per_sm * std::max(1, c->sm_count);
+    }
+    TbArgs g{};
+    g.a = make_params(c);
+    g.X = owned0(c, c->buf[2]);
+    g.Y = owned0(c, c->buf[3]);
+    g.src_off = c->src_off;
+    g.wavelet = c->wavelet;
+    g.n_src = c->n_src;
+    g.wl_len = c->wl_len;
+    g.step1 = c->step + 1;
+    g.tiles_x = (c->pitch + 127) / 128;
+    g.tiles = g.tiles_x * ((c->H + kTbTY - 1) / kTbTY);
+    const TmaSchedule sch = tb_schedule(g.tiles, c->nz, (uint32_t)grid);
+    g.clen = sch.clen;
+    g.nitems = sch.nitems;
+    k_step_tma2<kC2F><<<sch.grid, kThreads, smem, c->stream>>>(c->mapA[c->ip], c->mapB[c->ipp],
+                                                               c->mapC2b, g);
+    ws3d_status s = check_launch(c, "k_step_tma2");
+    if (s != WS3D_OK) return s;
+    c->tb_launches++;
+    // New roles: buffer 3 (p_{t+2}) is the pressure, buffer 2 (p_{t+1}) the
+    // previous pressure; the old pair becomes the free pair.
+    const int order[4] = {3, 2, c->ip, c->ipp};
+    float* nb[4];
+    CUtensorMap nP[4], nT[4], nA[4], nB[4];
+    for (int k = 0; k < 4; ++k) {
+        nb[k] = c->buf[order[k]];
+        nP[k] = c->mapP[order[k]];
+        nT[k] = c->mapT[order[k]];
+        nA[k] = c->mapA[order[k]];
+        nB[k] = c->mapB[order[k]];
+    }
+    for (int k = 0; k < 4; ++k) {
+        c->buf[k] = nb[k];
+        c->mapP[k] = nP[k];
+        c->mapT[k] = nT[k];
+        c->mapA[k] = nA[k];
+        c->mapB[k] = nB[k];
+    }
+    c->ip = 0;
+    c->ipp = 1;
+    return WS3D_OK;
 }
 
 // ---- cp.async kernel (one GPU or z-slabs, default face layout) -------------
@@ -365,10 +475,12 @@ ws3d_status launch_persistent(ws3d_ctx* c, uint64_t n) {
     }
     PersistentArgs q{};
     q.a = make_params(c);
+    // index 0 = pressure, 1 = pressure_prev at the start of the launch
+    const int role[2] = {c->ip, c->ipp};
     for (int b = 0; b < 2; ++b) {
-        q.buf[b] = c->buf[b];
-        q.lo_base[b] = c->lo_base[b];
-        q.hi_base[b] = c->hi_base[b];
+        q.buf[b] = c->buf[role[b]];
+        q.lo_base[b] = c->lo_base[role[b] & 1];
+        q.hi_base[b] = c->hi_base[role[b] & 1];
     }
     q.lo_ghost_off = c->lo_ghost_off;
     q.lo_flag = c->halo ? c->lo_flag : nullptr;
@@ -383,7 +495,7 @@ ws3d_status launch_persistent(ws3d_ctx* c, uint64_t n) {
     q.wl_len = c->wl_len;
     q.step0 = c->step;
     q.nsteps = n;
-    q.cur0 = (uint32_t)c->cur;
+    q.cur0 = 0;
     q.tiles_x = (c->pitch + kZsTileX - 1) / kZsTileX;
     q.tiles = q.tiles_x * ((c->H + kPersTY - 1) / kPersTY);
     // Persistent launches are latency-bound per plane (small, L2-resident
@@ -410,10 +522,12 @@ ws3d_status launch_step(ws3d_ctx* c) {
     const bool f = a.c2f != nullptr;
     const bool cells = a.types != nullptr;
     uint32_t v = c->desc.variant;
-    // auto: the TMA pipeline on one GPU (0.91 of measured HBM peak at 512^3);
+    // auto (single steps; pairs of steps go to k_step_tma2, see use_two_step):
+    // the TMA pipeline on one GPU (0.91 of measured HBM peak at 512^3);
     // z-slabs and cell arrays take the register-prefetch z-stream kernel
     // (0.75), which measured ahead of the cp.async pipeline (0.73) on slabs.
     if (v == WS3D_VARIANT_AUTO) v = tma_eligible(c) ? WS3D_VARIANT_TMA : WS3D_VARIANT_ZSTREAM;
+    if (v == WS3D_VARIANT_TMA2) v = WS3D_VARIANT_TMA;  // single steps of the two-step variant
     if (v == WS3D_VARIANT_ASYNC) {
         if (!c->cells_default)
             return fail(c, WS3D_EINVAL,
@@ -529,9 +643,9 @@ ws3d_status rebuild_source_ghosts(ws3d_ctx* c) {
 
 ws3d_status launch_sources(ws3d_ctx* c) {
     if (!c->n_src) return WS3D_OK;
-    float* glo = c->lo_base[c->cur];  // neighbours' current pressure buffers
-    float* ghi = c->hi_base[c->cur];
-    k_inject_sources<<<1, 32, 0, c->stream>>>(c->buf[c->cur], c->buf[c->cur ^ 1], c->src_off,
+    float* glo = c->lo_base[c->ip];  // neighbours' current pressure buffers
+    float* ghi = c->hi_base[c->ip];
+    k_inject_sources<<<1, 32, 0, c->stream>>>(c->buf[c->ip], c->buf[c->ipp], c->src_off,
                                               c->wavelet, c->n_src, c->wl_len, c->step,
                                               c->src_ghost, glo, ghi);
     return check_launch(c, "k_inject_sources");
@@ -552,7 +666,7 @@ ws3d_status check_device_status(ws3d_ctx* c) {
                     (st & 1u) ? "lower" : "", (st & 3u) == 3u ? " and " : "",
                     (st & 2u) ? "upper" : "", c->budget_ns * 1e-9);
     return fail(c, WS3D_ETIMEOUT,
-                "a TMA pipeline stage wait gave up (status 0x%x); the field of that step is "
+                "a pipeline stage wait gave up (status 0x%x); the field of that step is "
                 "not valid", st);
 }
 
@@ -566,7 +680,7 @@ bool desc_ok(const ws3d_desc* d, std::string* why) {
     if (!(zb == 0 && ze == 0) && !(zb < ze && ze <= d->depth)) {
         *why = "z_begin/z_end outside [0, depth]"; return false;
     }
-    if (d->variant > WS3D_VARIANT_ASYNC) { *why = "unknown variant"; return false; }
+    if (d->variant > WS3D_VARIANT_TMA2) { *why = "unknown variant"; return false; }
     if (d->sponge_width > 4096) { *why = "sponge_width above 4096"; return false; }
     return true;
 }
@@ -672,6 +786,9 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
             const double t = (double)(c->sponge_w - d) / (double)c->sponge_w;
             tab[d] = (float)(1.0 - (double)desc->sponge_max * t * t);
         }
+        for (uint32_t d = 0; d < c->sponge_w; ++d)
+            if (!(tab[d] <= 1.0f) || (d + 1 < c->sponge_w && !(tab[d] <= tab[d + 1])))
+                c->sponge_monotone = false;
         if ((s = dalloc(c, &c->sponge, c->sponge_w, "sponge")) != WS3D_OK) return bail(s);
         e = cudaMemcpy(c->sponge, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice);
         if (e != cudaSuccess) return bail(cuda_fail(c, WS3D_EMEMORY, e, "cudaMemcpy(sponge)"));
@@ -705,7 +822,7 @@ void ws3d_destroy(ws3d_ctx* c) {
         } else {
             cudaDeviceSynchronize();
         }
-        for (int b = 0; b < 2; ++b) dfree(c, c->buf[b], c->slab);
+        for (int b = 0; b < 4; ++b) dfree(c, c->buf[b], c->slab);
         dfree(c, c->c2f, c->slab);
         dfree(c, c->types, c->slab);
         dfree(c, c->refl, c->slab);
@@ -729,8 +846,8 @@ ws3d_status ws3d_upload(ws3d_ctx* c, const float* p, const float* pp) {
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     ws3d_status s = WS3D_OK;
-    if (p && (s = h2d_pitched(c, c->buf[c->cur], p)) != WS3D_OK) return s;
-    if (pp && (s = h2d_pitched(c, c->buf[c->cur ^ 1], pp)) != WS3D_OK) return s;
+    if (p && (s = h2d_pitched(c, c->buf[c->ip], p)) != WS3D_OK) return s;
+    if (pp && (s = h2d_pitched(c, c->buf[c->ipp], pp)) != WS3D_OK) return s;
     if (p) c->halo_synced = false;
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EMEMORY);
     return WS3D_OK;
@@ -739,8 +856,8 @@ ws3d_status ws3d_upload(ws3d_ctx* c, const float* p, const float* pp) {
 ws3d_status ws3d_download(ws3d_ctx* c, float* p, float* pp) {
     if (!c || !p) return c ? fail(c, WS3D_EINVAL, "download: pressure is NULL") : WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
-    ws3d_status s = d2h_pitched(c, p, c->buf[c->cur], WS3D_EMEMORY);
-    if (s == WS3D_OK && pp) s = d2h_pitched(c, pp, c->buf[c->cur ^ 1], WS3D_EMEMORY);
+    ws3d_status s = d2h_pitched(c, p, c->buf[c->ip], WS3D_EMEMORY);
+    if (s == WS3D_OK && pp) s = d2h_pitched(c, pp, c->buf[c->ipp], WS3D_EMEMORY);
     if (s != WS3D_OK) return s;
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EMEMORY);
     return WS3D_OK;
@@ -748,7 +865,8 @@ ws3d_status ws3d_download(ws3d_ctx* c, float* p, float* pp) {
 
 ws3d_status ws3d_reset(ws3d_ctx* c, const float* p, const float* pp) {
     if (!c) return WS3D_EINVAL;
-    c->cur = 0;
+    c->ip = 0;
+    c->ipp = 1;
     c->step = 0;
     c->halo_synced = false;
     DeviceGuard g(c->desc.device);
@@ -867,7 +985,19 @@ ws3d_status ws3d_set_sources(ws3d_ctx* c, uint32_t n, const uint32_t* xyz, const
 }
 
 namespace {
-ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed) {
+// Two steps per launch for the auto and tma2 variants where the context
+// allows it (one GPU, default faces, TMA maps, at most 32 sources, a
+// monotone sponge of width <= 64, memory for two more field buffers);
+// otherwise single steps.  Measured on B200 at 512^3 (c2 field, sponge):
+// 0.64 ms per two-step launch against 2 x 0.359 ms for two TMA steps.
+bool use_two_step(ws3d_ctx* c) {
+    const uint32_t v = c->desc.variant;
+    return (v == WS3D_VARIANT_TMA2 || v == WS3D_VARIANT_AUTO) && tb_eligible(c);
+}
+
+// Advances n steps; with `timed`, records an event pair around every step
+// launch and returns the number of launches in *nlaunch.
+ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed, uint64_t* nlaunch = nullptr) {
     if (c->halo && c->host_ordered)
         return fail(c, WS3D_ECOMMAND, "step: same-device slabs advance through ws3d_step_group");
     if (c->halo && !c->halo_synced)
@@ -879,9 +1009,21 @@ ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed) {
             c->tev.push_back(ev);
         }
     }
-    for (uint64_t i = 0; i < n; ++i) {
+    uint64_t ev = 0;
+    for (uint64_t i = 0; i < n;) {
         ws3d_status s = launch_sources(c);
         if (s != WS3D_OK) return s;
+        if (n - i >= 2 && use_two_step(c)) {
+            // sources of step t went into A and B above; the kernel applies
+            // those of step t+1 between its two steps
+            if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
+            s = c->c2f ? launch_tb<true>(c) : launch_tb<false>(c);
+            if (s != WS3D_OK) return s;
+            if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
+            c->step += 2;
+            i += 2;
+            continue;
+        }
         if (c->halo) {
             // Tell the neighbours that this slab finished its previous step (its
             // ghost writes into them and its reads of its own ghosts) and that the
@@ -889,13 +1031,15 @@ ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed) {
             k_halo_signal<<<1, 32, 0, c->stream>>>(c->lo_flag, c->hi_flag, c->halo_steps + 1);
             if ((s = check_launch(c, "k_halo_signal")) != WS3D_OK) return s;
         }
-        if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[2 * i], c->stream), WS3D_EDEVICE);
+        if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
         if ((s = launch_step(c)) != WS3D_OK) return s;
-        if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[2 * i + 1], c->stream), WS3D_EDEVICE);
-        c->cur ^= 1;
+        if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
+        std::swap(c->ip, c->ipp);
         c->step++;
         c->halo_steps++;
+        ++i;
     }
+    if (nlaunch) *nlaunch = ev / 2;
     return WS3D_OK;
 }
 }  // namespace
@@ -911,11 +1055,12 @@ ws3d_status ws3d_step_timed(ws3d_ctx* c, uint64_t n, double* kernel_ms) {
                                    : WS3D_EINVAL;
     if (n > (1u << 20)) return fail(c, WS3D_EINVAL, "step_timed: more than 2^20 steps");
     DeviceGuard g(c->desc.device);
-    ws3d_status s = step_impl(c, n, true);
+    uint64_t nl = 0;
+    ws3d_status s = step_impl(c, n, true, &nl);
     if (s != WS3D_OK) return s;
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_ELAUNCH);
     double tot = 0.0;
-    for (uint64_t i = 0; i < n; ++i) {
+    for (uint64_t i = 0; i < nl; ++i) {
         float ms = 0.f;
         WS3D_CUDA(c, cudaEventElapsedTime(&ms, c->tev[2 * i], c->tev[2 * i + 1]), WS3D_EDEVICE);
         tot += ms;
@@ -933,8 +1078,8 @@ ws3d_status apply_impulse_table(ws3d_ctx* c, const std::vector<uint64_t>& off,
                                 const std::vector<float>& fhi, float amp) {
     struct Part { const std::vector<uint64_t>* o; const std::vector<float>* f; float* ghost; };
     const Part parts[3] = {{&off, &fac, nullptr},
-                           {&glo, &flo, c->lo_base[c->cur] ? c->lo_base[c->cur] + c->lo_ghost_off : nullptr},
-                           {&ghi, &fhi, c->hi_base[c->cur]}};
+                           {&glo, &flo, c->lo_base[c->ip] ? c->lo_base[c->ip] + c->lo_ghost_off : nullptr},
+                           {&ghi, &fhi, c->hi_base[c->ip]}};
     ws3d_status s = WS3D_OK;
     for (int k = 0; k < 3 && s == WS3D_OK; ++k) {
         const Part& q = parts[k];
@@ -955,7 +1100,7 @@ ws3d_status apply_impulse_table(ws3d_ctx* c, const std::vector<uint64_t>& off,
             s = cuda_fail(c, WS3D_EMEMORY, e1 != cudaSuccess ? e1 : e2, "cudaMemcpyAsync(impulse)");
         } else if (k == 0) {
             k_inject_table<<<(n + 255) / 256, 256, 0, c->stream>>>(
-                c->buf[c->cur], c->buf[c->cur ^ 1], d_off, d_fac, n, amp);
+                c->buf[c->ip], c->buf[c->ipp], d_off, d_fac, n, amp);
             s = check_launch(c, "k_inject_table");
         } else {
             k_inject_ghost<<<(n + 255) / 256, 256, 0, c->stream>>>(q.ghost, d_off, d_fac, n, amp);
@@ -991,7 +1136,7 @@ ws3d_status ws3d_inject_impulse(ws3d_ctx* c, uint32_t x, uint32_t y, uint32_t z,
     const uint64_t off = (uint64_t)(z - c->z0 + 1) * c->plane + (uint64_t)y * c->pitch + x;
     const bool on_lo = z == c->z0 && c->lo_base[0], on_hi = z + 1 == c->z0 + c->nz && c->hi_base[0];
     if (!on_lo && !on_hi) {
-        k_inject_point<<<1, 32, 0, c->stream>>>(c->buf[c->cur], c->buf[c->cur ^ 1], off, amp);
+        k_inject_point<<<1, 32, 0, c->stream>>>(c->buf[c->ip], c->buf[c->ipp], off, amp);
         return check_launch(c, "k_inject_point");
     }
     // amp * 1.0f == amp exactly, so the table path adds the same values.
@@ -1032,7 +1177,7 @@ ws3d_status ws3d_energy(ws3d_ctx* c, double* out) {
     DeviceGuard g(c->desc.device);
     const uint64_t rows = (uint64_t)c->nz * c->H;
     k_energy_partials<<<c->red_blocks, kRedThreads, 0, c->stream>>>(
-        owned0(c, c->buf[c->cur]), c->W, c->pitch, rows, c->red_scratch);
+        owned0(c, c->buf[c->ip]), c->W, c->pitch, rows, c->red_scratch);
     ws3d_status s = check_launch(c, "k_energy_partials");
     if (s != WS3D_OK) return s;
     k_fold_partials<<<1, kRedThreads, 0, c->stream>>>(c->red_scratch, c->red_blocks,
@@ -1051,7 +1196,7 @@ ws3d_status ws3d_max_pressure(ws3d_ctx* c, float* out) {
     const uint64_t rows = (uint64_t)c->nz * c->H;
     float* part = reinterpret_cast<float*>(c->red_scratch);
     k_maxabs_partials<<<c->red_blocks, kRedThreads, 0, c->stream>>>(
-        owned0(c, c->buf[c->cur]), c->W, c->pitch, rows, part);
+        owned0(c, c->buf[c->ip]), c->W, c->pitch, rows, part);
     ws3d_status s = check_launch(c, "k_maxabs_partials");
     if (s != WS3D_OK) return s;
     float* res = reinterpret_cast<float*>(c->red_scratch + c->red_blocks);
@@ -1122,7 +1267,7 @@ ws3d_status ws3d_step_persistent(ws3d_ctx* c, uint64_t n) {
     else if (cells) s = launch_persistent<false, true>(c, n);
     else s = launch_persistent<false, false>(c, n);
     if (s != WS3D_OK) return s;
-    if (n & 1u) c->cur ^= 1;
+    if (n & 1u) std::swap(c->ip, c->ipp);
     c->step += n;
     c->halo_steps += n;
     return WS3D_OK;
@@ -1131,7 +1276,7 @@ ws3d_status ws3d_step_persistent(ws3d_ctx* c, uint64_t n) {
 ws3d_status ws3d_get_slice(ws3d_ctx* c, uint32_t axis, uint32_t index, float* out) {
     if (!c || !out) return c ? fail(c, WS3D_EINVAL, "get_slice: out is NULL") : WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
-    const float* P = owned0(c, c->buf[c->cur]);
+    const float* P = owned0(c, c->buf[c->ip]);
     cudaError_t e = cudaSuccess;
     if (axis == 0) {  // XY at z (grid3d.rs:414-418)
         const uint32_t z = std::min(index, c->Dg - 1);
@@ -1181,7 +1326,7 @@ ws3d_status ws3d_sample_pressure(ws3d_ctx* c, uint32_t n, const float* pos_m, fl
     if (s != WS3D_OK) return s;
     cudaError_t e = cudaMemcpyAsync(d, pos_m, (size_t)n * 12, cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess) {
-        k_sample<<<(n + 127) / 128, 128, 0, c->stream>>>(owned0(c, c->buf[c->cur]), c->W, c->H,
+        k_sample<<<(n + 127) / 128, 128, 0, c->stream>>>(owned0(c, c->buf[c->ip]), c->W, c->H,
                                                          c->Dg, c->pitch, c->plane, c->z0, d,
                                                          cell_size, n, d + 3 * (size_t)n);
         s = check_launch(c, "k_sample");
@@ -1336,13 +1481,13 @@ ws3d_status ws3d_halo_sync(ws3d_ctx* c, uint32_t phase) {
     WS3D_CUDA(c, cudaMemset(c->flags, 0, kFlagWords * sizeof(unsigned long long)), WS3D_EDEVICE);
     c->halo_steps = 0;
     const size_t bytes = c->plane * sizeof(float);
-    float* P = c->buf[c->cur];
+    float* P = c->buf[c->ip];
     if (c->lo_base[0])
-        WS3D_CUDA(c, cudaMemcpyAsync(c->lo_base[c->cur] + c->lo_ghost_off, P + c->plane, bytes,
+        WS3D_CUDA(c, cudaMemcpyAsync(c->lo_base[c->ip] + c->lo_ghost_off, P + c->plane, bytes,
                                      cudaMemcpyDefault, c->stream),
                   WS3D_EPEER);
     if (c->hi_base[0])
-        WS3D_CUDA(c, cudaMemcpyAsync(c->hi_base[c->cur], P + (size_t)c->nz * c->plane, bytes,
+        WS3D_CUDA(c, cudaMemcpyAsync(c->hi_base[c->ip], P + (size_t)c->nz * c->plane, bytes,
                                      cudaMemcpyDefault, c->stream),
                   WS3D_EPEER);
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EPEER);
@@ -1359,7 +1504,7 @@ ws3d_status ws3d_step_group(ws3d_ctx* const* ctxs, uint32_t n, uint64_t steps) {
             return fail(c, WS3D_EINVAL, "step_group: contexts must share one device and stream");
         if (c->halo && !c->halo_synced)
             return fail(c, WS3D_ECOMMAND, "step_group: fields changed since the last halo sync");
-        if (c->cur != ctxs[0]->cur || c->step != ctxs[0]->step)
+        if (c->ip != ctxs[0]->ip || c->step != ctxs[0]->step)
             return fail(c, WS3D_ECOMMAND, "step_group: contexts are at different steps");
     }
     DeviceGuard g(ctxs[0]->desc.device);
@@ -1374,7 +1519,7 @@ ws3d_status ws3d_step_group(ws3d_ctx* const* ctxs, uint32_t n, uint64_t steps) {
             if (st != WS3D_OK) return st;
         }
         for (uint32_t k = 0; k < n; ++k) {
-            ctxs[k]->cur ^= 1;
+            std::swap(ctxs[k]->ip, ctxs[k]->ipp);
             ctxs[k]->step++;
             ctxs[k]->halo_steps++;
         }

@@ -135,6 +135,38 @@ inline TmaSchedule tma_schedule(uint32_t tiles, uint32_t nz, uint32_t resident,
     return s;
 }
 
+// Schedule of the two-step kernel: every run of clen planes costs clen + 4
+// staged items (two planes of X beyond the run, two leading pressure planes),
+// so pick the chunk count that minimises rounds x (clen + 4) -- fewer, longer
+// runs unless the last round leaves too many CTAs idle.
+inline TmaSchedule tb_schedule(uint32_t tiles, uint32_t nz, uint32_t resident,
+                               uint32_t min_chunk = 16) {
+    TmaSchedule s;
+    if (resident < 1) resident = 1;
+    if (tiles < 1) tiles = 1;
+    if (min_chunk < 1) min_chunk = 1;
+    uint32_t best_k = 1;
+    uint64_t best = ~0ull;
+    const uint32_t kmax = nz / min_chunk > 1 ? nz / min_chunk : 1;
+    for (uint32_t k = 1; k <= kmax && k <= 1024; ++k) {
+        const uint32_t clen = (nz + k - 1) / k;
+        const uint32_t chunks = (nz + clen - 1) / clen;
+        const uint64_t items = (uint64_t)chunks * tiles;
+        const uint64_t rounds = (items + resident - 1) / resident;
+        const uint64_t cost = rounds * (clen + 4u);
+        if (cost < best) {
+            best = cost;
+            best_k = k;
+        }
+    }
+    s.clen = (nz + best_k - 1) / best_k;
+    if (s.clen < 1) s.clen = 1;
+    const uint32_t chunks = (nz + s.clen - 1) / s.clen;
+    s.nitems = chunks * tiles;
+    s.grid = s.nitems < resident ? s.nitems : resident;
+    return s;
+}
+
 // ---- cp.async pipeline (k_step_async): per-thread copy assignments --------
 // A stage holds the front pressure plane as 10 rows x 136 floats (x from
 // x0-4, rows y0-1 .. y0+8) = 340 float4 chunks, and p_prev / c2 as 8 x 128

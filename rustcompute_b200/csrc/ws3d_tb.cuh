@@ -1,0 +1,403 @@
+// ws3d_tb.cuh -- two FDTD steps per launch (temporal blocking, depth 2), one GPU.
+//
+// Inputs A = p_t (pressure), B = p_{t-1} (pressure_prev) and c2; outputs
+// X = p_{t+1} and Y = p_{t+2} go to two buffers that no CTA reads during the
+// launch (neighbouring tiles still read A and B), so the context rotates over
+// four field buffers.  HBM traffic per cell for two steps: read A, B, c2 once,
+// write X and Y -- 20 bytes instead of 2 x 16.
+//
+// A CTA takes (z-chunk, tile) items in chunk-major order like k_step_tma; a
+// tile is 128 x TY cells.  For a run of planes [zs, ze) the producer stages
+// item i = 0 .. (ze - zs) + 3 as
+//   A plane zs-2+i, a 136 x (TY+4) box from (x0-4, y0-2), and for i >= 2
+//   B and c2 of plane q = zs-3+i, 136 x (TY+2) boxes from (x0-4, y0-1).
+// Consumer warp w (0 .. TY+1) owns the extended row y0-1+w.  At item i >= 2 it
+// computes X(q) on its row over the 128 core columns (a float4 per lane),
+// keeping A(q-1), A(q) of its row in registers and reading A(q+1), the y
+// neighbours, B and c2 from the stage.  The two halo-row warps (0 and TY+1)
+// also compute the halo columns x0-1 and x0+128 of all TY+2 rows (ten lanes
+// each, one cell per lane) into a small shared array.  Warps 1 .. TY then
+// compute Y(q-1) on their (core) row: z neighbours X(q-2), X(q-1), X(q) from
+// registers, y neighbours from a two-slot shared ring of X planes, x halo from
+// the shared halo array, p_prev = A(q-1) from registers.  One named barrier
+// per item (consumer warps only) orders the shared X planes: slot q&1 is
+// written in item i and read in item i+1.  Cells use the lean rule of
+// ws3d_lean.cuh (packed f32x2, same bits as the one-step kernels); lanes
+// with sponge or boundary cells take a fix-up branch.  The item loop is
+// unrolled three times so that the z queues rotate by renaming registers
+// instead of moving them.
+//
+// Sources of step t are added to A and B by the host before the launch, like
+// every step.  Sources of step t+1 are applied inside: X(src) += a in source
+// order (also to the halo copies of X), and Y's p_prev A(src) += a/2 --
+// exactly what injecting between the two steps does.  So one launch equals
+// two steps bit for bit.  At most 32 sources (a shared table; lane k reads
+// source k in tiles that hold one); the host checks.
+//
+// Every mbarrier wait is bounded.  The item's barrier is a vote
+// (bar.red.or): if any consumer warp's wait gave up, all consumer warps see
+// it and leave together, so no warp is left waiting at a barrier.
+// The producer waits (bounded) for the copies it issued before it exits.  TMA
+// loads read local memory only, without multicast; used only on one GPU with
+// the default face layout.
+#pragma once
+
+#include "ws3d_lean.cuh"
+#include "ws3d_tma.cuh"
+
+namespace ws3d {
+
+constexpr int kTbTY = 8;
+constexpr int kTbStages = 5;
+constexpr int kTbRow = 136;       // floats per staged row (x0-4 .. x0+131)
+constexpr int kTbMaxSrc = 32;     // sources per launch (one per lane)
+constexpr int kTbSpongeMax = 64;  // sponge widths the kernel takes (table in shared memory)
+
+template <bool kC2F>
+struct TbLayout {
+    static constexpr int kABytes = kTbRow * (kTbTY + 4) * 4;             // 6528
+    static constexpr int kBBytes = kTbRow * (kTbTY + 2) * 4;             // 5440
+    static constexpr int kBBytesPad = (kBBytes + 127) / 128 * 128;       // 5504
+    static constexpr int kStage = kABytes + kBBytesPad * (kC2F ? 2 : 1);
+    static constexpr int kTx = kABytes + kBBytes * (kC2F ? 2 : 1);
+    static constexpr int kRingPlane = 128 * (kTbTY + 2);                 // floats
+    static constexpr int kRingBytes = 2 * kRingPlane * 4;
+    static constexpr int kHaloBytes = 256;                               // 2 x (TY+2) x 2 floats
+    static constexpr int kTabBytes = kTbSpongeMax * 4;
+    static constexpr int kSrcBytes = kTbMaxSrc * 16;
+    // stages | X ring | X halo columns | sponge table | sources | 2*S mbarriers | slack
+    static constexpr int smem_bytes() {
+        return kTbStages * kStage + kRingBytes + kHaloBytes + kTabBytes + kSrcBytes +
+               16 * kTbStages + 128;
+    }
+};
+
+struct TbArgs {
+    StepParams a;             // p = A, pp = B (owned plane 0), c2f, geometry, sponge
+    float* X;                 // owned plane 0 of the p_{t+1} output buffer
+    float* Y;                 // owned plane 0 of the p_{t+2} output buffer
+    const uint64_t* src_off;  // n_src slab offsets ((z+1)*plane + y*pitch + x)
+    const float* wavelet;     // n_src x wl_len
+    uint32_t n_src;
+    uint64_t wl_len;
+    uint64_t step1;           // global index of step t+1
+    uint32_t tiles_x, tiles, clen, nitems;
+};
+
+// Named barrier of the consumer warps that also ORs a predicate over them:
+// every consumer thread gets the same answer.
+__device__ __forceinline__ bool tb_bar_any(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred ip, op;\n setp.ne.u32 ip, %1, 0;\n"
+        " bar.red.or.pred op, 1, %2, ip;\n selp.u32 %0, 1, 0, op;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)p), "n"(32 * (kTbTY + 2))
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ float4 add_at(float4 v, int e, float d) {
+    if (e == 0) v.x = __fadd_rn(v.x, d);
+    else if (e == 1) v.y = __fadd_rn(v.y, d);
+    else if (e == 2) v.z = __fadd_rn(v.z, d);
+    else v.w = __fadd_rn(v.w, d);
+    return v;
+}
+
+template <bool kC2F>
+__global__ void __launch_bounds__(32 * (kTbTY + 3), 2)
+k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmC2, TbArgs g) {
+    using L = TbLayout<kC2F>;
+    constexpr int S = kTbStages, TY = kTbTY, R = kTbRow;
+    const StepParams& a = g.a;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+    float* ring = reinterpret_cast<float*>(smem + S * L::kStage);
+    float* hring = reinterpret_cast<float*>(smem + S * L::kStage + L::kRingBytes);  // [2][TY+2][2]
+    float* stab = reinterpret_cast<float*>(smem + S * L::kStage + L::kRingBytes + L::kHaloBytes);
+    int4* srcs = reinterpret_cast<int4*>(smem + S * L::kStage + L::kRingBytes + L::kHaloBytes +
+                                         L::kTabBytes);  // (x, y, local z, amplitude bits)
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * L::kStage + L::kRingBytes +
+                                                 L::kHaloBytes + L::kTabBytes + L::kSrcBytes);
+    uint64_t* empty = full + S;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (blockIdx.x >= g.nitems) return;  // uniform over the CTA, before any barrier
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], TY + 2);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x < kTbSpongeMax)
+        stab[threadIdx.x] = threadIdx.x < a.sponge_w ? a.sponge[threadIdx.x] : 1.0f;
+    if (threadIdx.x < g.n_src) {
+        // source k: slab offset ((z+1) * plane + y * pitch + x) -> coordinates
+        const uint32_t k = threadIdx.x;
+        const uint64_t off = g.src_off[k];
+        const uint64_t pl = off / a.plane, rem = off - pl * a.plane;
+        const uint32_t yy = (uint32_t)(rem / a.pitch);
+        const float amp = g.step1 < g.wl_len ? g.wavelet[(uint64_t)k * g.wl_len + g.step1] : 0.0f;
+        srcs[k] = make_int4((int)(rem - (uint64_t)yy * a.pitch), (int)yy, (int)pl - 1,
+                            __float_as_int(amp));
+    }
+    __syncthreads();
+
+    if (warp == TY + 2) {
+        // ------------------------------------------------------------ producer
+        if (lane != 0) return;
+        uint32_t j = 0, s = 0, round = 0;  // items issued; stage and ring round of item j
+        bool ok = true;
+        for (uint32_t item = blockIdx.x; ok && item < g.nitems; item += gridDim.x) {
+            const uint32_t chunk = item / g.tiles, tile = item - chunk * g.tiles;
+            const int zs = (int)(chunk * g.clen);
+            const int ze = (int)min(a.nz, chunk * g.clen + g.clen);
+            const int x0 = (int)((tile % g.tiles_x) * 128u), y0 = (int)((tile / g.tiles_x) * TY);
+            for (int i = 0; i <= ze - zs + 3; ++i) {
+                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char* st = smem + s * L::kStage;
+                const int zA = zs - 2 + i;  // A plane; tensor z = plane + 1
+                if (i < 2) {
+                    mbar_expect_tx(&full[s], L::kABytes);
+                    tma_load_3d(st, &tmA, x0 - 4, y0 - 2, zA + 1, &full[s]);
+                } else {
+                    const int q = zA - 1;
+                    mbar_expect_tx(&full[s], L::kTx);
+                    tma_load_3d(st, &tmA, x0 - 4, y0 - 2, zA + 1, &full[s]);
+                    tma_load_3d(st + L::kABytes, &tmB, x0 - 4, y0 - 1, q + 1, &full[s]);
+                    if (kC2F)
+                        tma_load_3d(st + L::kABytes + L::kBBytesPad, &tmC2, x0 - 4, y0 - 1, q + 1,
+                                    &full[s]);
+                }
+                ++j;
+                if (++s == S) {
+                    s = 0;
+                    ++round;
+                }
+            }
+        }
+        // A give-up leaves the consumers without items: their bounded waits end
+        // the launch.  Do not leave while copies this thread issued may land.
+        if (!ok) atomicOr(a.status, 4u);
+        for (uint32_t q = j > (uint32_t)S ? j - S : 0u; q < j; ++q)
+            mbar_wait(&full[q % S], (q / S) & 1u);
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    const int w = warp;  // extended row y0 - 1 + w
+    const bool do_y = w >= 1 && w <= TY;
+    const int64_t P = (int64_t)a.plane;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const f2 damp = pk(a.damping, a.damping);
+    const int ecol = lane == 0 ? 3 : 132;  // x halo of lanes 0 / 31 (x0-1, x0+128)
+    // halo-column cells: warps 0 and TY+1, lanes 0..TY+1, one (row, side) each
+    const bool hwarp = w == 0 || w == TY + 1;
+    const bool hlane = hwarp && lane < TY + 2;
+    const int hrow = hlane ? (w == 0 ? 0 : (TY + 2) / 2) + (lane >> 1) : 0;
+    const int hside = lane & 1;
+    const int arow = (w + 1) * R;                        // this row in the A box
+    const int hr = (hrow + 1) * R + (hside ? 132 : 3);  // the halo cell in the A box
+    const bool has_src = (uint32_t)lane < g.n_src;       // lane k reads source k
+    // plane sponge factor (planes 0 <= zg < Dg)
+    auto fz_of = [&](uint32_t zg) -> float {
+        const uint32_t dz = min(zg, a.Dg - 1 - zg);
+        return dz < a.sponge_w ? stab[dz] : 1.0f;
+    };
+
+    uint32_t s = 0, ph = 0;  // stage and full-barrier parity of the current item
+    for (uint32_t item = blockIdx.x; item < g.nitems; item += gridDim.x) {
+        const uint32_t chunk = item / g.tiles, tile = item - chunk * g.tiles;
+        const int zs = (int)(chunk * g.clen);
+        const int ze = (int)min(a.nz, chunk * g.clen + g.clen);
+        const uint32_t x0 = (tile % g.tiles_x) * 128u, y0 = (tile / g.tiles_x) * TY;
+        const uint32_t x = x0 + 4u * lane;
+        const uint32_t y = y0 + (uint32_t)w - 1u;  // wraps for y0 = 0, w = 0: not a grid row
+        const LeanRow lr = make_lean_row(x, y, a);
+        const float fxmin = fminf(fminf(lr.fx[0], lr.fx[1]), fminf(lr.fx[2], lr.fx[3]));
+        const bool act = do_y && x < a.pitch && y < a.H;
+        const int64_t row = (int64_t)y * a.pitch + x;  // + q * plane
+        // halo cell of this lane (hlane only); x / y may wrap: not interior.
+        // hf < 0 marks a halo cell that is not interior in x and y.
+        float hf = -1.0f;
+        {
+            const uint32_t hx = hside ? x0 + 128u : x0 - 1u;
+            const uint32_t hy = y0 + (uint32_t)hrow - 1u;
+            if (lean_in(hx, a.W) && lean_in(hy, a.H))
+                hf = sponge_f(min(min(hx, a.W - 1 - hx), min(hy, a.H - 1 - hy)), a);
+        }
+        // any source inside the tile's extended region (core + halo)?
+        bool tile_src = false;
+        if (g.n_src) {
+            const int4 sc = has_src ? srcs[lane] : make_int4(-1000, -1000, 0, 0);
+            tile_src = __any_sync(0xffffffffu, sc.x + 1 >= (int)x0 && sc.x <= (int)x0 + 128 &&
+                                                   sc.y + 1 >= (int)y0 && sc.y <= (int)y0 + TY);
+        }
+        const int n = ze - zs;
+
+        // Ends an item: release the previous item's stage (this warp no longer
+        // reads it), barrier with abort vote, next stage.  True = abort.
+        auto end_item = [&](bool ok, bool release) -> bool {
+            __syncwarp();
+            if (release && lane == 0) mbar_arrive(&empty[s == 0 ? S - 1 : s - 1]);
+            const bool abort = tb_bar_any(!ok);
+            if (++s == S) {
+                s = 0;
+                ph ^= 1u;
+            }
+            return abort;
+        };
+        // Items 0, 1: A planes zs-2, zs-1 of this row (and of the halo cell).
+        auto prologue = [&](float4& av, float& hv, bool release) -> bool {
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph));
+            if (ok) {
+                const float* Ac = reinterpret_cast<const float*>(smem + s * L::kStage);
+                av = *reinterpret_cast<const float4*>(Ac + arow + 4 + 4 * lane);
+                hv = hlane ? Ac[hr] : 0.f;
+            }
+            return end_item(ok, release);
+        };
+        // Item i >= 2: X(q), q = zs-3+i, from A(q-1) = a_m, A(q) = a_c and the
+        // staged A(q+1) (kept in a_p); then Y(q-1) from X(q-2) = x_m,
+        // X(q-1) = x_c and X(q) (kept in x_n).  Halo lanes: h_m, h_c, h_p.
+        auto body = [&](int i, float4& a_m, float4& a_c, float4& a_p, float4& x_m, float4& x_c,
+                        float4& x_n, float& h_m, float& h_c, float& h_p) -> bool {
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph));
+            if (ok) {
+                const int q = zs - 3 + i;
+                const uint32_t sp = s == 0 ? S - 1 : s - 1;
+                const float* Ac = reinterpret_cast<const float*>(smem + s * L::kStage);
+                const float* Ap = reinterpret_cast<const float*>(smem + sp * L::kStage);
+                const float* Bq = Ac + L::kABytes / 4;
+                const float* Cq = Ac + (L::kABytes + L::kBBytesPad) / 4;
+                a_p = *reinterpret_cast<const float4*>(Ac + arow + 4 + 4 * lane);
+                h_p = hlane ? Ac[hr] : 0.f;
+                x_n = z4;
+                if (q >= 0 && q < (int)a.nz) {
+                    // ---- X(q) on extended row w
+                    const uint32_t zg = a.z0 + (uint32_t)q;
+                    const bool zin = zg >= 1 && zg + 1 < a.Dg;
+                    const float fz = fz_of(zg);
+                    const float4 sv = *reinterpret_cast<const float4*>(Ap + arow - R + 4 + 4 * lane);
+                    const float4 nv = *reinterpret_cast<const float4*>(Ap + arow + R + 4 + 4 * lane);
+                    const float4 bv = *reinterpret_cast<const float4*>(Bq + w * R + 4 + 4 * lane);
+                    const float4 cq = kC2F ? *reinterpret_cast<const float4*>(Cq + w * R + 4 + 4 * lane)
+                                           : make_float4(a.c2, a.c2, a.c2, a.c2);
+                    const float ed = Ap[arow + ecol];
+                    float wl = __shfl_up_sync(0xffffffffu, a_c.w, 1);
+                    float er = __shfl_down_sync(0xffffffffu, a_c.x, 1);
+                    if (lane == 0) wl = ed;
+                    if (lane == 31) er = ed;
+                    float4 xv = cells4_fast(wl, er, sv, nv, a_m, a_c, a_p, bv, cq, damp);
+                    const uint32_t m = zin ? lr.bits : 0u;
+                    const bool sp_lane = fz < 1.0f || fxmin < 1.0f;
+                    if (sp_lane || m != 0xFu) xv = cells4_fixup(xv, sp_lane, lr.fx, fz, m, bv);
+                    if (tile_src) {  // sources of step t+1: X += a, in source order
+                        const int4 sc = has_src ? srcs[lane] : make_int4(0, -1, -1, 0);
+                        unsigned mk = __ballot_sync(0xffffffffu, sc.z == q && sc.y == (int)y);
+                        while (mk) {
+                            const int k = __ffs(mk) - 1;
+                            mk &= mk - 1;
+                            const int dx = __shfl_sync(0xffffffffu, sc.x, k) - (int)x0;
+                            const float amp = __int_as_float(__shfl_sync(0xffffffffu, sc.w, k));
+                            if (dx >= 0 && dx < 128 && lane == (dx >> 2)) xv = add_at(xv, dx & 3, amp);
+                        }
+                    }
+                    *reinterpret_cast<float4*>(ring + (q & 1) * L::kRingPlane + w * 128 + 4 * lane) = xv;
+                    if (act && q >= zs && q < ze) st4(g.X + zs_plane(q, P) + row, xv);
+                    x_n = xv;
+                    if (hwarp) {
+                        // ---- X(q) at the halo columns x0-1, x0+128 of rows 0 .. TY+1
+                        float xh = 0.f;
+                        if (hlane) {
+                            const int br = hr - R;  // the halo cell in the B / c2 boxes
+                            xh = cell1_lean(zin && hf >= 0.0f, fminf(hf, fz), Ap[hr - 1], Ap[hr + 1],
+                                            Ap[hr - R], Ap[hr + R], h_m, h_p, h_c, Bq[br],
+                                            kC2F ? Cq[br] : a.c2, a.damping);
+                        }
+                        if (tile_src) {
+                            const int hx = (int)(hside ? x0 + 128u : x0 - 1u);
+                            const int hy = (int)(y0 + (uint32_t)hrow - 1u);
+                            const int4 sc = has_src ? srcs[lane] : make_int4(0, -1, -1, 0);
+                            unsigned mk = __ballot_sync(0xffffffffu, sc.z == q);
+                            while (mk) {
+                                const int k = __ffs(mk) - 1;
+                                mk &= mk - 1;
+                                const int kx = __shfl_sync(0xffffffffu, sc.x, k);
+                                const int ky = __shfl_sync(0xffffffffu, sc.y, k);
+                                const float amp = __int_as_float(__shfl_sync(0xffffffffu, sc.w, k));
+                                if (hlane && kx == hx && ky == hy) xh = __fadd_rn(xh, amp);
+                            }
+                        }
+                        if (hlane) hring[((q & 1) * (TY + 2) + hrow) * 2 + hside] = xh;
+                    }
+                }
+                // ---- Y(q-1) on core row w (shared X(q-1) written last item)
+                const int qy = q - 1;
+                if (do_y && qy >= zs && qy < ze) {
+                    const float* Xr = ring + (qy & 1) * L::kRingPlane;
+                    const float4 sv = *reinterpret_cast<const float4*>(Xr + (w - 1) * 128 + 4 * lane);
+                    const float4 nv = *reinterpret_cast<const float4*>(Xr + (w + 1) * 128 + 4 * lane);
+                    const float* Cp = reinterpret_cast<const float*>(smem + sp * L::kStage) +
+                                      (L::kABytes + L::kBBytesPad) / 4;
+                    const float4 c2y = kC2F ? *reinterpret_cast<const float4*>(Cp + w * R + 4 + 4 * lane)
+                                            : make_float4(a.c2, a.c2, a.c2, a.c2);
+                    const float eh = hring[((qy & 1) * (TY + 2) + w) * 2 + (lane == 31 ? 1 : 0)];
+                    float wl = __shfl_up_sync(0xffffffffu, x_c.w, 1);
+                    float er = __shfl_down_sync(0xffffffffu, x_c.x, 1);
+                    if (lane == 0) wl = eh;
+                    if (lane == 31) er = eh;
+                    float4 pv = a_m;  // A(q-1)
+                    if (tile_src) {  // sources of step t+1: p_prev += a/2
+                        const int4 sc = has_src ? srcs[lane] : make_int4(0, -1, -1, 0);
+                        unsigned mk = __ballot_sync(0xffffffffu, sc.z == qy && sc.y == (int)y);
+                        while (mk) {
+                            const int k = __ffs(mk) - 1;
+                            mk &= mk - 1;
+                            const int dx = __shfl_sync(0xffffffffu, sc.x, k) - (int)x0;
+                            const float amp = __int_as_float(__shfl_sync(0xffffffffu, sc.w, k));
+                            if (dx >= 0 && dx < 128 && lane == (dx >> 2))
+                                pv = add_at(pv, dx & 3, __fmul_rn(amp, 0.5f));
+                        }
+                    }
+                    const uint32_t zgy = a.z0 + (uint32_t)qy;
+                    const float fzy = fz_of(zgy);
+                    float4 yv = cells4_fast(wl, er, sv, nv, x_m, x_c, x_n, pv, c2y, damp);
+                    const uint32_t my = (zgy >= 1 && zgy + 1 < a.Dg) ? lr.bits : 0u;
+                    const bool spy = fzy < 1.0f || fxmin < 1.0f;
+                    if (spy || my != 0xFu) yv = cells4_fixup(yv, spy, lr.fx, fzy, my, pv);
+                    if (act) st4(g.Y + zs_plane(qy, P) + row, yv);
+                }
+            }
+            return end_item(ok, true);
+        };
+
+        float4 am = z4, ac = z4, ap = z4, xm = z4, xc = z4, xn = z4;
+        float hm = 0.f, hc = 0.f, hp = 0.f;
+        bool abort = prologue(am, hm, false) || prologue(ac, hc, true);
+        int i = 2;
+        const int last = n + 3;
+        for (; !abort && i + 2 <= last; i += 3) {
+            abort = body(i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
+                    body(i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
+                    body(i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
+        }
+        if (!abort && i <= last) abort = body(i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
+        if (!abort && i <= last) abort = body(i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
+        if (abort) {
+            if (threadIdx.x == 0) atomicOr(a.status, 4u);
+            return;  // every consumer thread saw the same vote
+        }
+        // the run's last stage
+        if (lane == 0) mbar_arrive(&empty[s == 0 ? S - 1 : s - 1]);
+    }
+}
+
+}  // namespace ws3d

@@ -54,11 +54,11 @@ def test_c1_slices_fixture_consistent():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "refshape", "tma", "async"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "refshape", "tma", "async", "tma2"])
 @pytest.mark.parametrize("key", CASES)
 def test_gpu_reproduces_golden(key, variant):
     wl = workload(key)
-    if variant == "tma" and not (wl.W > 128 and wl.H >= 16):
+    if variant in ("tma", "tma2") and not (wl.W > 128 and wl.H >= 16):
         pytest.skip("TMA kernel needs W > 128 and H >= 16")
     g = SimulationGrid3D(wl.W, wl.H, wl.D,
                          AcousticParams3D(c_squared=wl.c_squared, simple_damping=wl.damping))

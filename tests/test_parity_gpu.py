@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 REL_L2 = 1e-5
 MAX_ABS_FRAC = 1e-4
-VARIANTS = ["auto", "zstream", "naive", "refshape", "tma", "async"]
+VARIANTS = ["auto", "zstream", "naive", "refshape", "tma", "async", "tma2"]
 
 
 def tma_ok(W, H, cells=False):
@@ -24,7 +24,7 @@ def tma_ok(W, H, cells=False):
 
 
 def skip_unless_applicable(variant, W, H, cells=False):
-    if variant == "tma" and not tma_ok(W, H, cells):
+    if variant in ("tma", "tma2") and not tma_ok(W, H, cells):
         pytest.skip("TMA kernel needs W > 128, H >= 16 and the default face layout")
     if variant == "async" and cells:
         pytest.skip("the async kernel takes the default face layout only")
@@ -133,7 +133,7 @@ def test_cell_types_obstacles_reflectors(variant):
     assert_parity(g.pressure_prev, ref.pressure_prev, f"cells-prev/{variant}")
 
 
-@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma", "async"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma", "async", "tma2"])
 def test_c2_scaled_sources_and_sponge(variant):
     wl = configs.build("c2", 144, 44, 40, steps=120)
     ref = oracle.from_workload(wl)
@@ -145,7 +145,7 @@ def test_c2_scaled_sources_and_sponge(variant):
     assert_parity(g.pressure, ref.pressure, f"c2s/{variant}")
 
 
-@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma", "async"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "naive", "tma", "async", "tma2"])
 def test_c3_scaled_heterogeneous(variant):
     wl = configs.build("c3", 160, 72, 64, steps=90)
     ref = oracle.from_workload(wl)
