@@ -163,13 +163,20 @@ def cpu_sample_run(wl, target_s: float = 12.0, nthreads: int = 0):
     import oracle
     nthreads = nthreads or host_threads()
     g = oracle.from_workload(wl)
-    g.run(1, nthreads)                     # warm-up (first touch)
-    t0 = time.perf_counter()
-    g.run(1, nthreads)                     # calibration
-    t1 = time.perf_counter() - t0
+    # Step counts stay even: an odd count makes the oracle copy the fields
+    # back into the caller's arrays, which would be timed with the steps.
+    g.run(2, nthreads)                     # warm-up (first touch, thread pool)
+    # calibration: steady-state seconds per step over at least ~1 s of steps
+    n, t0 = 0, time.perf_counter()
+    while True:
+        g.run(2, nthreads)
+        n += 2
+        t1 = (time.perf_counter() - t0) / n
+        if n * t1 >= 1.0 or t1 * 3 > target_s:
+            break
     if t1 * 3 <= target_s:
-        steps = max(2, int(target_s / max(t1, 1e-6)))
-        sample = f"{steps} full {wl.W}x{wl.H}x{wl.D} steps after 2 untimed steps"
+        steps = max(2, int(target_s / max(t1, 1e-6)) // 2 * 2)
+        sample = f"{steps} full {wl.W}x{wl.H}x{wl.D} steps after {2 + n} untimed steps"
         cells = wl.cells
     else:
         planes = max(8, min(wl.D, int(wl.D * target_s / 3 / t1)))
@@ -193,11 +200,12 @@ def run_reference(args, wl):
         return
     nthreads = host_threads()
     # One timed step = one full-grid step when affordable, else a z-slab sample.
-    probe = wl.scaled(wl.W, wl.H, min(wl.D, 34), steps=2)
+    probe = wl.scaled(wl.W, wl.H, min(wl.D, 34), steps=4)
     g = oracle.from_workload(probe)
+    g.run(2, nthreads)                     # warm-up; even counts: no copy-back
     t0 = time.perf_counter()
-    g.run(1, nthreads)
-    rate = probe.cells / max(time.perf_counter() - t0, 1e-9)
+    g.run(2, nthreads)
+    rate = 2 * probe.cells / max(time.perf_counter() - t0, 1e-9)
     budget = 150.0 / max(args.steps + args.warmup, 1)
     if wl.cells / rate <= budget:
         sample, desc = wl, f"full {wl.W}x{wl.H}x{wl.D} grid per step"

@@ -55,6 +55,8 @@ def lib() -> C.CDLL:
         L.ws3o_step_parallel.argtypes = [u32, u32, u32, vp, vp, vp, vp, C.POINTER(_Params), C.c_int]
         L.ws3o_run.argtypes = [u32, u32, u32, vp, vp, vp, vp, C.POINTER(_Params), C.c_uint64,
                                C.c_uint64, u32, vp, vp, C.c_uint64, C.c_int]
+        L.ws3o_run_swap.argtypes = L.ws3o_run.argtypes
+        L.ws3o_run_swap.restype = C.c_int
         L.ws3o_total_energy_f32.argtypes = [vp, C.c_uint64]
         L.ws3o_total_energy_f32.restype = f32
         L.ws3o_total_energy_f64.argtypes = [vp, C.c_uint64]
@@ -142,10 +144,13 @@ class OracleGrid(SimulationGrid3D):
         prm = self._params()
         n_src = len(self.src_idx)
         wl_len = self.wavelet.shape[1] if n_src else 0
-        lib().ws3o_run(self.width, self.height, self.depth, _ptr(self.pressure),
-                       _ptr(self.pressure_prev), t, r, C.byref(prm), self.step, nsteps,
-                       n_src, _ptr(self.src_idx) if n_src else None,
-                       _ptr(self.wavelet) if n_src else None, wl_len, int(nthreads))
+        swapped = lib().ws3o_run_swap(self.width, self.height, self.depth, _ptr(self.pressure),
+                                      _ptr(self.pressure_prev), t, r, C.byref(prm), self.step,
+                                      nsteps, n_src, _ptr(self.src_idx) if n_src else None,
+                                      _ptr(self.wavelet) if n_src else None, wl_len,
+                                      int(nthreads))
+        if swapped:
+            self.pressure, self.pressure_prev = self.pressure_prev, self.pressure
         self.advance_clock(nsteps)
 
     def inject_spherical_impulse(self, cx, cy, cz, amplitude, radius):

@@ -231,6 +231,30 @@ void ws3o_step_parallel(uint32_t W, uint32_t H, uint32_t D, const float *p, floa
  * (inject_impulse semantic, grid3d.rs:146-152, driven per step the way
  * bin/wavesim3d.rs:80-100 drives it).  nthreads <= 1 selects step_sequential.
  */
+/* ws3o_run without the copy-back: returns 1 when the current field ends in
+ * pp (odd nsteps), 0 when it ends in p; the caller swaps its references, as
+ * the reference swaps its buffers (grid3d.rs:264). */
+int ws3o_run_swap(uint32_t W, uint32_t H, uint32_t D, float *p, float *pp,
+                  const uint8_t *types, const float *refl, const ws3o_params *prm,
+                  uint64_t step0, uint64_t nsteps, uint32_t n_src, const uint64_t *src_idx,
+                  const float *wavelet, uint64_t wl_len, int nthreads) {
+    float *cur = p, *prev = pp;
+    for (uint64_t s = 0; s < nsteps; ++s) {
+        uint64_t gs = step0 + s;
+        for (uint32_t k = 0; k < n_src; ++k) {
+            float a = gs < wl_len ? wavelet[(size_t)k * wl_len + gs] : 0.0f;
+            cur[src_idx[k]] += a;
+            prev[src_idx[k]] += a * 0.5f;
+        }
+        if (nthreads > 1)
+            ws3o_step_parallel(W, H, D, cur, prev, types, refl, prm, nthreads);
+        else
+            ws3o_step_sequential(W, H, D, cur, prev, types, refl, prm);
+        float *t = cur; cur = prev; prev = t;
+    }
+    return cur != p;
+}
+
 void ws3o_run(uint32_t W, uint32_t H, uint32_t D, float *p, float *pp,
               const uint8_t *types, const float *refl, const ws3o_params *prm,
               uint64_t step0, uint64_t nsteps, uint32_t n_src, const uint64_t *src_idx,
