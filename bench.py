@@ -267,9 +267,9 @@ def kernel_name(variant, wl, world, mode="step"):
     if mode == "persistent":
         return "k_persistent"
     if variant == "auto":   # mirrors the library's choice for the default face layout
-        one_gpu_tma = world == 1 and wl.W > 128 and wl.H >= 16
-        two_step = one_gpu_tma and len(wl.sources) <= 32 and wl.sponge_width <= 64
-        variant = "tma2" if two_step else ("tma" if one_gpu_tma else "zstream")
+        tma_ok = wl.W > 128 and wl.H >= 16
+        two_step = world == 1 and tma_ok and len(wl.sources) <= 32 and wl.sponge_width <= 64
+        variant = "tma2" if two_step else ("tma" if tma_ok else "zstream")
     return {"tma": "k_step_tma", "tma2": "k_step_tma2", "async": "k_step_async",
             "zstream": "k_step_zstream",
             "naive": "k_step_naive", "refshape": "k_ref_stencil+k_ref_boundary"}[variant]

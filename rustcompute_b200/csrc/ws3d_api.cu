@@ -295,8 +295,10 @@ void build_tma_c2_map(ws3d_ctx* c) {
                     encode_slab_map(c, &c->mapC2b, c->c2f, kTbRow, kTbTY + 2);
 }
 
+// The TMA kernel serves one GPU and z-slabs (its loads read only this GPU's
+// memory; the ghost planes are local buffers written by the neighbours).
 bool tma_eligible(const ws3d_ctx* c) {
-    return !c->halo && c->cells_default && c->tma_maps && (!c->c2f || c->tma_c2_map);
+    return c->cells_default && c->tma_maps && (!c->c2f || c->tma_c2_map);
 }
 
 template <bool kC2F>
@@ -318,7 +320,10 @@ ws3d_status launch_tma(ws3d_ctx* c, const StepParams& a) {
     }
     const uint32_t tiles_x = (c->pitch + 127) / 128;
     const uint32_t tiles = tiles_x * ((c->H + kTmaTY - 1) / kTmaTY);
-    const TmaSchedule sch = tma_schedule(tiles, c->nz, (uint32_t)grid, c->tma_min_chunk);
+    // slabs: shorter chunks, so that interior chunks overlap the exchange
+    const TmaSchedule sch =
+        tma_schedule(tiles, c->nz, (uint32_t)grid, c->halo ? std::min(16u, c->tma_min_chunk)
+                                                           : c->tma_min_chunk);
     const int P = c->ip, T = c->ipp;
     k_step_tma<kC2F, kTmaTY><<<sch.grid, kThreads, smem, c->stream>>>(
         c->mapP[P], c->mapT[T], c->mapC2, a, tiles_x, tiles, sch.clen, sch.nitems);
@@ -351,7 +356,8 @@ bool ensure_tb_buffers(ws3d_ctx* c) {
 }
 
 bool tb_eligible(ws3d_ctx* c) {
-    return tma_eligible(c) && c->sponge_monotone && c->sponge_w <= (uint32_t)kTbSpongeMax &&
+    return !c->halo && tma_eligible(c) && c->sponge_monotone &&
+           c->sponge_w <= (uint32_t)kTbSpongeMax &&
            c->n_src <= (uint32_t)kTbMaxSrc &&
            (!c->c2f || c->tma_c2_map) && ensure_tb_buffers(c);
 }
@@ -523,9 +529,9 @@ ws3d_status launch_step(ws3d_ctx* c) {
     const bool cells = a.types != nullptr;
     uint32_t v = c->desc.variant;
     // auto (single steps; pairs of steps go to k_step_tma2, see use_two_step):
-    // the TMA pipeline on one GPU (0.91 of measured HBM peak at 512^3);
-    // z-slabs and cell arrays take the register-prefetch z-stream kernel
-    // (0.75), which measured ahead of the cp.async pipeline (0.73) on slabs.
+    // the TMA pipeline on one GPU and on z-slabs (0.91 of measured HBM peak at
+    // 512^3 on one GPU); cell arrays and grids too narrow for its boxes take
+    // the register-prefetch z-stream kernel (0.75).
     if (v == WS3D_VARIANT_AUTO) v = tma_eligible(c) ? WS3D_VARIANT_TMA : WS3D_VARIANT_ZSTREAM;
     if (v == WS3D_VARIANT_TMA2) v = WS3D_VARIANT_TMA;  // single steps of the two-step variant
     if (v == WS3D_VARIANT_ASYNC) {
@@ -538,8 +544,8 @@ ws3d_status launch_step(ws3d_ctx* c) {
     if (v == WS3D_VARIANT_TMA) {
         if (!tma_eligible(c))
             return fail(c, WS3D_EINVAL,
-                        "the TMA kernel needs one GPU, the default face layout, W > 128 and "
-                        "H >= 16; use the auto or zstream variant");
+                        "the TMA kernel needs the default face layout, W > 128 and H >= 16; "
+                        "use the auto or zstream variant");
         return f ? launch_tma<true>(c, a) : launch_tma<false>(c, a);
     }
     switch (v) {
@@ -1358,8 +1364,9 @@ ws3d_status attach_common(ws3d_ctx* c, bool has_lo, uint32_t lo_nz, bool has_hi)
     c->halo_steps = 0;
     c->lo_ghost_off = has_lo ? (uint64_t)(lo_nz + 1) * c->plane : 0;
     if (c->halo && c->desc.variant != WS3D_VARIANT_ZSTREAM &&
-        c->desc.variant != WS3D_VARIANT_AUTO && c->desc.variant != WS3D_VARIANT_ASYNC)
-        return fail(c, WS3D_EINVAL, "halo exchange needs the auto, async or zstream variant");
+        c->desc.variant != WS3D_VARIANT_AUTO && c->desc.variant != WS3D_VARIANT_ASYNC &&
+        c->desc.variant != WS3D_VARIANT_TMA)
+        return fail(c, WS3D_EINVAL, "halo exchange needs the auto, tma, async or zstream variant");
     return rebuild_source_ghosts(c);
 }
 

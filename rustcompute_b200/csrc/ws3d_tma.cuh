@@ -1,4 +1,4 @@
-// ws3d_tma.cuh -- TMA-fed step kernel for one GPU (sm_100a).
+// ws3d_tma.cuh -- TMA-fed step kernel for one GPU or a z-slab (sm_100a).
 //
 // Same cell rule and arithmetic as k_step_zstream, different data movement:
 //
@@ -20,6 +20,16 @@
 // Every mbarrier wait is bounded (try_wait with a suspend hint, iteration
 // cap); a wait that gives up sets the status word, the CTA stops consuming,
 // and the producer waits (bounded) for the copies it issued before exiting.
+//
+// z-slabs: the (chunk, tile) items of the two boundary z-chunks come after
+// all interior items.  Before the first copy of a boundary run the producer
+// waits (bounded) for the neighbour's flag, then fences the async proxy so
+// that the TMA load of the upper ghost plane sees the neighbour's peer
+// stores; consumers read the lower ghost plane through L2 after the run's
+// first stage arrived (ordered after that wait).  Boundary planes are stored
+// into the neighbours' ghost planes and fenced at system scope, like the
+// other slab kernels.  All TMA loads read this GPU's own memory (the ghost
+// planes are local buffers the neighbours write into); none uses multicast.
 #pragma once
 
 #include <cuda.h>
@@ -97,11 +107,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 struct TmaRun {
     uint32_t tile, zs, ze;  // planes [zs, ze) of tile `tile`
 };
+// halo: boundary chunks after the interior ones (async_chunk_of).
 __device__ __forceinline__ bool next_run(uint32_t& item, uint32_t nitems, uint32_t tiles,
-                                         uint32_t clen, uint32_t nz, TmaRun& r) {
+                                         uint32_t clen, uint32_t nz, bool halo, TmaRun& r) {
     if (item >= nitems) return false;
-    const uint32_t chunk = item / tiles;
-    r.tile = item - chunk * tiles;
+    const uint32_t nchunks = (nz + clen - 1) / clen;
+    const uint32_t chunk = async_chunk_of(item, tiles, nchunks, halo);
+    r.tile = item % tiles;
     r.zs = chunk * clen;
     r.ze = min(nz, r.zs + clen);
     item += gridDim.x;
@@ -137,6 +149,8 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
     }
     __syncthreads();
 
+    const bool halo = a.wait_lo != nullptr || a.wait_hi != nullptr || a.peer_lo != nullptr ||
+                      a.peer_hi != nullptr;
     if (warp == TY) {
         // ------------------------------------------------------------ producer
         if (lane != 0) return;
@@ -144,8 +158,17 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
         uint32_t item = blockIdx.x;
         TmaRun r;
         bool ok = true;
-        while (ok && next_run(item, nitems, tiles, clen, a.nz, r)) {
+        while (ok && next_run(item, nitems, tiles, clen, a.nz, halo, r)) {
             const int x0 = (int)((r.tile % tiles_x) * 128u), y0 = (int)((r.tile / tiles_x) * TY);
+            const bool need_lo = a.wait_lo && r.zs == 0, need_hi = a.wait_hi && r.ze == a.nz;
+            if (need_lo || need_hi) {
+                unsigned int bad = 0;
+                if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns)) bad |= 1u;
+                if (need_hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns)) bad |= 2u;
+                if (bad) atomicOr(a.status, bad);
+                // the neighbour's ghost-plane stores, acquired above, before our TMA loads
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
             for (uint32_t i = 0; ok && i <= r.ze - r.zs; ++i, ++j) {
                 const int s = (int)(j % S);
                 if (j >= S && !mbar_wait(&empty[s], (uint32_t)((j / S - 1) & 1))) {
@@ -184,13 +207,16 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
     uint64_t j = 0;  // stage items consumed
     uint32_t item = blockIdx.x;
     TmaRun r;
-    while (next_run(item, nitems, tiles, clen, a.nz, r)) {
+    while (next_run(item, nitems, tiles, clen, a.nz, halo, r)) {
         const uint32_t x0 = (r.tile % tiles_x) * 128u, y0 = (r.tile / tiles_x) * TY;
         const uint32_t x = x0 + 4u * lane, y = y0 + w;
         const bool act = x < a.pitch && y < a.H;
         const int64_t row = (int64_t)y * a.pitch + x;
         const XYPre xy = make_xypre(x, y, a);
-        float4 pm = act ? ld4(a.p + zs_plane((int64_t)r.zs - 1, P) + row) : z4;
+        const float* pmp = a.p + zs_plane((int64_t)r.zs - 1, P) + row;  // plane zs-1
+        // one GPU: issue the load early; slabs: plane -1 is a ghost plane, read
+        // (through L2) once the producer has waited for the neighbour
+        float4 pm = act && !halo ? ld4(pmp) : z4;
         // prologue item
         {
             const int s = (int)(j % S);
@@ -199,6 +225,7 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
                 return;
             }
         }
+        if (act && halo) pm = ld4_plane(pmp, (int64_t)r.zs - 1, a.nz);
         const float* Pz = reinterpret_cast<const float*>(smem + (j % S) * L::kStage);
         float4 pc = *reinterpret_cast<const float4*>(Pz + (w + 1) * L::kPRow + 4 + 4 * lane);
         ++j;
@@ -229,6 +256,8 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
                 const float4 out = cells4_default(xy, a.z0 + z, wl, er, Sv, Nv, pm, pc, pn, vpp,
                                                   vc2, a);
                 st4(a.pp + zs_plane((int64_t)z, P) + row, out);
+                if (z == 0 && a.peer_lo) st4(a.peer_lo + row, out);
+                if (z + 1 == a.nz && a.peer_hi) st4(a.peer_hi + row, out);
             }
             // The previous stage (plane z: neighbours, and this row's centre) is done.
             __syncwarp();
@@ -241,6 +270,7 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[(j - 1) % S]);
     }
+    if (a.peer_lo || a.peer_hi) __threadfence_system();
 }
 
 }  // namespace ws3d

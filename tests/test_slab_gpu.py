@@ -40,12 +40,14 @@ def make(wl, zb, ze, device=0, budget_ns=0, variant="auto"):
     return b
 
 
-@pytest.mark.parametrize("variant", ["auto", "zstream"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "tma"])
 @pytest.mark.parametrize("nslab", [2, 3, 4])
 @pytest.mark.parametrize("name,grid,steps", [("c3", (96, 72, 64), 50), ("c2", (48, 40, 37), 60),
-                                             ("c3", (160, 40, 45), 30)])
+                                             ("c3", (160, 40, 45), 30), ("c2", (264, 24, 70), 24)])
 def test_local_slab_group_equals_single_context(nslab, name, grid, steps, variant):
     W, H, D = grid
+    if variant == "tma" and not (W > 128 and H >= 16):
+        pytest.skip("TMA kernel needs W > 128 and H >= 16")
     wl = configs.build(name, W, H, D, steps=steps)
     bounds = [slab_bounds(D, nslab, r) for r in range(nslab)]
     # put extra sources exactly on slab boundary planes (both sides)
@@ -74,7 +76,8 @@ def test_local_slab_group_equals_single_context(nslab, name, grid, steps, varian
 
 
 def _idle_lower_neighbour(conn, grid, zb, ze):
-    """Child process: owns the lower slab, exports it, never steps."""
+    """Child process: owns the lower slab, exports it, never steps (its
+    flags stay 0, so the parent's wait for the lower neighbour runs out)."""
     sys.path.insert(0, ROOT)
     from rustcompute_b200 import configs as cfg
     from rustcompute_b200.slab import export_handles as exp
@@ -86,8 +89,8 @@ def _idle_lower_neighbour(conn, grid, zb, ze):
     b.close()
 
 
-def test_bounded_wait_times_out_and_context_stays_usable():
-    grid = (64, 40, 48)
+@pytest.mark.parametrize("grid", [(64, 40, 48), (160, 40, 48)])  # z-stream / TMA kernel
+def test_bounded_wait_times_out_and_context_stays_usable(grid):
     W, H, D = grid
     wl = configs.build("c1", W, H, D, steps=4)
     ctx = mpm.get_context("spawn")
