@@ -314,6 +314,123 @@ WS3D_API ws3d_status ws3d_halo_sync(ws3d_ctx *ctx, uint32_t phase);
  * on their shared stream. */
 WS3D_API ws3d_status ws3d_step_group(ws3d_ctx *const *ctxs, uint32_t n, uint64_t steps);
 
+/* ---------------------------------------------------------------------------
+ * Resident (command-driven) persistent kernel, one GPU.
+ *
+ * The reference's persistent backend (persistent_backend.rs:174-446 over
+ * ringkernel-cuda persistent.rs:571-1050, kernel persistent_fdtd.rs:713-978)
+ * keeps one kernel running and drives it through queues in pinned mapped
+ * host memory: host-to-kernel commands (H2K) and kernel-to-host responses
+ * (K2H), 64-byte messages with the reference host's layout and codes
+ * (ringkernel-cuda persistent.rs:571-590, 807-824; codes persistent_fdtd.rs:257-271).  Here the kernel's leader thread drains the
+ * H2K queue between steps; all CTAs meet at a bounded grid barrier once per
+ * step and run the same cell body as ws3d_step (bit-identical fields).
+ * Progress (step, steps remaining, energy = sum of p^2, deterministic) goes
+ * to K2H every progress_interval steps and on GET_PROGRESS.
+ *
+ * Differences, on purpose: INJECT_IMPULSE applies ws3d_inject_impulse's
+ * semantics (p += a, p_prev += a/2), not the reference kernel's p-only add,
+ * so that resident and per-step runs stay bit-identical; and an idle kernel
+ * (no steps to run) does not spin forever: after idle_budget_ns without work
+ * it leaves, and the next resident call that finds pending commands or steps
+ * relaunches it transparently (the state lives in device memory).  While
+ * resident mode is active the context accepts only ws3d_resident_* calls,
+ * ws3d_stats_get, ws3d_last_error and ws3d_memory_usage; the others return
+ * WS3D_ECOMMAND.  One GPU (no z-slabs).
+ * ------------------------------------------------------------------------- */
+enum {
+    WS3D_CMD_NOP = 0,
+    WS3D_CMD_RUN_STEPS = 1,      /* param1: steps to add */
+    WS3D_CMD_PAUSE = 2,
+    WS3D_CMD_RESUME = 3,
+    WS3D_CMD_TERMINATE = 4,
+    WS3D_CMD_INJECT_IMPULSE = 5, /* param1: (x << 32) | y, param2: z, param4: amplitude */
+    WS3D_CMD_SET_SOURCE = 6,     /* not handled (the reference kernel ignores it): RESP_ERROR */
+    WS3D_CMD_GET_PROGRESS = 7
+};
+enum {
+    WS3D_RESP_ACK = 0,
+    WS3D_RESP_PROGRESS = 1,
+    WS3D_RESP_ERROR = 2,
+    WS3D_RESP_TERMINATED = 3,
+    WS3D_RESP_ENERGY = 4
+};
+
+typedef struct ws3d_h2k_msg { /* H2KMessage, ringkernel-cuda persistent.rs:571-590 (64 bytes) */
+    uint32_t cmd;
+    uint32_t flags;
+    uint64_t cmd_id;
+    uint64_t param1;
+    uint32_t param2;
+    uint32_t param3;
+    float param4;
+    float param5;
+    uint64_t reserved[3];
+} ws3d_h2k_msg;
+
+typedef struct ws3d_k2h_msg { /* K2HMessage, ringkernel-cuda persistent.rs:807-824 (64 bytes) */
+    uint32_t resp_type;
+    uint32_t flags;
+    uint64_t cmd_id;
+    uint64_t step;
+    uint64_t steps_remaining;
+    float energy;
+    uint32_t error_code;
+    uint64_t reserved[3];
+} ws3d_k2h_msg;
+
+typedef struct ws3d_resident_config { /* PersistentBackendConfig, persistent_backend.rs:88-99 */
+    uint64_t progress_interval; /* 0 = 100 */
+    uint32_t h2k_capacity;      /* power of two <= 65536, 0 = 256 */
+    uint32_t k2h_capacity;      /* power of two <= 65536, 0 = 256 */
+    uint64_t idle_budget_ns;    /* 0 = 1 s */
+    uint64_t reserved[4];
+} ws3d_resident_config;
+
+typedef struct ws3d_resident_stats { /* PersistentBackendStats, persistent_backend.rs:134-152 */
+    uint64_t current_step;
+    uint64_t steps_remaining;
+    float total_energy;          /* at the last progress report */
+    uint32_t has_terminated;     /* the kernel left after TERMINATE (or gave up) */
+    uint64_t messages_processed;
+    uint64_t k2h_dropped;        /* responses dropped because the K2H queue was full */
+    uint64_t launches;           /* launches of the resident kernel, relaunches included */
+    uint32_t is_running;         /* resident mode active (started, not shut down) */
+    uint32_t kernel_alive;       /* a resident kernel occupies the GPU right now */
+    uint32_t paused;
+    uint32_t reserved32;
+    uint64_t reserved[3];
+} ws3d_resident_stats;
+
+/* PersistentBackend::start: allocate the mapped queues (first call) and
+ * launch the resident kernel on the context's stream.  cfg may be NULL. */
+WS3D_API ws3d_status ws3d_resident_start(ws3d_ctx *ctx, const ws3d_resident_config *cfg);
+/* Enqueue one command; WS3D_ECOMMAND when the H2K queue is full.  Relaunches
+ * an idle-exited kernel. */
+WS3D_API ws3d_status ws3d_resident_send(ws3d_ctx *ctx, const ws3d_h2k_msg *msg);
+/* RUN_STEPS / INJECT_IMPULSE commands (PersistentSimulation::run_steps,
+ * inject_impulse). */
+WS3D_API ws3d_status ws3d_resident_run_steps(ws3d_ctx *ctx, uint64_t steps);
+WS3D_API ws3d_status ws3d_resident_inject_impulse(ws3d_ctx *ctx, uint32_t x, uint32_t y,
+                                                  uint32_t z, float amplitude);
+/* Block until the kernel reports current_step >= step (PersistentBackend::step
+ * polls the control block the same way, persistent_backend.rs:283-326);
+ * WS3D_ETIMEOUT after timeout_ns (0 = 10 s, the reference's timeout). */
+WS3D_API ws3d_status ws3d_resident_wait_step(ws3d_ctx *ctx, uint64_t step, uint64_t timeout_ns);
+/* PersistentBackend::poll_responses: drain up to max K2H messages. */
+WS3D_API ws3d_status ws3d_resident_poll(ws3d_ctx *ctx, ws3d_k2h_msg *out, uint32_t max,
+                                        uint32_t *n_out);
+/* PersistentBackend::stats (reads the mapped control block). */
+WS3D_API ws3d_status ws3d_resident_stats_get(const ws3d_ctx *ctx, ws3d_resident_stats *out);
+/* PersistentBackend::download_pressure: waits (bounded) until no steps are
+ * pending, then copies the current field on a side stream while the kernel
+ * stays resident. */
+WS3D_API ws3d_status ws3d_resident_download(ws3d_ctx *ctx, float *pressure, uint64_t timeout_ns);
+/* PersistentBackend::shutdown: TERMINATE, wait (bounded; 0 = 10 s) for the
+ * kernel to leave, and hand the fields back to the ordinary API (step count
+ * and buffer roles follow the steps the kernel ran). */
+WS3D_API ws3d_status ws3d_resident_shutdown(ws3d_ctx *ctx, uint64_t timeout_ns);
+
 #ifdef __cplusplus
 }
 #endif

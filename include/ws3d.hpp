@@ -128,35 +128,70 @@ private:
     ws3d_ctx* ctx_ = nullptr;
 };
 
-// PersistentBackend: steps run inside one cooperative launch per call.
+// PersistentBackend: one resident kernel driven by H2K commands, K2H
+// responses and a control block in mapped host memory (ws3d_resident_*),
+// like persistent_backend.rs:174-446.
 class PersistentBackend {
 public:
-    PersistentBackend(const GridDims& g, const float* pressure, const float* pressure_prev)
-        : gpu_(g, pressure, pressure_prev) {}
-    void start() { running_ = true; }
-    // persistent_backend.rs:269-336: run `steps` steps, return when done.
+    PersistentBackend(const GridDims& g, const float* pressure, const float* pressure_prev,
+                      const ws3d_resident_config* cfg = nullptr)
+        : gpu_(g, pressure, pressure_prev) {
+        if (cfg) cfg_ = *cfg;
+    }
+    ~PersistentBackend() {
+        if (running_) ws3d_resident_shutdown(gpu_.raw(), 0);
+    }
+    // persistent_backend.rs:253-264
+    void start() {
+        if (running_) return;
+        detail::check(ws3d_resident_start(gpu_.raw(), &cfg_), gpu_.raw(), "PersistentBackend::start");
+        running_ = true;
+    }
+    // persistent_backend.rs:269-336: RUN_STEPS, wait for the target step (10 s).
     void step(uint64_t steps) {
         if (!running_) start();
-        detail::check(ws3d_step_persistent(gpu_.raw(), steps), gpu_.raw(),
+        ws3d_resident_stats st;
+        detail::check(ws3d_resident_stats_get(gpu_.raw(), &st), gpu_.raw(), "PersistentBackend::step");
+        detail::check(ws3d_resident_run_steps(gpu_.raw(), steps), gpu_.raw(),
                       "PersistentBackend::step");
-        gpu_.sync();
+        detail::check(ws3d_resident_wait_step(gpu_.raw(), st.current_step + steps, 0), gpu_.raw(),
+                      "PersistentBackend::step");
     }
     void inject_impulse(uint32_t x, uint32_t y, uint32_t z, float amplitude) {
         if (!running_) start();
-        gpu_.inject_impulse(x, y, z, amplitude);
+        detail::check(ws3d_resident_inject_impulse(gpu_.raw(), x, y, z, amplitude), gpu_.raw(),
+                      "PersistentBackend::inject_impulse");
     }
     void download_pressure(float* pressure) {
-        if (running_) gpu_.download_pressure(pressure);
+        if (running_)
+            detail::check(ws3d_resident_download(gpu_.raw(), pressure, 0), gpu_.raw(),
+                          "PersistentBackend::download_pressure");
     }
+    // persistent_backend.rs:403-419: drain up to max responses.
+    uint32_t poll_responses(ws3d_k2h_msg* out, uint32_t max) {
+        uint32_t n = 0;
+        detail::check(ws3d_resident_poll(gpu_.raw(), out, max, &n), gpu_.raw(),
+                      "PersistentBackend::poll_responses");
+        return n;
+    }
+    ws3d_resident_stats stats() const {
+        ws3d_resident_stats st;
+        detail::check(ws3d_resident_stats_get(const_cast<GpuBackend3D&>(gpu_).raw(), &st), nullptr,
+                      "PersistentBackend::stats");
+        return st;
+    }
+    // persistent_backend.rs:422-433
     void shutdown() {
-        if (running_) gpu_.sync();
+        if (!running_) return;
         running_ = false;
+        detail::check(ws3d_resident_shutdown(gpu_.raw(), 0), gpu_.raw(), "PersistentBackend::shutdown");
     }
     bool is_running() const { return running_; }
     GpuBackend3D& backend() { return gpu_; }
 
 private:
     GpuBackend3D gpu_;
+    ws3d_resident_config cfg_{};
     bool running_ = false;
 };
 

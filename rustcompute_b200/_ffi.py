@@ -87,6 +87,76 @@ class ws3d_halo_handles(C.Structure):
     ]
 
 
+# resident (command-driven) mode: message codes and layouts (include/ws3d.h)
+WS3D_CMD_NOP = 0
+WS3D_CMD_RUN_STEPS = 1
+WS3D_CMD_PAUSE = 2
+WS3D_CMD_RESUME = 3
+WS3D_CMD_TERMINATE = 4
+WS3D_CMD_INJECT_IMPULSE = 5
+WS3D_CMD_SET_SOURCE = 6
+WS3D_CMD_GET_PROGRESS = 7
+WS3D_RESP_ACK = 0
+WS3D_RESP_PROGRESS = 1
+WS3D_RESP_ERROR = 2
+WS3D_RESP_TERMINATED = 3
+WS3D_RESP_ENERGY = 4
+
+
+class ws3d_h2k_msg(C.Structure):
+    _fields_ = [
+        ("cmd", C.c_uint32),
+        ("flags", C.c_uint32),
+        ("cmd_id", C.c_uint64),
+        ("param1", C.c_uint64),
+        ("param2", C.c_uint32),
+        ("param3", C.c_uint32),
+        ("param4", C.c_float),
+        ("param5", C.c_float),
+        ("reserved", C.c_uint64 * 3),
+    ]
+
+
+class ws3d_k2h_msg(C.Structure):
+    _fields_ = [
+        ("resp_type", C.c_uint32),
+        ("flags", C.c_uint32),
+        ("cmd_id", C.c_uint64),
+        ("step", C.c_uint64),
+        ("steps_remaining", C.c_uint64),
+        ("energy", C.c_float),
+        ("error_code", C.c_uint32),
+        ("reserved", C.c_uint64 * 3),
+    ]
+
+
+class ws3d_resident_config(C.Structure):
+    _fields_ = [
+        ("progress_interval", C.c_uint64),
+        ("h2k_capacity", C.c_uint32),
+        ("k2h_capacity", C.c_uint32),
+        ("idle_budget_ns", C.c_uint64),
+        ("reserved", C.c_uint64 * 4),
+    ]
+
+
+class ws3d_resident_stats(C.Structure):
+    _fields_ = [
+        ("current_step", C.c_uint64),
+        ("steps_remaining", C.c_uint64),
+        ("total_energy", C.c_float),
+        ("has_terminated", C.c_uint32),
+        ("messages_processed", C.c_uint64),
+        ("k2h_dropped", C.c_uint64),
+        ("launches", C.c_uint64),
+        ("is_running", C.c_uint32),
+        ("kernel_alive", C.c_uint32),
+        ("paused", C.c_uint32),
+        ("reserved32", C.c_uint32),
+        ("reserved", C.c_uint64 * 3),
+    ]
+
+
 _P = C.c_void_p
 _F = C.POINTER(C.c_float)
 _U8 = C.POINTER(C.c_uint8)
@@ -131,6 +201,16 @@ SIGNATURES = {
     "ws3d_halo_attach_local": (C.c_int, [_CTX, _CTX, _CTX]),
     "ws3d_halo_sync": (C.c_int, [_CTX, C.c_uint32]),
     "ws3d_step_group": (C.c_int, [C.POINTER(_CTX), C.c_uint32, C.c_uint64]),
+    "ws3d_resident_start": (C.c_int, [_CTX, C.POINTER(ws3d_resident_config)]),
+    "ws3d_resident_send": (C.c_int, [_CTX, C.POINTER(ws3d_h2k_msg)]),
+    "ws3d_resident_run_steps": (C.c_int, [_CTX, C.c_uint64]),
+    "ws3d_resident_inject_impulse": (
+        C.c_int, [_CTX, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float]),
+    "ws3d_resident_wait_step": (C.c_int, [_CTX, C.c_uint64, C.c_uint64]),
+    "ws3d_resident_poll": (C.c_int, [_CTX, C.POINTER(ws3d_k2h_msg), C.c_uint32, _U32]),
+    "ws3d_resident_stats_get": (C.c_int, [_CTX, C.POINTER(ws3d_resident_stats)]),
+    "ws3d_resident_download": (C.c_int, [_CTX, _F, C.c_uint64]),
+    "ws3d_resident_shutdown": (C.c_int, [_CTX, C.c_uint64]),
 }
 
 _lib = None

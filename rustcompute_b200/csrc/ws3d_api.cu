@@ -22,6 +22,9 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <atomic>
+#include <chrono>
+#include <thread>
 #include <vector>
 
 using namespace ws3d;
@@ -97,6 +100,28 @@ struct ws3d_ctx {
     // persistent mode: co-resident CTAs of k_persistent per instantiation
     int pers_resident[4] = {0, 0, 0, 0};
     uint64_t persistent_launches = 0;
+
+    // resident (command-driven) mode: queues and control block in mapped
+    // host memory; see ws3d_resident_* and k_resident
+    bool res_active = false;       // started and not shut down
+    bool res_alive = false;        // a launch is (or may still be) on the GPU
+    bool res_terminated = false;   // the kernel left after TERMINATE
+    void* res_mem = nullptr;       // cudaHostAlloc'd block (host view; mapped)
+    size_t res_bytes = 0;
+    ResidentCtrl* res_ctrl = nullptr;
+    ResQueue* res_h2k = nullptr;
+    ResMsg* res_h2k_slots = nullptr;
+    ResQueue* res_k2h = nullptr;
+    ResMsg* res_k2h_slots = nullptr;
+    uint64_t res_h2k_tail = 0;     // host producer index
+    uint64_t res_k2h_head = 0;     // host consumer index
+    ws3d_resident_config res_cfg{};
+    cudaEvent_t res_done = nullptr;
+    cudaStream_t res_side = nullptr;  // downloads while the kernel stays resident
+    uint64_t res_launches = 0;
+    int res_role[2] = {0, 1};      // field buffers of roles 0 / 1 of the current launch
+    uint64_t res_step0 = 0;        // step count at the current launch
+    int res_resident = 0;          // co-resident CTAs of k_resident
 };
 
 namespace {
@@ -133,6 +158,16 @@ ws3d_status cuda_fail(ws3d_ctx* c, ws3d_status s, cudaError_t e, const char* wha
     do {                                                              \
         cudaError_t e_ = (call);                                      \
         if (e_ != cudaSuccess) return cuda_fail(ctx, status, e_, #call); \
+    } while (0)
+
+// Calls that use the context's stream or its fields are refused while a
+// resident kernel owns them (ws3d_resident_shutdown hands them back).
+#define WS3D_NOT_RESIDENT(ctx)                                                        \
+    do {                                                                              \
+        if ((ctx) && (ctx)->res_active)                                               \
+            return fail(ctx, WS3D_ECOMMAND,                                           \
+                        "%s: a resident kernel owns this context; use ws3d_resident_* " \
+                        "or ws3d_resident_shutdown first", __func__);                 \
     } while (0)
 
 ws3d_status check_launch(ws3d_ctx* c, const char* what) {
@@ -199,8 +234,10 @@ StepParams make_params(const ws3d_ctx* c) {
         // Before step s a neighbour raises its flag to s+1 (after its step s-1
         // and after its sources of step s reached our ghost planes).
         a.wait_val = c->halo_steps + 1;
-        a.budget_ns = c->budget_ns;
     }
+    // bound of every device-side wait: neighbour flags and the grid barriers
+    // of the persistent and resident kernels (one GPU too)
+    a.budget_ns = c->budget_ns;
     a.status = reinterpret_cast<unsigned int*>(c->flags + 2);
     return a;
 }
@@ -821,6 +858,8 @@ void ws3d_destroy(ws3d_ctx* c) {
     if (!c) return;
     {
         DeviceGuard g(c->desc.device);
+        // a resident kernel is told to terminate first (bounded wait)
+        if (c->res_active) ws3d_resident_shutdown(c, 10000000000ull);
         // Never dereference a caller's stream here (it may already be gone):
         // wait for our own stream, or for the device when an external one is set.
         if (c->stream == c->own_stream) {
@@ -840,6 +879,9 @@ void ws3d_destroy(ws3d_ctx* c) {
         dfree(c, c->flags, kFlagWords);
         for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
         for (cudaEvent_t ev : c->tev) cudaEventDestroy(ev);
+        if (c->res_mem) cudaFreeHost(c->res_mem);
+        if (c->res_done) cudaEventDestroy(c->res_done);
+        if (c->res_side) cudaStreamDestroy(c->res_side);
         c->ipc_opened.clear();
         if (c->own_stream) cudaStreamDestroy(c->own_stream);
     }
@@ -849,6 +891,7 @@ void ws3d_destroy(ws3d_ctx* c) {
 const char* ws3d_last_error(const ws3d_ctx* c) { return c ? c->err.c_str() : ""; }
 
 ws3d_status ws3d_upload(ws3d_ctx* c, const float* p, const float* pp) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     ws3d_status s = WS3D_OK;
@@ -860,6 +903,7 @@ ws3d_status ws3d_upload(ws3d_ctx* c, const float* p, const float* pp) {
 }
 
 ws3d_status ws3d_download(ws3d_ctx* c, float* p, float* pp) {
+    WS3D_NOT_RESIDENT(c);
     if (!c || !p) return c ? fail(c, WS3D_EINVAL, "download: pressure is NULL") : WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     ws3d_status s = d2h_pitched(c, p, c->buf[c->ip], WS3D_EMEMORY);
@@ -870,6 +914,7 @@ ws3d_status ws3d_download(ws3d_ctx* c, float* p, float* pp) {
 }
 
 ws3d_status ws3d_reset(ws3d_ctx* c, const float* p, const float* pp) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     c->ip = 0;
     c->ipp = 1;
@@ -883,6 +928,7 @@ ws3d_status ws3d_reset(ws3d_ctx* c, const float* p, const float* pp) {
 }
 
 ws3d_status ws3d_set_cells(ws3d_ctx* c, const uint8_t* types, const float* refl) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     if ((types == nullptr) != (refl == nullptr))
         return fail(c, WS3D_EINVAL, "set_cells: pass both arrays or neither");
@@ -929,6 +975,7 @@ ws3d_status ws3d_set_cells(ws3d_ctx* c, const uint8_t* types, const float* refl)
 }
 
 ws3d_status ws3d_set_c2_field(ws3d_ctx* c, const float* c2) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     if (!c2) {
@@ -951,6 +998,7 @@ ws3d_status ws3d_set_c2_field(ws3d_ctx* c, const float* c2) {
 
 ws3d_status ws3d_set_sources(ws3d_ctx* c, uint32_t n, const uint32_t* xyz, const float* wavelet,
                              uint64_t len) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     if (n > 0 && (!xyz || !wavelet || len == 0))
         return fail(c, WS3D_EINVAL, "set_sources: xyz/wavelet missing");
@@ -1051,12 +1099,14 @@ ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed, uint64_t* nlaunch = n
 }  // namespace
 
 ws3d_status ws3d_step(ws3d_ctx* c, uint64_t n) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     return step_impl(c, n, false);
 }
 
 ws3d_status ws3d_step_timed(ws3d_ctx* c, uint64_t n, double* kernel_ms) {
+    WS3D_NOT_RESIDENT(c);
     if (!c || !kernel_ms) return c ? fail(c, WS3D_EINVAL, "step_timed: kernel_ms is NULL")
                                    : WS3D_EINVAL;
     if (n > (1u << 20)) return fail(c, WS3D_EINVAL, "step_timed: more than 2^20 steps");
@@ -1135,6 +1185,7 @@ struct ImpulseCells {
 }  // namespace
 
 ws3d_status ws3d_inject_impulse(ws3d_ctx* c, uint32_t x, uint32_t y, uint32_t z, float amp) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     if (x >= c->W || y >= c->H || z >= c->Dg) return WS3D_OK;  // grid3d.rs:147
     if (z < c->z0 || z >= c->z0 + c->nz) return WS3D_OK;      // another slab owns it
@@ -1154,6 +1205,7 @@ ws3d_status ws3d_inject_impulse(ws3d_ctx* c, uint32_t x, uint32_t y, uint32_t z,
 
 ws3d_status ws3d_inject_spherical_impulse(ws3d_ctx* c, uint32_t cx, uint32_t cy, uint32_t cz,
                                           float amp, float radius) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     if (!(radius >= 0.0f) || radius > 1024.0f)
         return fail(c, WS3D_EINVAL, "inject_spherical_impulse: radius %g outside [0, 1024]",
@@ -1179,6 +1231,7 @@ ws3d_status ws3d_inject_spherical_impulse(ws3d_ctx* c, uint32_t cx, uint32_t cy,
 }
 
 ws3d_status ws3d_energy(ws3d_ctx* c, double* out) {
+    WS3D_NOT_RESIDENT(c);
     if (!c || !out) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     const uint64_t rows = (uint64_t)c->nz * c->H;
@@ -1197,6 +1250,7 @@ ws3d_status ws3d_energy(ws3d_ctx* c, double* out) {
 }
 
 ws3d_status ws3d_max_pressure(ws3d_ctx* c, float* out) {
+    WS3D_NOT_RESIDENT(c);
     if (!c || !out) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     const uint64_t rows = (uint64_t)c->nz * c->H;
@@ -1217,6 +1271,7 @@ ws3d_status ws3d_max_pressure(ws3d_ctx* c, float* out) {
 size_t ws3d_memory_usage(const ws3d_ctx* c) { return c ? c->device_bytes : 0; }
 
 ws3d_status ws3d_sync(ws3d_ctx* c) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_ELAUNCH);
@@ -1224,6 +1279,7 @@ ws3d_status ws3d_sync(ws3d_ctx* c) {
 }
 
 ws3d_status ws3d_set_stream(ws3d_ctx* c, void* stream) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
@@ -1258,6 +1314,7 @@ ws3d_status ws3d_stats_get(const ws3d_ctx* c, ws3d_stats* o) {
 
 
 ws3d_status ws3d_step_persistent(ws3d_ctx* c, uint64_t n) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     if (c->halo && c->host_ordered)
         return fail(c, WS3D_ECOMMAND, "step_persistent: same-device slab groups step through "
@@ -1280,6 +1337,7 @@ ws3d_status ws3d_step_persistent(ws3d_ctx* c, uint64_t n) {
 }
 
 ws3d_status ws3d_get_slice(ws3d_ctx* c, uint32_t axis, uint32_t index, float* out) {
+    WS3D_NOT_RESIDENT(c);
     if (!c || !out) return c ? fail(c, WS3D_EINVAL, "get_slice: out is NULL") : WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     const float* P = owned0(c, c->buf[c->ip]);
@@ -1308,6 +1366,7 @@ ws3d_status ws3d_get_slice(ws3d_ctx* c, uint32_t axis, uint32_t index, float* ou
 
 ws3d_status ws3d_sample_pressure(ws3d_ctx* c, uint32_t n, const float* pos_m, float cell_size,
                                  float* out) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     if (n == 0) return WS3D_OK;
     if (!pos_m || !out || !(cell_size > 0.0f) || n > (1u << 24))
@@ -1347,6 +1406,7 @@ ws3d_status ws3d_sample_pressure(ws3d_ctx* c, uint32_t n, const float* pos_m, fl
 }
 
 ws3d_status ws3d_set_step(ws3d_ctx* c, uint64_t step) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     DeviceGuard g(c->desc.device);
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
@@ -1376,6 +1436,7 @@ bool same_geometry(const ws3d_ctx* c, uint32_t W, uint32_t H, uint32_t D, uint32
 }  // namespace
 
 ws3d_status ws3d_halo_export(ws3d_ctx* c, ws3d_halo_handles* out) {
+    WS3D_NOT_RESIDENT(c);
     if (!c || !out) return c ? fail(c, WS3D_EINVAL, "halo_export: out is NULL") : WS3D_EINVAL;
     static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
     DeviceGuard g(c->desc.device);
@@ -1398,6 +1459,7 @@ ws3d_status ws3d_halo_export(ws3d_ctx* c, ws3d_halo_handles* out) {
 }
 
 ws3d_status ws3d_halo_attach(ws3d_ctx* c, const ws3d_halo_handles* lo, const ws3d_halo_handles* hi) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     if (c->halo) return fail(c, WS3D_EPEER, "halo_attach: neighbours already attached");
     if (lo && (!same_geometry(c, lo->width, lo->height, lo->depth, lo->pitch) || lo->z_end != c->z0))
@@ -1442,6 +1504,7 @@ ws3d_status ws3d_halo_attach(ws3d_ctx* c, const ws3d_halo_handles* lo, const ws3
 }
 
 ws3d_status ws3d_halo_attach_local(ws3d_ctx* c, ws3d_ctx* lo, ws3d_ctx* hi) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     if (c->halo) return fail(c, WS3D_EPEER, "halo_attach_local: neighbours already attached");
     for (ws3d_ctx* n : {lo, hi}) {
@@ -1474,6 +1537,7 @@ ws3d_status ws3d_halo_attach_local(ws3d_ctx* c, ws3d_ctx* lo, ws3d_ctx* hi) {
 }
 
 ws3d_status ws3d_halo_sync(ws3d_ctx* c, uint32_t phase) {
+    WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
     if (!c->halo) return WS3D_OK;
     if (phase > 1) return fail(c, WS3D_EINVAL, "halo_sync: phase must be 0 or 1");
@@ -1507,6 +1571,7 @@ ws3d_status ws3d_step_group(ws3d_ctx* const* ctxs, uint32_t n, uint64_t steps) {
     for (uint32_t k = 0; k < n; ++k) {
         ws3d_ctx* c = ctxs[k];
         if (!c) return WS3D_EINVAL;
+        WS3D_NOT_RESIDENT(c);
         if (c->desc.device != ctxs[0]->desc.device || c->stream != ctxs[0]->stream)
             return fail(c, WS3D_EINVAL, "step_group: contexts must share one device and stream");
         if (c->halo && !c->halo_synced)
@@ -1532,6 +1597,381 @@ ws3d_status ws3d_step_group(ws3d_ctx* const* ctxs, uint32_t n, uint64_t steps) {
         }
     }
     return WS3D_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Resident mode (host side of k_resident).
+// ---------------------------------------------------------------------------
+static_assert(sizeof(ws3d_resident_config) == 56, "ws3d_resident_config layout");
+static_assert(sizeof(ws3d_resident_stats) == 88, "ws3d_resident_stats layout");
+
+namespace {
+template <class T>
+T vload(const T* p) {
+    return *reinterpret_cast<const volatile T*>(p);
+}
+template <class T>
+void vstore(T* p, T v) {
+    *reinterpret_cast<volatile T*>(p) = v;
+}
+bool is_pow2(uint32_t v) { return v && !(v & (v - 1)); }
+
+// Block layout: control block | H2K header | H2K slots | K2H header | K2H slots.
+size_t res_layout(uint32_t h2k_cap, uint32_t k2h_cap, size_t off[4]) {
+    off[0] = sizeof(ResidentCtrl);
+    off[1] = off[0] + sizeof(ResQueue);
+    off[2] = off[1] + (size_t)h2k_cap * sizeof(ResMsg);
+    off[3] = off[2] + sizeof(ResQueue);
+    return off[3] + (size_t)k2h_cap * sizeof(ResMsg);
+}
+
+// The launch in flight (if any) has ended: take over its step count and
+// buffer roles.
+ws3d_status res_absorb(ws3d_ctx* c) {
+    if (!c->res_alive) return WS3D_OK;
+    const cudaError_t e = cudaEventQuery(c->res_done);
+    if (e == cudaErrorNotReady) return WS3D_OK;
+    if (e != cudaSuccess) return cuda_fail(c, WS3D_EDEVICE, e, "resident kernel");
+    c->res_alive = false;
+    std::atomic_thread_fence(std::memory_order_acquire);
+    const uint64_t ran = vload(&c->res_ctrl->steps_run);
+    const uint32_t cb = vload(&c->res_ctrl->current_buffer);
+    const uint32_t why = vload(&c->res_ctrl->exit_reason);
+    c->step = c->res_step0 + ran;
+    if (cb & 1u) std::swap(c->ip, c->ipp);
+    if (why == 1u) c->res_terminated = true;
+    if (why == 3u || why == 0u) {
+        c->res_terminated = true;
+        const ws3d_status st = check_device_status(c);
+        return st != WS3D_OK ? st
+                             : fail(c, WS3D_EDEVICE, "the resident kernel left without a reason");
+    }
+    return WS3D_OK;
+}
+
+// Work the kernel has not consumed: queued commands, or steps while not paused.
+bool res_pending(const ws3d_ctx* c) {
+    if (c->res_h2k_tail != vload(&c->res_h2k->head)) return true;
+    return vload(&c->res_ctrl->steps_remaining) > 0 && !vload(&c->res_ctrl->paused);
+}
+
+template <bool kC2F, bool kCells>
+ws3d_status res_launch_t(ws3d_ctx* c) {
+    auto kern = k_resident<kC2F, kCells, kPersTY>;
+    const int threads = 32 * kPersTY;
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0);
+    if (e != cudaSuccess || per_sm < 1) return cuda_fail(c, WS3D_ELAUNCH, e, "occupancy(resident)");
+    c->res_resident = per_sm * std::max(1, c->sm_count);
+    PersistentArgs q{};
+    q.a = make_params(c);
+    q.buf[0] = c->buf[c->ip];
+    q.buf[1] = c->buf[c->ipp];
+    q.bar_count = reinterpret_cast<unsigned int*>(c->flags + 4);
+    q.bar_gen = reinterpret_cast<unsigned int*>(c->flags + 5);
+    q.src_off = c->src_off;
+    q.wavelet = c->wavelet;
+    q.n_src = c->n_src;
+    q.wl_len = c->wl_len;
+    q.step0 = c->step;
+    q.tiles_x = (c->pitch + kZsTileX - 1) / kZsTileX;
+    q.tiles = q.tiles_x * ((c->H + kPersTY - 1) / kPersTY);
+    const TmaSchedule sch = tma_schedule(q.tiles, c->nz, (uint32_t)c->res_resident, 4);
+    q.clen = sch.clen;
+    q.nitems = sch.nitems;
+    if (sch.grid > c->red_blocks)
+        return fail(c, WS3D_ELAUNCH, "resident grid %u above the reduction scratch (%u)", sch.grid,
+                    c->red_blocks);
+    ResidentArgs r{};
+    r.q = q;
+    char* dev = nullptr;
+    e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev), c->res_mem, 0);
+    if (e != cudaSuccess) return cuda_fail(c, WS3D_EMEMORY, e, "cudaHostGetDevicePointer");
+    size_t off[4];
+    res_layout(c->res_cfg.h2k_capacity, c->res_cfg.k2h_capacity, off);
+    r.ctrl = reinterpret_cast<ResidentCtrl*>(dev);
+    r.h2k = reinterpret_cast<ResQueue*>(dev + off[0]);
+    r.h2k_slots = reinterpret_cast<const ResMsg*>(dev + off[1]);
+    r.k2h = reinterpret_cast<ResQueue*>(dev + off[2]);
+    r.k2h_slots = reinterpret_cast<ResMsg*>(dev + off[3]);
+    r.decision = reinterpret_cast<unsigned int*>(c->flags + 6);
+    r.partial = c->red_scratch;
+    r.progress_interval = c->res_cfg.progress_interval;
+    r.idle_budget_ns = c->res_cfg.idle_budget_ns;
+    r.h2k_mask = c->res_cfg.h2k_capacity - 1;
+    r.k2h_capacity = c->res_cfg.k2h_capacity;
+    void* args[] = {&r};
+    e = cudaLaunchCooperativeKernel((const void*)kern, dim3(sch.grid), dim3(32, kPersTY, 1), args,
+                                    0, c->stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(c, WS3D_ELAUNCH, e, "cudaLaunchCooperativeKernel(k_resident)");
+    }
+    WS3D_CUDA(c, cudaEventRecord(c->res_done, c->stream), WS3D_EDEVICE);
+    c->launches++;
+    c->res_launches++;
+    c->res_alive = true;
+    c->res_role[0] = c->ip;
+    c->res_role[1] = c->ipp;
+    c->res_step0 = c->step;
+    return WS3D_OK;
+}
+
+ws3d_status res_launch(ws3d_ctx* c) {
+    // a stale give-up bit would make every grid barrier of the new launch fail
+    unsigned int st = 0;
+    WS3D_CUDA(c, cudaMemcpy(&st, c->flags + 2, sizeof st, cudaMemcpyDeviceToHost), WS3D_EDEVICE);
+    if (st) return check_device_status(c);
+    ResidentCtrl* k = c->res_ctrl;
+    vstore(&k->has_terminated, 0u);
+    vstore(&k->exit_reason, 0u);
+    vstore(&k->current_buffer, 0u);
+    vstore(&k->steps_run, (uint64_t)0);
+    vstore(&k->current_step, c->step);
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    const bool f = c->c2f != nullptr, cells = !c->cells_default;
+    if (f && cells) return res_launch_t<true, true>(c);
+    if (f) return res_launch_t<true, false>(c);
+    if (cells) return res_launch_t<false, true>(c);
+    return res_launch_t<false, false>(c);
+}
+
+// Take over a finished launch; relaunch when work is waiting.
+ws3d_status res_service(ws3d_ctx* c) {
+    ws3d_status s = res_absorb(c);
+    if (s != WS3D_OK) return s;
+    if (!c->res_alive && c->res_active && !c->res_terminated && res_pending(c)) return res_launch(c);
+    return WS3D_OK;
+}
+
+ws3d_status res_enqueue(ws3d_ctx* c, const ws3d_h2k_msg& m) {
+    static_assert(sizeof(ws3d_h2k_msg) == sizeof(ResMsg), "H2K message size");
+    const uint64_t head = vload(&c->res_h2k->head);
+    if (c->res_h2k_tail - head >= c->res_cfg.h2k_capacity)
+        return fail(c, WS3D_ECOMMAND, "resident: H2K queue full (%u commands not yet consumed)",
+                    c->res_cfg.h2k_capacity);
+    std::memcpy(&c->res_h2k_slots[c->res_h2k_tail & (c->res_cfg.h2k_capacity - 1)], &m, sizeof m);
+    std::atomic_thread_fence(std::memory_order_seq_cst);  // slot before index
+    vstore(&c->res_h2k->tail, ++c->res_h2k_tail);
+    return WS3D_OK;
+}
+
+void res_sleep() { std::this_thread::sleep_for(std::chrono::microseconds(20)); }
+uint64_t now_ns() {
+    return (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+               std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+}  // namespace
+
+extern "C" {
+
+ws3d_status ws3d_resident_start(ws3d_ctx* c, const ws3d_resident_config* cfg_in) {
+    if (!c) return WS3D_EINVAL;
+    if (c->res_active) return WS3D_OK;  // persistent_backend.rs:253-256
+    if (c->halo) return fail(c, WS3D_EINVAL, "resident mode runs on one GPU (no z-slabs)");
+    ws3d_resident_config cfg{};
+    if (cfg_in) cfg = *cfg_in;
+    if (!cfg.progress_interval) cfg.progress_interval = 100;
+    if (!cfg.h2k_capacity) cfg.h2k_capacity = 256;
+    if (!cfg.k2h_capacity) cfg.k2h_capacity = 256;
+    if (!cfg.idle_budget_ns) cfg.idle_budget_ns = 1000000000ull;
+    if (!is_pow2(cfg.h2k_capacity) || !is_pow2(cfg.k2h_capacity) || cfg.h2k_capacity > 65536 ||
+        cfg.k2h_capacity > 65536)
+        return fail(c, WS3D_EINVAL, "resident: queue capacities must be powers of two <= 65536");
+    DeviceGuard g(c->desc.device);
+    WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
+    ws3d_status s = check_device_status(c);
+    if (s != WS3D_OK) return s;
+    size_t off[4];
+    const size_t bytes = res_layout(cfg.h2k_capacity, cfg.k2h_capacity, off);
+    if (c->res_mem && bytes != c->res_bytes) {
+        cudaFreeHost(c->res_mem);
+        c->res_mem = nullptr;
+    }
+    if (!c->res_mem) {
+        WS3D_CUDA(c, cudaHostAlloc(&c->res_mem, bytes, cudaHostAllocMapped | cudaHostAllocPortable),
+                  WS3D_EMEMORY);
+        c->res_bytes = bytes;
+    }
+    if (!c->res_done) WS3D_CUDA(c, cudaEventCreateWithFlags(&c->res_done, cudaEventDisableTiming),
+                                WS3D_EDEVICE);
+    if (!c->res_side) WS3D_CUDA(c, cudaStreamCreateWithFlags(&c->res_side, cudaStreamNonBlocking),
+                                WS3D_EDEVICE);
+    std::memset(c->res_mem, 0, bytes);
+    char* h = static_cast<char*>(c->res_mem);
+    c->res_ctrl = reinterpret_cast<ResidentCtrl*>(h);
+    c->res_h2k = reinterpret_cast<ResQueue*>(h + off[0]);
+    c->res_h2k_slots = reinterpret_cast<ResMsg*>(h + off[1]);
+    c->res_k2h = reinterpret_cast<ResQueue*>(h + off[2]);
+    c->res_k2h_slots = reinterpret_cast<ResMsg*>(h + off[3]);
+    c->res_h2k->capacity = cfg.h2k_capacity;
+    c->res_h2k->mask = cfg.h2k_capacity - 1;
+    c->res_k2h->capacity = cfg.k2h_capacity;
+    c->res_k2h->mask = cfg.k2h_capacity - 1;
+    c->res_ctrl->current_step = c->step;
+    c->res_h2k_tail = 0;
+    c->res_k2h_head = 0;
+    c->res_cfg = cfg;
+    c->res_terminated = false;
+    c->res_active = true;
+    s = res_launch(c);
+    if (s != WS3D_OK) c->res_active = false;
+    return s;
+}
+
+ws3d_status ws3d_resident_send(ws3d_ctx* c, const ws3d_h2k_msg* msg) {
+    if (!c || !msg) return c ? fail(c, WS3D_EINVAL, "resident_send: msg is NULL") : WS3D_EINVAL;
+    if (!c->res_active) return fail(c, WS3D_ECOMMAND, "resident mode is not started");
+    DeviceGuard g(c->desc.device);
+    ws3d_status s = res_absorb(c);
+    if (s != WS3D_OK) return s;
+    if (c->res_terminated)
+        return fail(c, WS3D_ECOMMAND, "the resident kernel has terminated; start it again");
+    if ((s = res_enqueue(c, *msg)) != WS3D_OK) return s;
+    return res_service(c);
+}
+
+ws3d_status ws3d_resident_run_steps(ws3d_ctx* c, uint64_t steps) {
+    ws3d_h2k_msg m{};
+    m.cmd = WS3D_CMD_RUN_STEPS;
+    m.param1 = steps;
+    return ws3d_resident_send(c, &m);
+}
+
+ws3d_status ws3d_resident_inject_impulse(ws3d_ctx* c, uint32_t x, uint32_t y, uint32_t z,
+                                         float amplitude) {
+    ws3d_h2k_msg m{};
+    m.cmd = WS3D_CMD_INJECT_IMPULSE;
+    m.param1 = ((uint64_t)x << 32) | y;
+    m.param2 = z;
+    m.param4 = amplitude;
+    return ws3d_resident_send(c, &m);
+}
+
+ws3d_status ws3d_resident_wait_step(ws3d_ctx* c, uint64_t step, uint64_t timeout_ns) {
+    if (!c) return WS3D_EINVAL;
+    if (!c->res_active) return fail(c, WS3D_ECOMMAND, "resident mode is not started");
+    DeviceGuard g(c->desc.device);
+    const uint64_t deadline = now_ns() + (timeout_ns ? timeout_ns : 10000000000ull);
+    for (;;) {
+        ws3d_status s = res_service(c);
+        if (s != WS3D_OK) return s;
+        const uint64_t cur = c->res_alive ? vload(&c->res_ctrl->current_step) : c->step;
+        if (cur >= step) return WS3D_OK;
+        if (c->res_terminated)
+            return fail(c, WS3D_ECOMMAND, "the resident kernel terminated at step %llu < %llu",
+                        (unsigned long long)cur, (unsigned long long)step);
+        if (!c->res_alive && !res_pending(c))
+            return fail(c, WS3D_ECOMMAND,
+                        "step %llu < %llu and no steps pending (paused, or too few RUN_STEPS)",
+                        (unsigned long long)cur, (unsigned long long)step);
+        if (now_ns() > deadline)
+            return fail(c, WS3D_ETIMEOUT, "timeout waiting for step %llu (at %llu)",
+                        (unsigned long long)step, (unsigned long long)cur);
+        res_sleep();
+    }
+}
+
+ws3d_status ws3d_resident_poll(ws3d_ctx* c, ws3d_k2h_msg* out, uint32_t max, uint32_t* n_out) {
+    static_assert(sizeof(ws3d_k2h_msg) == sizeof(ResMsg), "K2H message size");
+    if (!c || !n_out || (max && !out)) return c ? fail(c, WS3D_EINVAL, "resident_poll: bad arguments")
+                                               : WS3D_EINVAL;
+    *n_out = 0;
+    if (!c->res_mem) return WS3D_OK;
+    const uint64_t tail = vload(&c->res_k2h->tail);
+    std::atomic_thread_fence(std::memory_order_acquire);
+    uint32_t k = 0;
+    while (c->res_k2h_head != tail && k < max) {
+        std::memcpy(&out[k++], &c->res_k2h_slots[c->res_k2h_head & (c->res_cfg.k2h_capacity - 1)],
+                    sizeof(ws3d_k2h_msg));
+        ++c->res_k2h_head;
+    }
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    vstore(&c->res_k2h->head, c->res_k2h_head);
+    *n_out = k;
+    return WS3D_OK;
+}
+
+ws3d_status ws3d_resident_stats_get(const ws3d_ctx* c, ws3d_resident_stats* o) {
+    if (!c || !o) return WS3D_EINVAL;
+    std::memset(o, 0, sizeof *o);
+    o->current_step = c->step;
+    o->launches = c->res_launches;
+    o->is_running = c->res_active;
+    o->has_terminated = c->res_terminated;
+    if (!c->res_ctrl) return WS3D_OK;
+    const ResidentCtrl* k = c->res_ctrl;
+    const bool alive = c->res_alive && cudaEventQuery(c->res_done) == cudaErrorNotReady;
+    if (c->res_alive) o->current_step = vload(&k->current_step);
+    o->steps_remaining = vload(&k->steps_remaining);
+    o->total_energy = vload(&k->total_energy);
+    o->messages_processed = vload(&k->messages_processed);
+    o->k2h_dropped = vload(&k->k2h_dropped);
+    o->paused = vload(&k->paused);
+    o->kernel_alive = alive;
+    if (vload(&k->exit_reason) == 1u) o->has_terminated = 1;
+    return WS3D_OK;
+}
+
+ws3d_status ws3d_resident_download(ws3d_ctx* c, float* p, uint64_t timeout_ns) {
+    if (!c || !p) return c ? fail(c, WS3D_EINVAL, "resident_download: NULL") : WS3D_EINVAL;
+    if (!c->res_active) return ws3d_download(c, p, nullptr);
+    DeviceGuard g(c->desc.device);
+    const uint64_t deadline = now_ns() + (timeout_ns ? timeout_ns : 10000000000ull);
+    for (;;) {  // until the kernel consumed every command and ran every step
+        ws3d_status s = res_service(c);
+        if (s != WS3D_OK) return s;
+        if (!res_pending(c)) break;
+        if (now_ns() > deadline)
+            return fail(c, WS3D_ETIMEOUT, "resident_download: steps still pending after the timeout");
+        res_sleep();
+    }
+    // idle kernel (or none): the fields do not change; copy on a side stream
+    const float* src = c->res_alive ? c->buf[c->res_role[vload(&c->res_ctrl->current_buffer) & 1u]]
+                                    : c->buf[c->ip];
+    cudaError_t e = cudaMemcpy2DAsync(p, c->W * sizeof(float), src + c->plane,
+                                      c->pitch * sizeof(float), c->W * sizeof(float),
+                                      (size_t)c->H * c->nz, cudaMemcpyDeviceToHost, c->res_side);
+    if (e != cudaSuccess) return cuda_fail(c, WS3D_EREADBACK, e, "resident_download copy");
+    WS3D_CUDA(c, cudaStreamSynchronize(c->res_side), WS3D_EREADBACK);
+    return WS3D_OK;
+}
+
+ws3d_status ws3d_resident_shutdown(ws3d_ctx* c, uint64_t timeout_ns) {
+    if (!c) return WS3D_EINVAL;
+    if (!c->res_active) return WS3D_OK;
+    DeviceGuard g(c->desc.device);
+    const uint64_t deadline = now_ns() + (timeout_ns ? timeout_ns : 10000000000ull);
+    ws3d_status s = res_absorb(c);
+    if (s == WS3D_OK && !c->res_terminated) {
+        // TERMINATE also reaches a kernel that left after its idle budget: it
+        // is relaunched to run the commands still queued, report the final
+        // energy and post TERMINATED (persistent_fdtd.rs:942-978)
+        ws3d_h2k_msg m{};
+        m.cmd = WS3D_CMD_TERMINATE;
+        while (res_enqueue(c, m) != WS3D_OK) {  // full queue: the kernel drains it every step
+            if ((s = res_service(c)) != WS3D_OK) break;
+            if (now_ns() > deadline)
+                return fail(c, WS3D_ETIMEOUT, "resident_shutdown: H2K queue stays full");
+            res_sleep();
+        }
+        c->err.clear();
+        if (s == WS3D_OK) s = res_service(c);
+        while (s == WS3D_OK && c->res_alive) {
+            if ((s = res_absorb(c)) != WS3D_OK || !c->res_alive) break;
+            if (now_ns() > deadline)
+                return fail(c, WS3D_ETIMEOUT, "resident_shutdown: kernel still running after the "
+                                              "timeout");
+            res_sleep();
+        }
+    }
+    c->res_active = false;
+    WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
+    if (s != WS3D_OK && s != WS3D_ECOMMAND) return s;
+    return check_device_status(c);
 }
 
 }  // extern "C"

@@ -126,4 +126,330 @@ __global__ void __launch_bounds__(32 * TY, 3) k_persistent(PersistentArgs q) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Resident (command-driven) kernel.
+//
+// The reference keeps its persistent kernel running and feeds it commands
+// through SPSC queues in mapped host memory (persistent_fdtd.rs:766-812,
+// 917-978; host side ringkernel-cuda persistent.rs:571-1050).  k_resident
+// does the same on one GPU: between steps the leader thread (CTA 0, thread 0)
+// drains the H2K queue, decides "step", "idle" or "exit" and publishes the
+// decision before the per-step grid barrier; the step itself is the
+// z-streaming cell body of k_persistent, so fields are bit-identical to
+// ws3d_step.  Every progress_interval steps all CTAs sum p^2 (fixed order,
+// double) and the leader posts a PROGRESS message.  Waits are bounded: the
+// grid barrier as in k_persistent, and an idle kernel (no steps, not paused
+// for work) leaves after idle_budget_ns; the host relaunches it when work
+// arrives.  Mapped memory is read with .sys-scope acquire / volatile loads
+// and written with posted volatile stores plus a release of the queue index.
+// ---------------------------------------------------------------------------
+struct ResidentCtrl {            // 256 bytes, mapped host memory
+    uint32_t should_terminate;
+    uint32_t paused;
+    uint64_t steps_remaining;
+    uint64_t current_step;
+    uint32_t current_buffer;     // pressure role relative to the launch (0 or 1)
+    uint32_t has_terminated;     // the kernel has left (any reason)
+    float total_energy;
+    uint32_t exit_reason;        // 0 running, 1 TERMINATE, 2 idle budget, 3 barrier gave up
+    uint64_t messages_processed;
+    uint64_t k2h_dropped;
+    uint64_t steps_run;          // steps run by this launch
+    uint64_t reserved[24];
+};
+static_assert(sizeof(ResidentCtrl) == 256, "control block layout");
+
+struct ResQueue {                // 128 bytes (SpscQueueHeader, persistent_fdtd.rs:224-231)
+    uint64_t head;               // consumer index
+    uint64_t tail;               // producer index
+    uint32_t capacity;
+    uint32_t mask;
+    uint64_t pad[13];
+};
+static_assert(sizeof(ResQueue) == 128, "queue header layout");
+
+struct ResMsg {                  // 64-byte H2K / K2H slot, read and written as 4 x 16 bytes
+    uint4 q[4];
+};
+
+struct ResidentArgs {
+    PersistentArgs q;            // one GPU: no neighbours
+    ResidentCtrl* ctrl;
+    ResQueue* h2k;
+    const ResMsg* h2k_slots;
+    ResQueue* k2h;
+    ResMsg* k2h_slots;
+    unsigned int* decision;      // device word written by the leader before each barrier
+    double* partial;             // per-CTA energy partials (>= gridDim.x)
+    uint64_t progress_interval;
+    unsigned long long idle_budget_ns;
+    uint32_t h2k_mask;           // queue capacities - 1 (kept off the PCIe path)
+    uint32_t k2h_capacity;
+};
+
+// The leader thread's copy of the control state, in shared memory so that
+// the other threads do not carry it in registers through the step.
+struct ResLeader {
+    uint64_t steps_rem, msgs, dropped, h2k_head, k2h_tail, k2h_head;
+    unsigned long long idle_t0;
+    uint32_t paused, term;
+    float energy;
+};
+
+enum : unsigned int { kResIdle = 0, kResStep = 1, kResExitTerm = 2, kResExitIdle = 3 };
+
+// 16-byte volatile accesses to mapped host memory (queue slots)
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_volatile_v4(void* p, uint4 v) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Leader: post one K2H message (dropped, and counted, when the queue is full).
+__device__ __forceinline__ void res_post(const ResidentArgs& r, uint64_t& tail, uint64_t& head_seen,
+                                         uint64_t& dropped, uint32_t type, uint64_t cmd_id,
+                                         uint64_t step, uint64_t remaining, float energy,
+                                         uint32_t error) {
+    const uint64_t cap = r.k2h_capacity;
+    if (tail - head_seen >= cap) head_seen = ld_acquire_sys_u64(&r.k2h->head);
+    if (tail - head_seen >= cap) {
+        ++dropped;
+        return;
+    }
+    ResMsg m;
+    m.q[0] = make_uint4(type, 0u, (uint32_t)cmd_id, (uint32_t)(cmd_id >> 32));
+    m.q[1] = make_uint4((uint32_t)step, (uint32_t)(step >> 32), (uint32_t)remaining,
+                        (uint32_t)(remaining >> 32));
+    m.q[2] = make_uint4(__float_as_uint(energy), error, 0u, 0u);
+    m.q[3] = make_uint4(0u, 0u, 0u, 0u);
+    uint4* dst = r.k2h_slots[tail & (cap - 1)].q;
+    for (int k = 0; k < 4; ++k) st_volatile_v4(dst + k, m.q[k]);
+    ++tail;
+    st_release_sys_u64(&r.k2h->tail, tail);  // orders the slot stores before the index
+}
+
+// All CTAs: sum of p^2 over the owned cells of `p` (owned plane 0), fixed
+// order; returns the total on the leader.  Two grid barriers.
+template <int TY>
+__device__ __forceinline__ bool res_energy(const ResidentArgs& r, const float* p, double* out,
+                                           int* s_ok) {
+    __shared__ double s_part[TY];
+    const PersistentArgs& q = r.q;
+    const StepParams& a = q.a;
+    const unsigned int nb = gridDim.x;
+    const int t = threadIdx.y * 32 + threadIdx.x;
+    double acc = 0.0;
+    const uint64_t rows = (uint64_t)a.nz * a.H;
+    for (uint64_t row = blockIdx.x; row < rows; row += nb) {
+        const uint64_t z = row / a.H, y = row - z * a.H;
+        const float* pr = p + z * a.plane + y * a.pitch;
+        for (uint32_t x = (uint32_t)t; x < a.W; x += 32u * TY) {
+            const float v = pr[x];
+            acc += (double)v * (double)v;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+    if (threadIdx.x == 0) s_part[threadIdx.y] = acc;
+    __syncthreads();
+    if (t == 0) {
+        double b = 0.0;
+        for (int k = 0; k < TY; ++k) b += s_part[k];
+        r.partial[blockIdx.x] = b;
+    }
+    if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, s_ok)) return false;
+    if (blockIdx.x == 0 && t == 0) {
+        double e = 0.0;
+        for (unsigned int k = 0; k < nb; ++k) e += r.partial[k];
+        *out = e;
+    }
+    return true;
+}
+
+template <bool kC2F, bool kCells, int TY>
+__global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
+    __shared__ int s_ok;
+    __shared__ unsigned int s_op;
+    __shared__ ResLeader L;  // used by the leader thread of CTA 0 only
+    const PersistentArgs& q = r.q;
+    const unsigned int nb = gridDim.x;
+    const bool leader = blockIdx.x == 0 && threadIdx.x == 0 && threadIdx.y == 0;
+    const uint64_t interval = r.progress_interval ? r.progress_interval : 100;
+
+    // The leader's copy of the control state (mapped memory is read once here).
+    volatile ResidentCtrl* ctrl = r.ctrl;
+    if (leader) {
+        L.steps_rem = ctrl->steps_remaining;
+        L.paused = ctrl->paused;
+        L.term = 0;
+        L.msgs = ctrl->messages_processed;
+        L.dropped = ctrl->k2h_dropped;
+        L.energy = ctrl->total_energy;
+        L.h2k_head = ld_acquire_sys_u64(&r.h2k->head);
+        L.k2h_tail = ld_acquire_sys_u64(&r.k2h->tail);
+        L.k2h_head = ld_acquire_sys_u64(&r.k2h->head);
+        L.idle_t0 = global_ns();
+    }
+    int cur = 0;           // role of the pressure buffer (0 = q.buf[0] at launch)
+    uint64_t ran = 0;      // steps run by this launch (same on every CTA)
+    unsigned int op = kResIdle;
+    for (;;) {
+        if (leader) {
+            // ---- commands (persistent_fdtd.rs:769-810)
+            const uint64_t tail = ld_acquire_sys_u64(&r.h2k->tail);
+            while (L.h2k_head != tail) {
+                const uint4* src = r.h2k_slots[L.h2k_head & r.h2k_mask].q;
+                const uint4 m0 = ld_volatile_v4(src), m1 = ld_volatile_v4(src + 1),
+                            m2 = ld_volatile_v4(src + 2);
+                const uint32_t cmd = m0.x;
+                const uint64_t cmd_id = (uint64_t)m0.z | ((uint64_t)m0.w << 32);
+                const uint64_t param1 = (uint64_t)m1.x | ((uint64_t)m1.y << 32);
+                const uint32_t param2 = m1.z;
+                const float param4 = __uint_as_float(m2.x);
+                ++L.h2k_head;
+                ++L.msgs;
+                switch (cmd) {
+                    case 0: break;                                   // NOP
+                    case 1: L.steps_rem += param1; break;            // RUN_STEPS
+                    case 2: L.paused = 1; break;                     // PAUSE
+                    case 3: L.paused = 0; break;                     // RESUME
+                    case 4: L.term = 1; break;                       // TERMINATE
+                    case 5: {                                        // INJECT_IMPULSE
+                        const uint32_t ix = (uint32_t)(param1 >> 32), iy = (uint32_t)param1;
+                        const uint32_t iz = param2;
+                        if (ix < q.a.W && iy < q.a.H && iz < q.a.Dg) {
+                            const uint64_t off = (uint64_t)(iz + 1) * q.a.plane +
+                                                 (uint64_t)iy * q.a.pitch + ix;
+                            float* pc = q.buf[cur] + off;
+                            float* pp = q.buf[cur ^ 1] + off;
+                            *pc = __fadd_rn(*pc, param4);
+                            *pp = __fadd_rn(*pp, __fmul_rn(param4, 0.5f));
+                        }
+                        break;
+                    }
+                    case 7:                                          // GET_PROGRESS
+                        res_post(r, L.k2h_tail, L.k2h_head, L.dropped, 1u, cmd_id, q.step0 + ran,
+                                 L.steps_rem, L.energy, 0u);
+                        break;
+                    default:                                         // SET_SOURCE, unknown
+                        res_post(r, L.k2h_tail, L.k2h_head, L.dropped, 2u, cmd_id, q.step0 + ran,
+                                 L.steps_rem, L.energy, cmd);
+                        break;
+                }
+            }
+            st_release_sys_u64(&r.h2k->head, L.h2k_head);
+            ctrl->paused = L.paused;
+            ctrl->steps_remaining = L.steps_rem;
+            ctrl->messages_processed = L.msgs;
+            if (L.term) {
+                op = kResExitTerm;
+            } else if (L.steps_rem > 0 && !L.paused) {
+                op = kResStep;
+                L.idle_t0 = global_ns();
+            } else if (global_ns() - L.idle_t0 > r.idle_budget_ns) {
+                op = kResExitIdle;
+            } else {
+                op = kResIdle;
+                __nanosleep(20000);
+            }
+            *reinterpret_cast<volatile unsigned int*>(r.decision) = op;
+        }
+        if (!grid_barrier(q.bar_count, q.bar_gen, nb, q.a.budget_ns, q.a.status, &s_ok)) {
+            op = 0xFFu;
+            break;
+        }
+        if (threadIdx.x == 0 && threadIdx.y == 0)
+            s_op = *reinterpret_cast<volatile unsigned int*>(r.decision);
+        __syncthreads();
+        op = s_op;
+        if (op == kResExitTerm || op == kResExitIdle) break;
+        if (op != kResStep) continue;
+
+        // ---- one step (k_persistent's body, one GPU)
+        StepParams a = q.a;
+        a.p = q.buf[cur] + a.plane;
+        a.pp = q.buf[cur ^ 1] + a.plane;
+        if (q.n_src) {
+            if (leader)
+                inject_sources_dev(q.buf[cur], q.buf[cur ^ 1], q.src_off, q.wavelet, q.n_src,
+                                   q.wl_len, q.step0 + ran, nullptr, nullptr, nullptr);
+            if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok)) {
+                op = 0xFFu;
+                break;
+            }
+        }
+        for (uint32_t item = blockIdx.x; item < q.nitems; item += nb) {
+            const uint32_t chunk = item / q.tiles, tile = item - chunk * q.tiles;
+            const uint32_t zs = chunk * q.clen, ze = min(a.nz, zs + q.clen);
+            zs_tile<kC2F, kCells, TY>(a, tile % q.tiles_x, tile / q.tiles_x, zs, ze);
+        }
+        cur ^= 1;
+        ++ran;
+        if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok)) {
+            op = 0xFFu;
+            break;
+        }
+        const bool progress = (q.step0 + ran) % interval == 0;
+        if (progress) {
+            double e = 0.0;
+            if (!res_energy<TY>(r, q.buf[cur] + a.plane, &e, &s_ok)) {
+                op = 0xFFu;
+                break;
+            }
+            if (leader) L.energy = (float)e;
+        }
+        if (leader) {
+            --L.steps_rem;
+            ctrl->current_step = q.step0 + ran;
+            ctrl->steps_remaining = L.steps_rem;
+            ctrl->current_buffer = (uint32_t)cur;
+            ctrl->steps_run = ran;
+            if (progress) {
+                ctrl->total_energy = L.energy;
+                res_post(r, L.k2h_tail, L.k2h_head, L.dropped, 1u, 0u, q.step0 + ran, L.steps_rem,
+                         L.energy, 0u);
+            }
+        }
+    }
+    // ---- leaving (persistent_fdtd.rs:942-978): final energy on TERMINATE
+    if (op == kResExitTerm) {
+        double e = 0.0;
+        if (res_energy<TY>(r, q.buf[cur] + q.a.plane, &e, &s_ok)) {
+            if (leader) L.energy = (float)e;
+        } else {
+            op = 0xFFu;
+        }
+    }
+    if (leader) {
+        ctrl->current_step = q.step0 + ran;
+        ctrl->steps_remaining = L.steps_rem;
+        ctrl->current_buffer = (uint32_t)cur;
+        ctrl->steps_run = ran;
+        ctrl->total_energy = L.energy;
+        ctrl->messages_processed = L.msgs;
+        ctrl->exit_reason = op == kResExitTerm ? 1u : (op == kResExitIdle ? 2u : 3u);
+        if (op == kResExitTerm)
+            res_post(r, L.k2h_tail, L.k2h_head, L.dropped, 3u, 0u, q.step0 + ran, 0u, L.energy, 0u);
+        ctrl->k2h_dropped = L.dropped;
+        __threadfence_system();
+        ctrl->has_terminated = 1u;
+    }
+}
+
 }  // namespace ws3d

@@ -1,14 +1,17 @@
-"""PersistentBackend: many steps per launch, mirroring the reference API.
+"""PersistentBackend: a resident kernel driven by commands, mirroring the
+reference API.
 
 Reference: crates/ringkernel-wavesim3d/src/simulation/persistent_backend.rs
-(config :86-131, stats :133-167, backend :174-446).  The reference keeps one
-kernel alive for the whole simulation and feeds it commands through mapped
-host memory, with a host poll loop and a 10 s timeout.  Here every `step`
-call is one cooperative launch that runs all requested steps on the device
-(ws3d_step_persistent) and returns when they are done; the device-side grid
-barrier and neighbour waits are bounded, so a stuck launch ends with a
-TimeoutError_ instead of a host-side timeout.  Results are bit-identical to
-GpuBackend3D.step_n.
+(config :86-131, stats :133-167, backend :174-446) over ringkernel-cuda
+persistent.rs.  As there, one kernel stays on the GPU and is driven through
+queues in pinned mapped host memory: `step` sends RUN_STEPS and polls the
+control block until the kernel reports the target step (10 s timeout),
+`inject_impulse` sends INJECT_IMPULSE, `poll_responses` drains the
+kernel-to-host queue (PROGRESS every progress_interval steps, with the
+energy), `shutdown` sends TERMINATE.  The C-ABI is ws3d_resident_*.  The
+kernel runs the same cell body as GpuBackend3D.step_n, so fields are
+bit-identical.  Its waits are bounded: an idle kernel leaves after
+idle_budget_s and is relaunched by the next call that has work for it.
 """
 from __future__ import annotations
 
@@ -16,23 +19,28 @@ import enum
 from dataclasses import dataclass, field
 from typing import List, Optional, Tuple
 
+import ctypes as C
+
 import numpy as np
 
+from . import _ffi
 from .backend import GpuBackend3D
 from .grid import SimulationGrid3D
 
 
 @dataclass
 class PersistentBackendConfig:
-    """persistent_backend.rs:86-131.  tile_size and the queue capacities are
-    accepted for API compatibility; the kernel picks its own tiling (128 x 8
-    cells per CTA row block, z-chunks balanced over the co-resident CTAs)."""
+    """persistent_backend.rs:86-131.  tile_size and use_cooperative are
+    accepted for API compatibility (the kernel picks its own tiling: 128 x 8
+    cells per CTA row block, z-chunks balanced over the co-resident CTAs; the
+    launch is always cooperative).  Queue capacities are powers of two."""
 
     tile_size: Tuple[int, int, int] = (8, 8, 8)
     use_cooperative: bool = True
     progress_interval: int = 100
     h2k_capacity: int = 256
     k2h_capacity: int = 256
+    idle_budget_s: float = 1.0
 
     def with_tile_size(self, tx: int, ty: int, tz: int) -> "PersistentBackendConfig":
         self.tile_size = (tx, ty, tz)
@@ -77,56 +85,69 @@ class PersistentBackend:
                  sponge_width: int = 0, sponge_max: float = 0.0):
         """persistent_backend.rs:187-248: device state for `grid`."""
         self.config = config or PersistentBackendConfig()
-        if not self.config.use_cooperative:
-            # The reference falls back to a software barrier without a
-            # cooperative launch; this backend always launches cooperatively
-            # (the bounded software barrier is used inside that launch).
-            pass
         self._gpu = GpuBackend3D(grid, device=device, variant="zstream",
                                  sponge_width=sponge_width, sponge_max=sponge_max)
-        self._grid_dims = grid.dimensions()
         self.started = False
-        self._terminated = False
-        self._messages = 0
-        self._responses: List[tuple] = []
-        self._energy = 0.0
 
     @property
     def backend(self) -> GpuBackend3D:
         return self._gpu
 
-    def start(self) -> None:
-        """persistent_backend.rs:253-264."""
-        self.started = True
-        self._terminated = False
+    def _chk(self, st: int, what: str) -> None:
+        self._gpu._chk(st, what)
 
-    def step(self, grid: SimulationGrid3D, steps: int) -> None:
-        """persistent_backend.rs:269-336: run `steps` steps and wait for them."""
+    def start(self) -> None:
+        """persistent_backend.rs:253-264: launch the resident kernel."""
+        if self.started:
+            return
+        c = self.config
+        cfg = _ffi.ws3d_resident_config(progress_interval=int(c.progress_interval),
+                                        h2k_capacity=int(c.h2k_capacity),
+                                        k2h_capacity=int(c.k2h_capacity),
+                                        idle_budget_ns=int(c.idle_budget_s * 1e9))
+        b = self._gpu
+        self._chk(b._lib.ws3d_resident_start(b._ctx, C.byref(cfg)), "PersistentBackend::start")
+        self.started = True
+
+    def send(self, cmd: int, *, cmd_id: int = 0, param1: int = 0, param2: int = 0,
+             param3: int = 0, param4: float = 0.0, param5: float = 0.0) -> None:
+        """Enqueue one H2K command (persistent_fdtd.rs:257-264 codes)."""
+        if not self.started:
+            self.start()
+        m = _ffi.ws3d_h2k_msg(cmd=cmd, cmd_id=cmd_id, param1=param1, param2=param2,
+                              param3=param3, param4=param4, param5=param5)
+        b = self._gpu
+        self._chk(b._lib.ws3d_resident_send(b._ctx, C.byref(m)), "PersistentBackend::send")
+
+    def step(self, grid: SimulationGrid3D, steps: int, timeout_s: float = 10.0) -> None:
+        """persistent_backend.rs:269-336: RUN_STEPS, then wait for the kernel
+        to report the target step (10 s timeout like the reference)."""
         if not self.started:
             self.start()
         b = self._gpu
-        done = 0
-        interval = max(1, int(self.config.progress_interval))
-        while done < steps:
-            # one launch per progress interval: progress and energy are reported
-            # at the same cadence as the reference kernel (persistent_fdtd.rs:883-908)
-            n = min(interval, steps - done)
-            b._chk(b._lib.ws3d_step_persistent(b._ctx, int(n)), "PersistentBackend::step")
-            done += n
-            self._messages += 1
-        b.sync()
-        cur = b.stats()["step"]
-        self._energy = b.energy()
-        self._responses.append((ResponseType.ACK, cur, 0, 0.0))
-        self._responses.append((ResponseType.ENERGY, cur, 0, float(np.float32(self._energy))))
+        target = self.stats().current_step + int(steps)
+        self._chk(b._lib.ws3d_resident_run_steps(b._ctx, int(steps)), "PersistentBackend::step")
+        self._chk(b._lib.ws3d_resident_wait_step(b._ctx, target, int(timeout_s * 1e9)),
+                  "PersistentBackend::step")
         grid.advance_clock(steps)
 
     def inject_impulse(self, x: int, y: int, z: int, amplitude: float) -> None:
-        """persistent_backend.rs:339-356."""
+        """persistent_backend.rs:339-356 (INJECT_IMPULSE; p += a, p_prev += a/2)."""
         if not self.started:
             self.start()
-        self._gpu.inject_impulse(x, y, z, amplitude)
-        self._messages += 1
+        b = self._gpu
+        self._chk(b._lib.ws3d_resident_inject_impulse(b._ctx, x, y, z, np.float32(amplitude)),
+                  "PersistentBackend::inject_impulse")
+
+    def pause(self) -> None:
+        self.send(_ffi.WS3D_CMD_PAUSE)
+
+    def resume(self) -> None:
+        self.send(_ffi.WS3D_CMD_RESUME)
+
+    def request_progress(self, cmd_id: int = 0) -> None:
+        """GET_PROGRESS: the kernel answers with a PROGRESS message."""
+        self.send(_ffi.WS3D_CMD_GET_PROGRESS, cmd_id=cmd_id)
 
     def reset(self, grid: SimulationGrid3D) -> None:
         """persistent_backend.rs:359-367 shuts the kernel down; here the device
@@ -134,41 +155,64 @@ class PersistentBackend:
         self.shutdown()
         self._gpu.reset(grid)
 
-    def download_pressure(self, grid: SimulationGrid3D) -> None:
-        """persistent_backend.rs:370-393 (nothing to download before start)."""
+    def download_pressure(self, grid: SimulationGrid3D, timeout_s: float = 10.0) -> None:
+        """persistent_backend.rs:370-393 (nothing to download before start):
+        waits until the kernel ran every requested step, copies while it stays
+        resident."""
         if not self.started:
             return
-        self._gpu.download_pressure(grid)
+        out = np.empty(self._gpu.n_local, dtype=np.float32)
+        b = self._gpu
+        self._chk(b._lib.ws3d_resident_download(b._ctx, out.ctypes.data_as(C.POINTER(C.c_float)),
+                                                int(timeout_s * 1e9)),
+                  "PersistentBackend::download_pressure")
+        grid.pressure[:] = out
 
     def stats(self) -> PersistentBackendStats:
-        """persistent_backend.rs:396-400."""
-        st = self._gpu.stats()
-        return PersistentBackendStats(current_step=int(st["step"]), steps_remaining=0,
-                                      total_energy=float(np.float32(self._energy)),
-                                      messages_processed=self._messages,
-                                      has_terminated=self._terminated,
-                                      is_running=self.is_running())
+        """persistent_backend.rs:396-400 (the mapped control block)."""
+        st = _ffi.ws3d_resident_stats()
+        b = self._gpu
+        self._chk(b._lib.ws3d_resident_stats_get(b._ctx, C.byref(st)), "PersistentBackend::stats")
+        return PersistentBackendStats(current_step=int(st.current_step),
+                                      steps_remaining=int(st.steps_remaining),
+                                      total_energy=float(st.total_energy),
+                                      messages_processed=int(st.messages_processed),
+                                      has_terminated=bool(st.has_terminated),
+                                      is_running=self.started and bool(st.is_running))
 
     def poll_responses(self) -> List[tuple]:
         """persistent_backend.rs:403-419: (type, step, steps_remaining, energy)."""
-        out, self._responses = self._responses, []
-        return out
+        buf = (_ffi.ws3d_k2h_msg * 256)()
+        n = C.c_uint32(0)
+        out: List[tuple] = []
+        b = self._gpu
+        while True:
+            self._chk(b._lib.ws3d_resident_poll(b._ctx, buf, 256, C.byref(n)),
+                      "PersistentBackend::poll_responses")
+            for k in range(n.value):
+                m = buf[k]
+                t = m.resp_type
+                out.append((ResponseType(t) if t <= 4 else ResponseType.ACK, int(m.step),
+                            int(m.steps_remaining), float(m.energy)))
+            if n.value < 256:
+                return out
 
     def shutdown(self) -> None:
-        """persistent_backend.rs:422-433."""
+        """persistent_backend.rs:422-433: TERMINATE and wait for the kernel."""
         if not self.started:
             return
-        self._gpu.sync()
+        b = self._gpu
         self.started = False
-        self._terminated = True
-        self._responses.append((ResponseType.TERMINATED, self._gpu.stats()["step"], 0, 0.0))
+        self._chk(b._lib.ws3d_resident_shutdown(b._ctx, 0), "PersistentBackend::shutdown")
 
     def is_running(self) -> bool:
-        return self.started
+        return self.started and self.stats().is_running
 
     def close(self) -> None:
-        self.shutdown()
-        self._gpu.close()
+        try:
+            self.shutdown()
+        finally:
+            self._gpu.close()
 
     def __del__(self):
         try:

@@ -71,6 +71,11 @@ def test_ctx_struct_layout():
     from rustcompute_b200 import _ffi
     assert C.sizeof(_ffi.ws3d_desc) == 56
     assert C.sizeof(_ffi.ws3d_stats) == 72
+    # resident mode: the reference host's 64-byte messages (ringkernel-cuda persistent.rs)
+    assert C.sizeof(_ffi.ws3d_h2k_msg) == 64
+    assert C.sizeof(_ffi.ws3d_k2h_msg) == 64
+    assert C.sizeof(_ffi.ws3d_resident_config) == 56
+    assert C.sizeof(_ffi.ws3d_resident_stats) == 88
 
 
 def test_no_cpu_fallback_in_package():

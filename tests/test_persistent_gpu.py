@@ -98,8 +98,9 @@ def test_persistent_backend_api_restated():
     assert pb.is_running() and grid.step == 60
     st = pb.stats()
     assert st.current_step == 60 and st.steps_remaining == 0 and st.total_energy > 0
-    resp = pb.poll_responses()
-    assert (ResponseType.ENERGY in [r[0] for r in resp]) and pb.poll_responses() == []
+    resp = pb.poll_responses()   # PROGRESS every 25 steps, with the energy
+    assert [r[1] for r in resp if r[0] == ResponseType.PROGRESS] == [25, 50]
+    assert all(r[3] > 0 for r in resp) and pb.poll_responses() == []
     pb.inject_impulse(10, 10, 10, 0.5)
     pb.step(grid, 10)
     pb.download_pressure(grid)
