@@ -57,9 +57,11 @@ def parse():
     ap.add_argument("--variant", default="auto",
                     help="auto (TMA pipeline on one GPU, z-stream for z-slabs), tma, zstream, "
                          "naive, refshape")
-    ap.add_argument("--mode", default="step", choices=["step", "persistent"],
+    ap.add_argument("--mode", default="step", choices=["step", "persistent", "resident"],
                     help="step: one launch per step (library-timed); persistent: all K steps "
-                         "in one cooperative launch (config 5)")
+                         "in one cooperative launch (config 5); resident: one resident kernel "
+                         "driven by a RUN_STEPS command (host wall clock from the command to "
+                         "the kernel reporting the last step; one GPU)")
     ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
                     help="N > 1: weak (default) keeps one D-plane slab of the recipe per GPU "
                          "(grid W x H x D*N, as BASELINE config 4's weak scaling); strong "
@@ -266,6 +268,8 @@ def pinned(a):
 def kernel_name(variant, wl, world, mode="step"):
     if mode == "persistent":
         return "k_persistent"
+    if mode == "resident":
+        return "k_resident"
     if variant == "auto":   # mirrors the library's choice for the default face layout
         tma_ok = wl.W > 128 and wl.H >= 16
         two_step = world == 1 and tma_ok and len(wl.sources) <= 32 and wl.sponge_width <= 64
@@ -322,6 +326,16 @@ def run_ours(args, wl):
     # on the launch stream; the library also times every step-kernel launch.
     b.step_n(None, max(args.warmup, 3))
     b.sync()
+    if args.mode == "resident":
+        if world != 1:
+            raise SystemExit("--mode resident runs on one GPU")
+        from rustcompute_b200 import _ffi
+        import ctypes as C
+        cfg = _ffi.ws3d_resident_config(progress_interval=1 << 62, idle_budget_ns=2_000_000_000)
+        b._chk(b._lib.ws3d_resident_start(b._ctx, C.byref(cfg)), "resident_start")
+        st0 = b.stats()["step"]
+        b._chk(b._lib.ws3d_resident_run_steps(b._ctx, max(args.warmup, 3)), "run_steps")
+        b._chk(b._lib.ws3d_resident_wait_step(b._ctx, st0 + max(args.warmup, 3), 0), "wait")
     launches0 = b.stats()["kernel_launches"]
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -329,7 +343,18 @@ def run_ours(args, wl):
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clk:
         e0.record(stream)
-        if args.mode == "persistent":
+        if args.mode == "resident":
+            rs = _ffi.ws3d_resident_stats()
+            b._chk(b._lib.ws3d_resident_stats_get(b._ctx, C.byref(rs)), "resident_stats")
+            t0 = time.perf_counter()
+            b._chk(b._lib.ws3d_resident_run_steps(b._ctx, args.steps), "run_steps")
+            b._chk(b._lib.ws3d_resident_wait_step(b._ctx, rs.current_step + args.steps, 0),
+                   "wait")
+            host_ms = (time.perf_counter() - t0) * 1e3
+            b._chk(b._lib.ws3d_resident_shutdown(b._ctx, 0), "resident_shutdown")
+            e1.record(stream)
+            kernel_ms = None
+        elif args.mode == "persistent":
             b.step_persistent(args.steps)
             e1.record(stream)
             b.sync()
@@ -340,11 +365,11 @@ def run_ours(args, wl):
         torch.cuda.synchronize(dev)
     barrier()
     launches = b.stats()["kernel_launches"] - launches0
-    total_ms = max_over_ranks(e0.elapsed_time(e1))
+    total_ms = max_over_ranks(host_ms if args.mode == "resident" else e0.elapsed_time(e1))
     value = wl.cells * args.steps / (total_ms * 1e-3) / 1e6
 
-    if kernel_ms is None:   # persistent: the one launch is the whole timed region
-        kernel_ms = e0.elapsed_time(e1)
+    if kernel_ms is None:   # persistent / resident: the one launch is the whole timed region
+        kernel_ms = total_ms
     bpc = wl.bytes_per_cell_step
     kname = kernel_name(args.variant, wl, world, args.mode)
     if kname == "k_step_tma2" and args.mode == "step":
@@ -383,6 +408,9 @@ def run_ours(args, wl):
                          % (wl.cells * 4 // 2 ** 20)},
         "us_per_step": total_ms * 1e3 / args.steps,
         "mode": args.mode,
+        "timing": ("host wall clock from the RUN_STEPS command to the kernel reporting the last "
+                   "step (the resident kernel owns the stream)") if args.mode == "resident"
+                  else "CUDA events on the launch stream",
         "roofline": roofline,
         "clocks": clk.summary(),
         "gpu_launches": int(launches),

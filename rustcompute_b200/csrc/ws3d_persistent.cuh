@@ -189,11 +189,13 @@ struct ResidentArgs {
 
 // The leader thread's copy of the control state, in shared memory so that
 // the other threads do not carry it in registers through the step.
+constexpr uint32_t kResMaxPending = 64;  // impulses queued between two barriers
 struct ResLeader {
     uint64_t steps_rem, msgs, dropped, h2k_head, k2h_tail, k2h_head;
     unsigned long long idle_t0;
-    uint32_t paused, term;
+    uint32_t paused, term, npend;
     float energy;
+    uint4 pend[kResMaxPending];  // (x, y, z, amplitude bits)
 };
 
 enum : unsigned int { kResIdle = 0, kResStep = 1, kResExitTerm = 2, kResExitIdle = 3 };
@@ -298,6 +300,7 @@ __global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
         L.steps_rem = ctrl->steps_remaining;
         L.paused = ctrl->paused;
         L.term = 0;
+        L.npend = 0;
         L.msgs = ctrl->messages_processed;
         L.dropped = ctrl->k2h_dropped;
         L.energy = ctrl->total_energy;
@@ -308,89 +311,122 @@ __global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
     }
     int cur = 0;           // role of the pressure buffer (0 = q.buf[0] at launch)
     uint64_t ran = 0;      // steps run by this launch (same on every CTA)
-    unsigned int op = kResIdle;
-    for (;;) {
-        if (leader) {
-            // ---- commands (persistent_fdtd.rs:769-810)
-            const uint64_t tail = ld_acquire_sys_u64(&r.h2k->tail);
-            while (L.h2k_head != tail) {
-                const uint4* src = r.h2k_slots[L.h2k_head & r.h2k_mask].q;
-                const uint4 m0 = ld_volatile_v4(src), m1 = ld_volatile_v4(src + 1),
-                            m2 = ld_volatile_v4(src + 2);
-                const uint32_t cmd = m0.x;
-                const uint64_t cmd_id = (uint64_t)m0.z | ((uint64_t)m0.w << 32);
-                const uint64_t param1 = (uint64_t)m1.x | ((uint64_t)m1.y << 32);
-                const uint32_t param2 = m1.z;
-                const float param4 = __uint_as_float(m2.x);
-                ++L.h2k_head;
-                ++L.msgs;
-                switch (cmd) {
-                    case 0: break;                                   // NOP
-                    case 1: L.steps_rem += param1; break;            // RUN_STEPS
-                    case 2: L.paused = 1; break;                     // PAUSE
-                    case 3: L.paused = 0; break;                     // RESUME
-                    case 4: L.term = 1; break;                       // TERMINATE
-                    case 5: {                                        // INJECT_IMPULSE
-                        const uint32_t ix = (uint32_t)(param1 >> 32), iy = (uint32_t)param1;
-                        const uint32_t iz = param2;
-                        if (ix < q.a.W && iy < q.a.H && iz < q.a.Dg) {
-                            const uint64_t off = (uint64_t)(iz + 1) * q.a.plane +
-                                                 (uint64_t)iy * q.a.pitch + ix;
-                            float* pc = q.buf[cur] + off;
-                            float* pp = q.buf[cur ^ 1] + off;
-                            *pc = __fadd_rn(*pc, param4);
-                            *pp = __fadd_rn(*pp, __fmul_rn(param4, 0.5f));
-                        }
-                        break;
-                    }
-                    case 7:                                          // GET_PROGRESS
-                        res_post(r, L.k2h_tail, L.k2h_head, L.dropped, 1u, cmd_id, q.step0 + ran,
-                                 L.steps_rem, L.energy, 0u);
-                        break;
-                    default:                                         // SET_SOURCE, unknown
-                        res_post(r, L.k2h_tail, L.k2h_head, L.dropped, 2u, cmd_id, q.step0 + ran,
-                                 L.steps_rem, L.energy, cmd);
-                        break;
-                }
+    unsigned int op = kResIdle, pre = 0;
+    uint64_t tail_hint = 0;  // leader: H2K tail read at the start of the step (relaxed)
+
+    // Leader: drain the H2K commands up to `tail` and decide what the grid
+    // does next (persistent_fdtd.rs:769-823).  Impulses are queued and applied
+    // after the next grid barrier, when no CTA is computing.
+    auto decide = [&](uint64_t tail) {
+        if (tail != L.h2k_head) asm volatile("fence.acq_rel.sys;" ::: "memory");
+        while (L.h2k_head != tail) {
+            const uint4* src = r.h2k_slots[L.h2k_head & r.h2k_mask].q;
+            const uint4 m0 = ld_volatile_v4(src), m1 = ld_volatile_v4(src + 1),
+                        m2 = ld_volatile_v4(src + 2);
+            const uint32_t cmd = m0.x;
+            if (cmd == 5u && L.npend == kResMaxPending) break;  // full: leave it queued
+            const uint64_t cmd_id = (uint64_t)m0.z | ((uint64_t)m0.w << 32);
+            const uint64_t param1 = (uint64_t)m1.x | ((uint64_t)m1.y << 32);
+            ++L.h2k_head;
+            ++L.msgs;
+            switch (cmd) {
+                case 0: break;                                   // NOP
+                case 1: L.steps_rem += param1; break;            // RUN_STEPS
+                case 2: L.paused = 1; break;                     // PAUSE
+                case 3: L.paused = 0; break;                     // RESUME
+                case 4: L.term = 1; break;                       // TERMINATE
+                case 5:                                          // INJECT_IMPULSE
+                    L.pend[L.npend++] = make_uint4((uint32_t)(param1 >> 32), (uint32_t)param1, m1.z,
+                                                   m2.x);
+                    break;
+                case 7:                                          // GET_PROGRESS
+                    res_post(r, L.k2h_tail, L.k2h_head, L.dropped, 1u, cmd_id, q.step0 + ran,
+                             L.steps_rem, L.energy, 0u);
+                    break;
+                default:                                         // SET_SOURCE, unknown
+                    res_post(r, L.k2h_tail, L.k2h_head, L.dropped, 2u, cmd_id, q.step0 + ran,
+                             L.steps_rem, L.energy, cmd);
+                    break;
             }
-            st_release_sys_u64(&r.h2k->head, L.h2k_head);
-            ctrl->paused = L.paused;
-            ctrl->steps_remaining = L.steps_rem;
-            ctrl->messages_processed = L.msgs;
-            if (L.term) {
-                op = kResExitTerm;
-            } else if (L.steps_rem > 0 && !L.paused) {
-                op = kResStep;
-                L.idle_t0 = global_ns();
-            } else if (global_ns() - L.idle_t0 > r.idle_budget_ns) {
-                op = kResExitIdle;
-            } else {
-                op = kResIdle;
-                __nanosleep(20000);
+        }
+        st_release_sys_u64(&r.h2k->head, L.h2k_head);
+        ctrl->paused = L.paused;
+        ctrl->steps_remaining = L.steps_rem;
+        ctrl->messages_processed = L.msgs;
+        unsigned int next;
+        if (L.term) {
+            next = kResExitTerm;
+        } else if (L.steps_rem > 0 && !L.paused) {
+            next = kResStep;
+            L.idle_t0 = global_ns();
+        } else if (global_ns() - L.idle_t0 > r.idle_budget_ns && L.h2k_head == tail) {
+            next = kResExitIdle;
+        } else {
+            next = kResIdle;
+        }
+        *reinterpret_cast<volatile unsigned int*>(r.decision) = next | (L.npend ? 0x100u : 0u);
+    };
+    // Leader: the queued impulses, in command order (ws3d_inject_impulse's
+    // semantics: p += a, p_prev += a/2).
+    auto apply_pending = [&]() {
+        for (uint32_t k = 0; k < L.npend; ++k) {
+            const uint4 e = L.pend[k];
+            if (e.x < q.a.W && e.y < q.a.H && e.z < q.a.Dg) {
+                const uint64_t off =
+                    (uint64_t)(e.z + 1) * q.a.plane + (uint64_t)e.y * q.a.pitch + e.x;
+                float* pc = q.buf[cur] + off;
+                float* pp = q.buf[cur ^ 1] + off;
+                const float amp = __uint_as_float(e.w);
+                *pc = __fadd_rn(*pc, amp);
+                *pp = __fadd_rn(*pp, __fmul_rn(amp, 0.5f));
             }
-            *reinterpret_cast<volatile unsigned int*>(r.decision) = op;
         }
-        if (!grid_barrier(q.bar_count, q.bar_gen, nb, q.a.budget_ns, q.a.status, &s_ok)) {
-            op = 0xFFu;
-            break;
-        }
+        L.npend = 0;
+    };
+    // Barrier that also hands the leader's decision to every thread.
+    auto barrier_decision = [&]() -> bool {
+        if (!grid_barrier(q.bar_count, q.bar_gen, nb, q.a.budget_ns, q.a.status, &s_ok))
+            return false;
         if (threadIdx.x == 0 && threadIdx.y == 0)
             s_op = *reinterpret_cast<volatile unsigned int*>(r.decision);
         __syncthreads();
-        op = s_op;
-        if (op == kResExitTerm || op == kResExitIdle) break;
-        if (op != kResStep) continue;
+        op = s_op & 0xFFu;
+        pre = s_op >> 8;
+        return true;
+    };
 
-        // ---- one step (k_persistent's body, one GPU)
+    if (leader) decide(ld_acquire_sys_u64(&r.h2k->tail));
+    bool ok = barrier_decision();
+    while (ok) {
+        if (pre && leader) apply_pending();
+        if (op == kResExitTerm || op == kResExitIdle) {
+            // the final energy reads the impulses just applied
+            if (pre && !grid_barrier(q.bar_count, q.bar_gen, nb, q.a.budget_ns, q.a.status, &s_ok))
+                ok = false;
+            break;
+        }
+        if (op != kResStep) {  // idle: sleep, poll again
+            if (leader) {
+                __nanosleep(20000);
+                decide(ld_acquire_sys_u64(&r.h2k->tail));
+            }
+            ok = barrier_decision();
+            continue;
+        }
+
+        // ---- one step (k_persistent's body, one GPU); one grid barrier, plus
+        // one when sources or queued impulses must land first
+        if (leader)  // read ahead: the PCIe round trip overlaps the step
+            tail_hint = *reinterpret_cast<volatile const uint64_t*>(&r.h2k->tail);
         StepParams a = q.a;
         a.p = q.buf[cur] + a.plane;
         a.pp = q.buf[cur ^ 1] + a.plane;
-        if (q.n_src) {
-            if (leader)
+        if (q.n_src || pre) {
+            if (leader && q.n_src)
                 inject_sources_dev(q.buf[cur], q.buf[cur ^ 1], q.src_off, q.wavelet, q.n_src,
                                    q.wl_len, q.step0 + ran, nullptr, nullptr, nullptr);
             if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok)) {
-                op = 0xFFu;
+                ok = false;
                 break;
             }
         }
@@ -401,15 +437,12 @@ __global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
         }
         cur ^= 1;
         ++ran;
-        if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok)) {
-            op = 0xFFu;
-            break;
-        }
         const bool progress = (q.step0 + ran) % interval == 0;
-        if (progress) {
+        if (progress) {  // every CTA's writes of the step, then sum p^2
             double e = 0.0;
-            if (!res_energy<TY>(r, q.buf[cur] + a.plane, &e, &s_ok)) {
-                op = 0xFFu;
+            if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok) ||
+                !res_energy<TY>(r, q.buf[cur] + a.plane, &e, &s_ok)) {
+                ok = false;
                 break;
             }
             if (leader) L.energy = (float)e;
@@ -425,8 +458,11 @@ __global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
                 res_post(r, L.k2h_tail, L.k2h_head, L.dropped, 1u, 0u, q.step0 + ran, L.steps_rem,
                          L.energy, 0u);
             }
+            decide(tail_hint);
         }
+        ok = barrier_decision();  // end of the step: every CTA's writes, the decision
     }
+    if (!ok) op = 0xFFu;
     // ---- leaving (persistent_fdtd.rs:942-978): final energy on TERMINATE
     if (op == kResExitTerm) {
         double e = 0.0;
