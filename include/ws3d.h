@@ -431,6 +431,43 @@ WS3D_API ws3d_status ws3d_resident_download(ws3d_ctx *ctx, float *pressure, uint
  * and buffer roles follow the steps the kernel ran). */
 WS3D_API ws3d_status ws3d_resident_shutdown(ws3d_ctx *ctx, uint64_t timeout_ns);
 
+/* ---------------------------------------------------------------------------
+ * Headless volume ray-march of the pressure field (one context holding the
+ * whole grid).  Restates the reference's volume renderer
+ * (visualization/volume.rs:76-160 shader, :396-420 update_volume; camera
+ * camera.rs:51-61, 98-110) without a graphics pipeline: the field is
+ * normalised by max(max|p|, 0.001) and stored as f16, each pixel's primary
+ * ray is marched through the box [0, grid_size] with linear filtering and
+ * clamp-to-edge sampling, blue-white-red colour mapping and front-to-back
+ * compositing, and RGBA floats are returned.  Every operation is a separately
+ * rounded f32 operation, so the CPU restatement in oracle/ matches bit for
+ * bit.
+ * ------------------------------------------------------------------------- */
+typedef struct ws3d_volume_params {
+    uint32_t width, height;   /* image size in pixels */
+    float density_scale;      /* VolumeParams::density_scale, 2.0 */
+    float step_size;          /* world units per march step, 0.05 */
+    uint32_t max_steps;       /* 256 */
+    float threshold;          /* |p| below it is transparent, 0.01 */
+    float cell_size;          /* grid_size = (W, H, D) * cell_size (world units), 1.0 */
+    float fov_y;              /* radians, pi/4 */
+    float eye[3];             /* camera position */
+    float target[3];          /* look-at point */
+    float up[3];              /* (0, 1, 0) */
+    uint32_t default_camera;  /* 1: Camera3D::for_grid (camera.rs:51-61); eye and target ignored */
+    float background[4];      /* target colour when composite = 1 */
+    uint32_t composite;       /* 0: the fragment output (RGBA, 0 where discarded);
+                                 1: BlendState::ALPHA_BLENDING over background */
+    uint32_t reserved[3];
+} ws3d_volume_params;
+
+/* Defaults of VolumeParams (volume.rs:180-190) and Camera3D::for_grid. */
+WS3D_API void ws3d_volume_params_init(ws3d_volume_params *p, uint32_t width, uint32_t height);
+/* Render into rgba (host, width * height * 4 floats, row-major, row 0 at the
+ * top).  Keeps a W x H x D f16 copy and the image buffer on the device. */
+WS3D_API ws3d_status ws3d_render_volume(ws3d_ctx *ctx, const ws3d_volume_params *params,
+                                        float *rgba);
+
 #ifdef __cplusplus
 }
 #endif

@@ -64,8 +64,57 @@ def lib() -> C.CDLL:
         L.ws3o_max_pressure.argtypes = [vp, C.c_uint64]
         L.ws3o_max_pressure.restype = f32
         L.ws3o_max_threads.restype = C.c_int
+        L.ws3o_render_volume.argtypes = [vp, u32, u32, u32, vp, vp]
+        L.ws3o_render_volume.restype = C.c_int
+        L.ws3o_quantize_f16.argtypes = [vp, C.c_uint64, vp]
         _lib = L
     return _lib
+
+
+class _VolumeParams(C.Structure):
+    """Layout of ws3o_volume_params (the same fields as ws3d_volume_params)."""
+    _fields_ = [
+        ("width", C.c_uint32), ("height", C.c_uint32), ("density_scale", C.c_float),
+        ("step_size", C.c_float), ("max_steps", C.c_uint32), ("threshold", C.c_float),
+        ("cell_size", C.c_float), ("fov_y", C.c_float), ("eye", C.c_float * 3),
+        ("target", C.c_float * 3), ("up", C.c_float * 3), ("default_camera", C.c_uint32),
+        ("background", C.c_float * 4), ("composite", C.c_uint32), ("reserved", C.c_uint32 * 3),
+    ]
+
+
+def render_volume(p: np.ndarray, W: int, H: int, D: int, width: int = 640, height: int = 360, *,
+                  density_scale: float = 2.0, step_size: float = 0.05, max_steps: int = 256,
+                  threshold: float = 0.01, cell_size: float = 1.0, fov_y: float = None, eye=None,
+                  target=None, up=(0.0, 1.0, 0.0), background=None) -> np.ndarray:
+    """CPU restatement of the volume ray-march (visualization/volume.rs:76-160,
+    :396-420; camera.rs:51-61): float32 RGBA image (height, width, 4)."""
+    prm = _VolumeParams(width=int(width), height=int(height), density_scale=density_scale,
+                        step_size=step_size, max_steps=int(max_steps), threshold=threshold,
+                        cell_size=cell_size,
+                        fov_y=np.float32(0.785398163397448309616) if fov_y is None else fov_y)
+    prm.default_camera = 1 if eye is None else 0
+    if eye is not None:
+        prm.eye[:] = [float(v) for v in eye]
+        prm.target[:] = [float(v) for v in target]
+    prm.up[:] = [float(v) for v in up]
+    if background is not None:
+        prm.composite = 1
+        prm.background[:] = [float(v) for v in background]
+    f = np.ascontiguousarray(p, dtype=np.float32).reshape(-1)
+    assert f.size == W * H * D
+    out = np.empty((int(height), int(width), 4), dtype=np.float32)
+    if lib().ws3o_render_volume(f.ctypes.data_as(C.c_void_p), W, H, D, C.byref(prm),
+                                out.ctypes.data_as(C.c_void_p)) != 0:
+        raise ValueError("render_volume: degenerate camera")
+    return out
+
+
+def quantize_f16(x: np.ndarray) -> np.ndarray:
+    """The renderer's f32 -> f16 (round to nearest even) -> f32."""
+    f = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    out = np.empty_like(f)
+    lib().ws3o_quantize_f16(f.ctypes.data_as(C.c_void_p), f.size, out.ctypes.data_as(C.c_void_p))
+    return out
 
 
 def _ptr(a):

@@ -312,3 +312,213 @@ int ws3o_max_threads(void) {
     return 1;
 #endif
 }
+
+/* ---------------------------------------------------------------------------
+ * Volume ray-march (visualization/volume.rs:76-160 shader, :396-420
+ * update_volume; camera camera.rs:51-61, 98-110), restated on the CPU with
+ * the operations of the CUDA renderer in the same order, so that the images
+ * agree bit for bit.  Test infrastructure only.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+    uint32_t width, height;
+    float density_scale, step_size;
+    uint32_t max_steps;
+    float threshold, cell_size, fov_y;
+    float eye[3], target[3], up[3];
+    uint32_t default_camera;
+    float background[4];
+    uint32_t composite;
+    uint32_t reserved[3];
+} ws3o_volume_params;
+
+/* IEEE binary16 round-to-nearest-even (the half crate's f16::from_f32 and
+ * CUDA's __float2half_rn); finite inputs of magnitude <= 65504 suffice here. */
+static uint16_t f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t ex = (x >> 23) & 0xffu;
+    uint32_t mant = x & 0x7fffffu;
+    if (ex == 0xffu) return (uint16_t)(sign | 0x7c00u | (mant ? 0x200u : 0u));
+    const int e = (int)ex - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        mant |= 0x800000u;
+        const int shift = 14 - e;
+        uint32_t h = mant >> shift;
+        const uint32_t rem = mant & ((1u << shift) - 1u), halfway = 1u << (shift - 1);
+        if (rem > halfway || (rem == halfway && (h & 1u))) ++h;
+        return (uint16_t)(sign | h);
+    }
+    uint32_t h = sign | ((uint32_t)e << 10) | (mant >> 13);
+    const uint32_t rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+    return (uint16_t)h;
+}
+
+static float f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t ex = (h >> 10) & 0x1fu, mant = h & 0x3ffu;
+    uint32_t x;
+    if (ex == 0) {
+        if (mant == 0) {
+            x = sign;
+        } else {  /* subnormal: mant * 2^-24, exact in f32 */
+            float v = (float)mant * 5.9604644775390625e-8f;
+            memcpy(&x, &v, 4);
+            x |= sign;
+        }
+    } else if (ex == 31) {
+        x = sign | 0x7f800000u | (mant << 13);
+    } else {
+        x = sign | ((ex - 15 + 127) << 23) | (mant << 13);
+    }
+    float f;
+    memcpy(&f, &x, 4);
+    return f;
+}
+
+static float lerp_rn(float a, float b, float t) { return a * (1.0f - t) + b * t; }
+
+static float vol_sample(const float *vol, uint32_t W, uint32_t H, uint32_t D, float u, float w_,
+                        float s) {
+    const float cx = u * (float)W - 0.5f, cy = w_ * (float)H - 0.5f, cz = s * (float)D - 0.5f;
+    const float x0f = floorf(cx), y0f = floorf(cy), z0f = floorf(cz);
+    const float fx = cx - x0f, fy = cy - y0f, fz = cz - z0f;
+    const int x0 = (int)x0f, y0 = (int)y0f, z0 = (int)z0f;
+#define CL(v, n) ((v) < 0 ? 0 : ((v) > (int)(n) - 1 ? (int)(n) - 1 : (v)))
+    const int xa = CL(x0, W), xb = CL(x0 + 1, W), ya = CL(y0, H), yb = CL(y0 + 1, H);
+    const int za = CL(z0, D), zb = CL(z0 + 1, D);
+#undef CL
+#define V(x, y, z) vol[((size_t)(z) * H + (y)) * W + (x)]
+    const float c00 = lerp_rn(V(xa, ya, za), V(xb, ya, za), fx);
+    const float c10 = lerp_rn(V(xa, yb, za), V(xb, yb, za), fx);
+    const float c01 = lerp_rn(V(xa, ya, zb), V(xb, ya, zb), fx);
+    const float c11 = lerp_rn(V(xa, yb, zb), V(xb, yb, zb), fx);
+#undef V
+    return lerp_rn(lerp_rn(c00, c10, fy), lerp_rn(c01, c11, fy), fz);
+}
+
+/* p: W x H x D z-major field; rgba: width x height x 4.  Returns 0 or -1
+ * (eye == target, or up parallel to the view). */
+int ws3o_render_volume(const float *p, uint32_t W, uint32_t H, uint32_t D,
+                       const ws3o_volume_params *prm, float *rgba) {
+    const size_t n = (size_t)W * H * D;
+    float mx = 0.0f;
+    for (size_t i = 0; i < n; ++i) mx = fmaxf(mx, fabsf(p[i]));
+    const float m = fmaxf(mx, 0.001f);
+    float *vol = (float *)malloc(n * sizeof(float));
+    if (!vol) return -1;
+    for (size_t i = 0; i < n; ++i) vol[i] = f16_to_f32(f32_to_f16(p[i] / m));
+
+    const float gx = (float)W * prm->cell_size, gy = (float)H * prm->cell_size;
+    const float gz = (float)D * prm->cell_size;
+    float eye[3], tgt[3];
+    if (prm->default_camera) {
+        const float cx = gx / 2.0f, cy = gy / 2.0f, cz = gz / 2.0f;
+        const float dist = fmaxf(fmaxf(gx, gz) * 1.5f, 5.0f);
+        eye[0] = cx + dist;
+        eye[1] = cy + dist * 0.7f;
+        eye[2] = cz + dist;
+        tgt[0] = cx;
+        tgt[1] = cy;
+        tgt[2] = cz;
+    } else {
+        for (int k = 0; k < 3; ++k) {
+            eye[k] = prm->eye[k];
+            tgt[k] = prm->target[k];
+        }
+    }
+    float f[3] = {tgt[0] - eye[0], tgt[1] - eye[1], tgt[2] - eye[2]};
+    float len = sqrtf(f[0] * f[0] + f[1] * f[1] + f[2] * f[2]);
+    if (!(len > 0.0f)) {
+        free(vol);
+        return -1;
+    }
+    for (int k = 0; k < 3; ++k) f[k] = f[k] / len;
+    const float *up = prm->up;
+    float r[3] = {f[1] * up[2] - f[2] * up[1], f[2] * up[0] - f[0] * up[2],
+                  f[0] * up[1] - f[1] * up[0]};
+    len = sqrtf(r[0] * r[0] + r[1] * r[1] + r[2] * r[2]);
+    if (!(len > 0.0f)) {
+        free(vol);
+        return -1;
+    }
+    for (int k = 0; k < 3; ++k) r[k] = r[k] / len;
+    const float u[3] = {r[1] * f[2] - r[2] * f[1], r[2] * f[0] - r[0] * f[2],
+                        r[0] * f[1] - r[1] * f[0]};
+    const float tan_half = (float)tan((double)prm->fov_y * 0.5);
+    const float aspect = (float)prm->width / (float)prm->height;
+    const float bmax[3] = {gx, gy, gz};
+
+    for (uint32_t j = 0; j < prm->height; ++j)
+        for (uint32_t i = 0; i < prm->width; ++i) {
+            const float xn = ((2.0f * ((float)i + 0.5f)) / (float)prm->width - 1.0f) * tan_half *
+                             aspect;
+            const float yn = (1.0f - (2.0f * ((float)j + 0.5f)) / (float)prm->height) * tan_half;
+            float d[3];
+            for (int k = 0; k < 3; ++k) d[k] = (f[k] + r[k] * xn) + u[k] * yn;
+            const float dl = sqrtf((d[0] * d[0] + d[1] * d[1]) + d[2] * d[2]);
+            for (int k = 0; k < 3; ++k) d[k] = d[k] / dl;
+            float tn = -INFINITY, tf = INFINITY;
+            for (int k = 0; k < 3; ++k) {
+                const float inv = 1.0f / d[k];
+                const float t1 = (0.0f - eye[k]) * inv, t2 = (bmax[k] - eye[k]) * inv;
+                tn = fmaxf(tn, fminf(t1, t2));
+                tf = fminf(tf, fmaxf(t1, t2));
+            }
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            int hit = !(tn > tf || tf < 0.0f);
+            if (hit) {
+                float t = fmaxf(tn, 0.0f);
+                for (uint32_t steps = 0; !(t >= tf || steps >= prm->max_steps || acc[3] >= 0.95f);
+                     ++steps) {
+                    float uvw[3];
+                    for (int k = 0; k < 3; ++k) uvw[k] = (eye[k] + d[k] * t) / bmax[k];
+                    const float pr = vol_sample(vol, W, H, D, uvw[0], uvw[1], uvw[2]);
+                    if (fabsf(pr) > prm->threshold) {
+                        const float pc = fminf(fmaxf(pr, -1.0f), 1.0f);
+                        float cr, cg, cb;
+                        if (pc >= 0.0f) {
+                            cr = 1.0f;
+                            cg = 1.0f - pc;
+                            cb = 1.0f - pc;
+                        } else {
+                            cr = 1.0f + pc;
+                            cg = 1.0f + pc;
+                            cb = 1.0f;
+                        }
+                        const float sa = fabsf(pc) * prm->density_scale;
+                        const float alpha = sa * (1.0f - acc[3]);
+                        acc[0] = acc[0] + cr * alpha;
+                        acc[1] = acc[1] + cg * alpha;
+                        acc[2] = acc[2] + cb * alpha;
+                        acc[3] = acc[3] + alpha;
+                    }
+                    t = t + prm->step_size;
+                }
+                if (acc[3] < 0.01f) hit = 0;
+            }
+            float *o = rgba + ((size_t)j * prm->width + i) * 4;
+            if (!hit) acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+            if (prm->composite) {
+                if (!hit) {
+                    for (int k = 0; k < 4; ++k) o[k] = prm->background[k];
+                } else {
+                    const float ia = 1.0f - acc[3];
+                    for (int k = 0; k < 3; ++k) o[k] = acc[k] * acc[3] + prm->background[k] * ia;
+                    o[3] = acc[3] + prm->background[3] * ia;
+                }
+            } else {
+                for (int k = 0; k < 4; ++k) o[k] = acc[k];
+            }
+        }
+    free(vol);
+    return 0;
+}
+
+/* f32 -> f16 (round to nearest even) -> f32, for tests of the quantiser. */
+void ws3o_quantize_f16(const float *in, uint64_t n, float *out) {
+    for (uint64_t i = 0; i < n; ++i) out[i] = f16_to_f32(f32_to_f16(in[i]));
+}

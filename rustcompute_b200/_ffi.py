@@ -157,6 +157,26 @@ class ws3d_resident_stats(C.Structure):
     ]
 
 
+class ws3d_volume_params(C.Structure):
+    _fields_ = [
+        ("width", C.c_uint32),
+        ("height", C.c_uint32),
+        ("density_scale", C.c_float),
+        ("step_size", C.c_float),
+        ("max_steps", C.c_uint32),
+        ("threshold", C.c_float),
+        ("cell_size", C.c_float),
+        ("fov_y", C.c_float),
+        ("eye", C.c_float * 3),
+        ("target", C.c_float * 3),
+        ("up", C.c_float * 3),
+        ("default_camera", C.c_uint32),
+        ("background", C.c_float * 4),
+        ("composite", C.c_uint32),
+        ("reserved", C.c_uint32 * 3),
+    ]
+
+
 _P = C.c_void_p
 _F = C.POINTER(C.c_float)
 _U8 = C.POINTER(C.c_uint8)
@@ -211,6 +231,8 @@ SIGNATURES = {
     "ws3d_resident_stats_get": (C.c_int, [_CTX, C.POINTER(ws3d_resident_stats)]),
     "ws3d_resident_download": (C.c_int, [_CTX, _F, C.c_uint64]),
     "ws3d_resident_shutdown": (C.c_int, [_CTX, C.c_uint64]),
+    "ws3d_volume_params_init": (None, [C.POINTER(ws3d_volume_params), C.c_uint32, C.c_uint32]),
+    "ws3d_render_volume": (C.c_int, [_CTX, C.POINTER(ws3d_volume_params), _F]),
 }
 
 _lib = None

@@ -326,6 +326,41 @@ class GpuBackend3D:
         self._chk(self._lib.ws3d_get_stream(self._ctx, C.byref(out)), "get_stream")
         return int(out.value or 0)
 
+    def volume_params(self, width: int = 640, height: int = 360, *, density_scale: float = 2.0,
+                      step_size: float = 0.05, max_steps: int = 256, threshold: float = 0.01,
+                      cell_size: float = 1.0, fov_y: Optional[float] = None, eye=None,
+                      target=None, up=(0.0, 1.0, 0.0), background=None):
+        """VolumeParams (volume.rs:166-190) plus the camera (camera.rs): the
+        default camera is Camera3D::for_grid; `background` (RGBA) turns on
+        ALPHA_BLENDING compositing."""
+        prm = _ffi.ws3d_volume_params()
+        self._lib.ws3d_volume_params_init(C.byref(prm), int(width), int(height))
+        prm.density_scale = density_scale
+        prm.step_size = step_size
+        prm.max_steps = int(max_steps)
+        prm.threshold = threshold
+        prm.cell_size = cell_size
+        if fov_y is not None:
+            prm.fov_y = fov_y
+        if eye is not None:
+            prm.default_camera = 0
+            prm.eye[:] = [float(v) for v in eye]
+            prm.target[:] = [float(v) for v in target]
+        prm.up[:] = [float(v) for v in up]
+        if background is not None:
+            prm.composite = 1
+            prm.background[:] = [float(v) for v in background]
+        return prm
+
+    def render_volume(self, width: int = 640, height: int = 360, **kw) -> np.ndarray:
+        """Headless volume ray-march of the current pressure (volume.rs:76-160):
+        float32 RGBA image of shape (height, width, 4), row 0 at the top."""
+        prm = self.volume_params(width, height, **kw)
+        out = np.empty((int(height), int(width), 4), dtype=np.float32)
+        self._chk(self._lib.ws3d_render_volume(self._ctx, C.byref(prm), _fptr(out)),
+                  "render_volume")
+        return out
+
     def stats(self) -> dict:
         s = _ffi.ws3d_stats()
         self._chk(self._lib.ws3d_stats_get(self._ctx, C.byref(s)), "stats")

@@ -10,6 +10,7 @@
 #include "ws3d_persistent.cuh"
 #include "ws3d_tb.cuh"
 #include "ws3d_tma.cuh"
+#include "ws3d_volume.cuh"
 
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -122,6 +123,12 @@ struct ws3d_ctx {
     int res_role[2] = {0, 1};      // field buffers of roles 0 / 1 of the current launch
     uint64_t res_step0 = 0;        // step count at the current launch
     int res_resident = 0;          // co-resident CTAs of k_resident
+
+    // volume rendering: normalised f16 copy of the field and the image
+    __half* vol16 = nullptr;
+    size_t vol_elems = 0;
+    float4* img = nullptr;
+    size_t img_elems = 0;
 };
 
 namespace {
@@ -879,6 +886,8 @@ void ws3d_destroy(ws3d_ctx* c) {
         dfree(c, c->flags, kFlagWords);
         for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
         for (cudaEvent_t ev : c->tev) cudaEventDestroy(ev);
+        dfree(c, c->vol16, c->vol_elems);
+        dfree(c, c->img, c->img_elems);
         if (c->res_mem) cudaFreeHost(c->res_mem);
         if (c->res_done) cudaEventDestroy(c->res_done);
         if (c->res_side) cudaStreamDestroy(c->res_side);
@@ -1972,6 +1981,133 @@ ws3d_status ws3d_resident_shutdown(ws3d_ctx* c, uint64_t timeout_ns) {
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
     if (s != WS3D_OK && s != WS3D_ECOMMAND) return s;
     return check_device_status(c);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Volume rendering (ws3d_volume.cuh).
+// ---------------------------------------------------------------------------
+extern "C" {
+
+void ws3d_volume_params_init(ws3d_volume_params* p, uint32_t width, uint32_t height) {
+    if (!p) return;
+    std::memset(p, 0, sizeof *p);
+    p->width = width;
+    p->height = height;
+    p->density_scale = 2.0f;  // volume.rs:180-190
+    p->step_size = 0.05f;
+    p->max_steps = 256;
+    p->threshold = 0.01f;
+    p->cell_size = 1.0f;
+    p->fov_y = 0.785398163397448309616f;  // FRAC_PI_4 (camera.rs:32)
+    p->up[1] = 1.0f;
+    p->default_camera = 1;
+}
+
+ws3d_status ws3d_render_volume(ws3d_ctx* c, const ws3d_volume_params* prm, float* rgba) {
+    WS3D_NOT_RESIDENT(c);
+    if (!c) return WS3D_EINVAL;
+    if (!prm || !rgba) return fail(c, WS3D_EINVAL, "render_volume: NULL argument");
+    if (prm->width == 0 || prm->height == 0 || prm->width > 16384 || prm->height > 16384 ||
+        !(prm->step_size > 0.0f) || !(prm->cell_size > 0.0f) || prm->max_steps > (1u << 20) ||
+        !(prm->fov_y > 0.0f && prm->fov_y < 3.1f))
+        return fail(c, WS3D_EINVAL, "render_volume: bad parameters");
+    if (c->nz != c->Dg)
+        return fail(c, WS3D_EINVAL, "render_volume needs the whole grid on this context");
+    DeviceGuard g(c->desc.device);
+    ws3d_status s;
+    const size_t n = (size_t)c->W * c->H * c->Dg;
+    if (c->vol_elems != n) {
+        dfree(c, c->vol16, c->vol_elems);
+        c->vol_elems = 0;
+        if ((s = dalloc(c, &c->vol16, n, "volume (f16)")) != WS3D_OK) return s;
+        c->vol_elems = n;
+    }
+    const size_t npix = (size_t)prm->width * prm->height;
+    if (c->img_elems != npix) {
+        dfree(c, c->img, c->img_elems);
+        c->img_elems = 0;
+        if ((s = dalloc(c, &c->img, npix, "volume image")) != WS3D_OK) return s;
+        c->img_elems = npix;
+    }
+    // update_volume (volume.rs:396-420): max |p| on the device, then p / max as f16
+    const uint64_t rows = (uint64_t)c->nz * c->H;
+    float* part = reinterpret_cast<float*>(c->red_scratch);
+    float* mx = reinterpret_cast<float*>(c->red_scratch + c->red_blocks);
+    k_maxabs_partials<<<c->red_blocks, kRedThreads, 0, c->stream>>>(owned0(c, c->buf[c->ip]), c->W,
+                                                                     c->pitch, rows, part);
+    if ((s = check_launch(c, "k_maxabs_partials")) != WS3D_OK) return s;
+    k_fold_max<<<1, kRedThreads, 0, c->stream>>>(part, c->red_blocks, mx);
+    if ((s = check_launch(c, "k_fold_max")) != WS3D_OK) return s;
+    k_volume_normalize<<<c->red_blocks, 256, 0, c->stream>>>(owned0(c, c->buf[c->ip]), c->W, c->H,
+                                                             c->Dg, c->pitch, c->plane, mx,
+                                                             c->vol16);
+    if ((s = check_launch(c, "k_volume_normalize")) != WS3D_OK) return s;
+
+    // camera (camera.rs:51-61 for_grid, :98-110 look_at_rh / perspective_rh),
+    // f32 operations in this order (the CPU restatement repeats them)
+    VolumeArgs v{};
+    v.vol = c->vol16;
+    v.W = c->W;
+    v.H = c->H;
+    v.D = c->Dg;
+    v.gx = (float)c->W * prm->cell_size;
+    v.gy = (float)c->H * prm->cell_size;
+    v.gz = (float)c->Dg * prm->cell_size;
+    float eye[3], tgt[3];
+    if (prm->default_camera) {
+        const float cx = v.gx / 2.0f, cy = v.gy / 2.0f, cz = v.gz / 2.0f;
+        const float dist = std::max(std::max(v.gx, v.gz) * 1.5f, 5.0f);
+        eye[0] = cx + dist;
+        eye[1] = cy + dist * 0.7f;
+        eye[2] = cz + dist;
+        tgt[0] = cx;
+        tgt[1] = cy;
+        tgt[2] = cz;
+    } else {
+        for (int k = 0; k < 3; ++k) {
+            eye[k] = prm->eye[k];
+            tgt[k] = prm->target[k];
+        }
+    }
+    float f[3] = {tgt[0] - eye[0], tgt[1] - eye[1], tgt[2] - eye[2]};
+    float len = std::sqrt(f[0] * f[0] + f[1] * f[1] + f[2] * f[2]);
+    if (!(len > 0.0f)) return fail(c, WS3D_EINVAL, "render_volume: eye == target");
+    for (float& q : f) q = q / len;
+    const float* up = prm->up;
+    float r[3] = {f[1] * up[2] - f[2] * up[1], f[2] * up[0] - f[0] * up[2],
+                  f[0] * up[1] - f[1] * up[0]};
+    len = std::sqrt(r[0] * r[0] + r[1] * r[1] + r[2] * r[2]);
+    if (!(len > 0.0f)) return fail(c, WS3D_EINVAL, "render_volume: up is parallel to the view");
+    for (float& q : r) q = q / len;
+    const float u[3] = {r[1] * f[2] - r[2] * f[1], r[2] * f[0] - r[0] * f[2],
+                        r[0] * f[1] - r[1] * f[0]};
+    for (int k = 0; k < 3; ++k) {
+        v.eye[k] = eye[k];
+        v.fwd[k] = f[k];
+        v.right[k] = r[k];
+        v.upv[k] = u[k];
+    }
+    v.tan_half = (float)std::tan((double)prm->fov_y * 0.5);
+    v.aspect = (float)prm->width / (float)prm->height;
+    v.density_scale = prm->density_scale;
+    v.step_size = prm->step_size;
+    v.threshold = prm->threshold;
+    v.max_steps = prm->max_steps;
+    v.width = prm->width;
+    v.height = prm->height;
+    for (int k = 0; k < 4; ++k) v.bg[k] = prm->background[k];
+    v.composite = prm->composite;
+    v.out = c->img;
+    const dim3 blk(16, 16), grd((prm->width + 15) / 16, (prm->height + 15) / 16);
+    k_volume_render<<<grd, blk, 0, c->stream>>>(v);
+    if ((s = check_launch(c, "k_volume_render")) != WS3D_OK) return s;
+    WS3D_CUDA(c, cudaMemcpyAsync(rgba, c->img, npix * sizeof(float4), cudaMemcpyDeviceToHost,
+                                 c->stream),
+              WS3D_EREADBACK);
+    WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EREADBACK);
+    return WS3D_OK;
 }
 
 }  // extern "C"
