@@ -194,6 +194,19 @@ __device__ __forceinline__ float4 cells4_fixup(float4 v, bool sponge, const floa
     return v;
 }
 
+// Branch-free sponge: v_k *= min(fx_k, fz) for all four cells (a factor of
+// exactly 1.0f outside the sponge leaves v unchanged), then cells that are
+// not interior (mask bit clear) become p_prev * 0.1.
+__device__ __forceinline__ float4 cells4_finish(float4 v, const float (&fx)[4], float fz,
+                                               uint32_t m, float4 PV) {
+    f2 lo = mul2(pk(v.x, v.y), pk(fminf(fx[0], fz), fminf(fx[1], fz)));
+    f2 hi = mul2(pk(v.z, v.w), pk(fminf(fx[2], fz), fminf(fx[3], fz)));
+    upk(lo, v.x, v.y);
+    upk(hi, v.z, v.w);
+    if (m != 0xFu) v = cells4_fixup(v, false, fx, fz, m, PV);
+    return v;
+}
+
 // One cell (scalar), same rule.
 __device__ __forceinline__ float cell1_lean(bool interior, float f, float w, float e, float s,
                                             float n, float dn, float up, float c, float pv, float c2,

@@ -22,8 +22,9 @@
 // the shared halo array, p_prev = A(q-1) from registers.  One named barrier
 // per item (consumer warps only) orders the shared X planes: slot q&1 is
 // written in item i and read in item i+1.  Cells use the lean rule of
-// ws3d_lean.cuh (packed f32x2, same bits as the one-step kernels); lanes
-// with sponge or boundary cells take a fix-up branch.  The item loop is
+// ws3d_lean.cuh (packed f32x2, same bits as the one-step kernels): the sponge
+// factor is applied to every cell (1.0 outside it), lanes with boundary
+// cells take a fix-up branch.  The item loop is
 // unrolled three times so that the z queues rotate by renaming registers
 // instead of moving them.
 //
@@ -221,7 +222,6 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         const uint32_t x = x0 + 4u * lane;
         const uint32_t y = y0 + (uint32_t)w - 1u;  // wraps for y0 = 0, w = 0: not a grid row
         const LeanRow lr = make_lean_row(x, y, a);
-        const float fxmin = fminf(fminf(lr.fx[0], lr.fx[1]), fminf(lr.fx[2], lr.fx[3]));
         const bool act = do_y && x < a.pitch && y < a.H;
         const int64_t row = (int64_t)y * a.pitch + x;  // + q * plane
         // halo cell of this lane (hlane only); x / y may wrap: not interior.
@@ -267,8 +267,11 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         // Item i >= 2: X(q), q = zs-3+i, from A(q-1) = a_m, A(q) = a_c and the
         // staged A(q+1) (kept in a_p); then Y(q-1) from X(q-2) = x_m,
         // X(q-1) = x_c and X(q) (kept in x_n).  Halo lanes: h_m, h_c, h_p.
-        auto body = [&](int i, float4& a_m, float4& a_c, float4& a_p, float4& x_m, float4& x_c,
-                        float4& x_n, float& h_m, float& h_c, float& h_p) -> bool {
+        // kSrc (compile time): the tile holds a source, so the sources of step
+        // t+1 are looked up; other tiles skip that code entirely.
+        auto body = [&](auto src_tag, int i, float4& a_m, float4& a_c, float4& a_p, float4& x_m,
+                        float4& x_c, float4& x_n, float& h_m, float& h_c, float& h_p) -> bool {
+            constexpr bool kSrc = decltype(src_tag)::value;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph));
             if (ok) {
                 const int q = zs - 3 + i;
@@ -296,10 +299,8 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     if (lane == 0) wl = ed;
                     if (lane == 31) er = ed;
                     float4 xv = cells4_fast(wl, er, sv, nv, a_m, a_c, a_p, bv, cq, damp);
-                    const uint32_t m = zin ? lr.bits : 0u;
-                    const bool sp_lane = fz < 1.0f || fxmin < 1.0f;
-                    if (sp_lane || m != 0xFu) xv = cells4_fixup(xv, sp_lane, lr.fx, fz, m, bv);
-                    if (tile_src) {  // sources of step t+1: X += a, in source order
+                    xv = cells4_finish(xv, lr.fx, fz, zin ? lr.bits : 0u, bv);
+                    if (kSrc) {  // sources of step t+1: X += a, in source order
                         const int4 sc = has_src ? srcs[lane] : make_int4(0, -1, -1, 0);
                         unsigned mk = __ballot_sync(0xffffffffu, sc.z == q && sc.y == (int)y);
                         while (mk) {
@@ -322,7 +323,7 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                                             Ap[hr - R], Ap[hr + R], h_m, h_p, h_c, Bq[br],
                                             kC2F ? Cq[br] : a.c2, a.damping);
                         }
-                        if (tile_src) {
+                        if (kSrc) {
                             const int hx = (int)(hside ? x0 + 128u : x0 - 1u);
                             const int hy = (int)(y0 + (uint32_t)hrow - 1u);
                             const int4 sc = has_src ? srcs[lane] : make_int4(0, -1, -1, 0);
@@ -355,7 +356,7 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     if (lane == 0) wl = eh;
                     if (lane == 31) er = eh;
                     float4 pv = a_m;  // A(q-1)
-                    if (tile_src) {  // sources of step t+1: p_prev += a/2
+                    if (kSrc) {  // sources of step t+1: p_prev += a/2
                         const int4 sc = has_src ? srcs[lane] : make_int4(0, -1, -1, 0);
                         unsigned mk = __ballot_sync(0xffffffffu, sc.z == qy && sc.y == (int)y);
                         while (mk) {
@@ -370,9 +371,8 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     const uint32_t zgy = a.z0 + (uint32_t)qy;
                     const float fzy = fz_of(zgy);
                     float4 yv = cells4_fast(wl, er, sv, nv, x_m, x_c, x_n, pv, c2y, damp);
-                    const uint32_t my = (zgy >= 1 && zgy + 1 < a.Dg) ? lr.bits : 0u;
-                    const bool spy = fzy < 1.0f || fxmin < 1.0f;
-                    if (spy || my != 0xFu) yv = cells4_fixup(yv, spy, lr.fx, fzy, my, pv);
+                    yv = cells4_finish(yv, lr.fx, fzy, (zgy >= 1 && zgy + 1 < a.Dg) ? lr.bits : 0u,
+                                       pv);
                     if (act) st4(g.Y + zs_plane(qy, P) + row, yv);
                 }
             }
@@ -381,16 +381,22 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
         float4 am = z4, ac = z4, ap = z4, xm = z4, xc = z4, xn = z4;
         float hm = 0.f, hc = 0.f, hp = 0.f;
+        auto run_items = [&](auto src_tag) -> bool {
+            bool ab = false;
+            int i = 2;
+            const int last = n + 3;
+            for (; !ab && i + 2 <= last; i += 3) {
+                ab = body(src_tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
+                     body(src_tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
+                     body(src_tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
+            }
+            if (!ab && i <= last) ab = body(src_tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
+            if (!ab && i <= last) ab = body(src_tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
+            return ab;
+        };
         bool abort = prologue(am, hm, false) || prologue(ac, hc, true);
-        int i = 2;
-        const int last = n + 3;
-        for (; !abort && i + 2 <= last; i += 3) {
-            abort = body(i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
-                    body(i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
-                    body(i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
-        }
-        if (!abort && i <= last) abort = body(i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
-        if (!abort && i <= last) abort = body(i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
+        if (!abort)
+            abort = tile_src ? run_items(std::true_type{}) : run_items(std::false_type{});
         if (abort) {
             if (threadIdx.x == 0) atomicOr(a.status, 4u);
             return;  // every consumer thread saw the same vote
