@@ -92,7 +92,7 @@ struct ws3d_ctx {
     bool tma_maps = false, tma_c2_map = false;
     bool tb_buffers = false;   // buffers 2 and 3 allocated, their maps encoded
     bool tb_failed = false;    // their allocation failed: run single steps
-    int tma_grid[2] = {0, 0};  // co-resident CTAs without / with c2
+    int tma_grid[4] = {0, 0, 0, 0};  // co-resident CTAs: [c2 field + 2 * lean rule]
     int tb_grid[2] = {0, 0};
     uint64_t tb_launches = 0;
     int async_grid[2] = {0, 0};
@@ -345,19 +345,19 @@ bool tma_eligible(const ws3d_ctx* c) {
     return c->cells_default && c->tma_maps && (!c->c2f || c->tma_c2_map);
 }
 
-template <bool kC2F>
-ws3d_status launch_tma(ws3d_ctx* c, const StepParams& a) {
+template <bool kC2F, bool kLean>
+ws3d_status launch_tma_t(ws3d_ctx* c, const StepParams& a) {
     using L = TmaLayout<kTmaTY, kC2F>;
     constexpr int kThreads = 32 * (kTmaTY + 1);
     const int smem = L::smem_bytes(kTmaStages);
-    int& grid = c->tma_grid[kC2F ? 1 : 0];
+    auto kern = k_step_tma<kC2F, kTmaTY, kLean>;
+    int& grid = c->tma_grid[(kC2F ? 1 : 0) + (kLean ? 2 : 0)];
     if (grid == 0) {
-        cudaError_t e = cudaFuncSetAttribute(k_step_tma<kC2F, kTmaTY>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(c, WS3D_ELAUNCH, e, "cudaFuncSetAttribute(tma)");
         int per_sm = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step_tma<kC2F, kTmaTY>,
-                                                          kThreads, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
         if (e != cudaSuccess || per_sm < 1)
             return cuda_fail(c, WS3D_ELAUNCH, e, "occupancy(tma)");
         grid = per_sm * std::max(1, c->sm_count);
@@ -369,9 +369,14 @@ ws3d_status launch_tma(ws3d_ctx* c, const StepParams& a) {
         tma_schedule(tiles, c->nz, (uint32_t)grid, c->halo ? std::min(16u, c->tma_min_chunk)
                                                            : c->tma_min_chunk);
     const int P = c->ip, T = c->ipp;
-    k_step_tma<kC2F, kTmaTY><<<sch.grid, kThreads, smem, c->stream>>>(
-        c->mapP[P], c->mapT[T], c->mapC2, a, tiles_x, tiles, sch.clen, sch.nitems);
+    kern<<<sch.grid, kThreads, smem, c->stream>>>(c->mapP[P], c->mapT[T], c->mapC2, a, tiles_x,
+                                                  tiles, sch.clen, sch.nitems);
     return check_launch(c, "k_step_tma");
+}
+
+template <bool kC2F>
+ws3d_status launch_tma(ws3d_ctx* c, const StepParams& a) {
+    return c->sponge_monotone ? launch_tma_t<kC2F, true>(c, a) : launch_tma_t<kC2F, false>(c, a);
 }
 
 // ---- two steps per launch (one GPU, default face layout) --------------------

@@ -35,6 +35,7 @@
 #include <cuda.h>
 
 #include "ws3d_kernels.cuh"
+#include "ws3d_lean.cuh"
 
 namespace ws3d {
 
@@ -120,7 +121,9 @@ __device__ __forceinline__ bool next_run(uint32_t& item, uint32_t nitems, uint32
     return true;
 }
 
-template <bool kC2F, int TY>
+// kLean: the packed cell rule of ws3d_lean.cuh (same bits; the host picks it
+// when the sponge table is monotone), else cells4_default.
+template <bool kC2F, int TY, bool kLean>
 __global__ void __launch_bounds__(32 * (TY + 1), 3)
 k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmPP,
            const __grid_constant__ CUtensorMap tmC2, StepParams a, uint32_t tiles_x,
@@ -212,7 +215,10 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
         const uint32_t x = x0 + 4u * lane, y = y0 + w;
         const bool act = x < a.pitch && y < a.H;
         const int64_t row = (int64_t)y * a.pitch + x;
-        const XYPre xy = make_xypre(x, y, a);
+        XYPre xy{};
+        LeanRow lr{};
+        if (kLean) lr = make_lean_row(x, y, a);
+        else xy = make_xypre(x, y, a);
         const float* pmp = a.p + zs_plane((int64_t)r.zs - 1, P) + row;  // plane zs-1
         // one GPU: issue the load early; slabs: plane -1 is a ghost plane, read
         // (through L2) once the producer has waited for the neighbour
@@ -253,8 +259,15 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
             if (lane == 31) er = Pz[(w + 1) * L::kPRow + 4 + 128];
             if (act) {
                 if (!kC2F) vc2 = make_float4(a.c2, a.c2, a.c2, a.c2);
-                const float4 out = cells4_default(xy, a.z0 + z, wl, er, Sv, Nv, pm, pc, pn, vpp,
-                                                  vc2, a);
+                float4 out;
+                if (kLean) {
+                    const uint32_t zg = a.z0 + z;
+                    out = cells4_fast(wl, er, Sv, Nv, pm, pc, pn, vpp, vc2,
+                                      pk(a.damping, a.damping));
+                    out = cells4_finish(out, lr.fx, lean_fz(zg, a), lean_mask(lr.bits, zg, a), vpp);
+                } else {
+                    out = cells4_default(xy, a.z0 + z, wl, er, Sv, Nv, pm, pc, pn, vpp, vc2, a);
+                }
                 st4(a.pp + zs_plane((int64_t)z, P) + row, out);
                 if (z == 0 && a.peer_lo) st4(a.peer_lo + row, out);
                 if (z + 1 == a.nz && a.peer_hi) st4(a.peer_hi + row, out);
