@@ -265,14 +265,17 @@ def pinned(a):
     return t.numpy()
 
 
-def kernel_name(variant, wl, world, mode="step"):
+def kernel_name(variant, wl, world, mode="step", depth=1):
+    """The step kernel the library runs; on z-slabs two-step launches need
+    temporal depth 2 (`depth`, as negotiated by slab.connect)."""
     if mode == "persistent":
         return "k_persistent"
     if mode == "resident":
         return "k_resident"
-    if variant == "auto":   # mirrors the library's choice for the default face layout
+    if variant in ("auto", "tma2"):   # mirrors the library's choice for the default faces
         tma_ok = wl.W > 128 and wl.H >= 16
-        two_step = world == 1 and tma_ok and len(wl.sources) <= 32 and wl.sponge_width <= 64
+        two_step = (world == 1 or depth == 2) and tma_ok and len(wl.sources) <= 32 and \
+            wl.sponge_width <= 64
         variant = "tma2" if two_step else ("tma" if tma_ok else "zstream")
     return {"tma": "k_step_tma", "tma2": "k_step_tma2", "async": "k_step_async",
             "zstream": "k_step_zstream",
@@ -318,9 +321,10 @@ def run_ours(args, wl):
 
     b = open_backend()
     upload_inputs(b, wl, p0, pp0, c20)
+    depth = 1   # steps per halo exchange on z-slabs
     if world > 1:
         from rustcompute_b200.slab import connect
-        connect(b, rank, world, pg.all_gather_object, barrier)
+        depth = connect(b, rank, world, pg.all_gather_object, barrier)
 
     # Warm-up (>= 3 steps), then the timed region: K steps between two events
     # on the launch stream; the library also times every step-kernel launch.
@@ -371,7 +375,7 @@ def run_ours(args, wl):
     if kernel_ms is None:   # persistent / resident: the one launch is the whole timed region
         kernel_ms = total_ms
     bpc = wl.bytes_per_cell_step
-    kname = kernel_name(args.variant, wl, world, args.mode)
+    kname = kernel_name(args.variant, wl, world, args.mode, depth)
     if kname == "k_step_tma2" and args.mode == "step":
         # K // 2 two-step launches (+ one single step for odd K)
         n_launch = args.steps // 2 + args.steps % 2
@@ -386,14 +390,14 @@ def run_ours(args, wl):
     achieved = total_bytes / (kernel_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"],
-                "traffic": ncu_traffic(wl, kernel_name(args.variant, wl, world)),
+                "traffic": ncu_traffic(wl, kernel_name(args.variant, wl, world, depth=depth)),
                 "algorithmic_bytes_per_launch": alg_bytes,
                 "steps_per_launch": 2 if kname == "k_step_tma2" and args.mode == "step" else 1,
                 "bytes_per_cell_step": bpc,
                 "kernel_avg_ms": avg_kernel_ms,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"
                                if peaks["source"] == "measured" else "fallback",
-                "kernel": kernel_name(args.variant, wl, world, args.mode),
+                "kernel": kernel_name(args.variant, wl, world, args.mode, depth),
                 "rank": rank}
 
     result = {
@@ -404,6 +408,7 @@ def run_ours(args, wl):
         "config": {"workload": wl.name, "grid": [wl.W, wl.H, wl.D], "variant": args.variant,
                    "heterogeneous": wl.heterogeneous, "sponge": wl.sponge_width,
                    "sources": int(len(wl.sources)), "decomposition": f"z-slabs x{world}",
+                   "halo_depth": depth,
                    "l2": "inputs larger than L2 (each field %d MiB > 126 MB)"
                          % (wl.cells * 4 // 2 ** 20)},
         "us_per_step": total_ms * 1e3 / args.steps,

@@ -277,16 +277,33 @@ WS3D_API ws3d_status ws3d_stats_get(const ws3d_ctx *ctx, ws3d_stats *out);
  * Protocol (every rank, same order):
  *   create with desc.z_begin/z_end -> upload -> ws3d_halo_export -> exchange
  *   the handles (e.g. all_gather) -> ws3d_halo_attach(lower, upper) ->
- *   ws3d_halo_sync(0) -> barrier -> ws3d_halo_sync(1) -> barrier -> steps.
+ *   [ws3d_halo_set_depth(2) when every rank's export has WS3D_HALO_CAP_TWO_STEP]
+ *   -> ws3d_halo_sync(0) -> barrier -> ws3d_halo_sync(1) -> barrier -> steps.
  * After any upload/reset, repeat the two ws3d_halo_sync phases.
+ *
+ * Temporal depth 2 (two steps per exchange): the field buffers of a z-slab
+ * carry two ghost planes per side.  Each pair of steps runs k_step_tma2,
+ * which also computes p_{t+1} on the first ghost plane of each side (from two
+ * ghost planes of p_t and the neighbour's own p_{t-1} and c2 plane, read over
+ * NVLink) and stores p_{t+2} of its two first / last planes into the
+ * neighbours' ghost planes; single steps (odd counts) store two planes too.
+ * Every rank takes the same sequence of one- and two-step launches (the
+ * choice depends only on the step count and on state all ranks share), so
+ * the buffer roles stay aligned across ranks.
  * ------------------------------------------------------------------------- */
+#define WS3D_HALO_CAP_TWO_STEP 1u  /* four field buffers exported, two-step capable */
+#define WS3D_HALO_CAP_C2_FIELD 2u  /* a c2 field is exported */
+
 typedef struct ws3d_halo_handles {
-    uint8_t buf[2][64];   /* cudaIpcMemHandle_t of both field buffers */
+    uint8_t buf[4][64];   /* cudaIpcMemHandle_t of the field buffers (2, 3: two-step capable) */
     uint8_t flags[64];    /* cudaIpcMemHandle_t of the flag block */
+    uint8_t c2[64];       /* cudaIpcMemHandle_t of the c2 field (WS3D_HALO_CAP_C2_FIELD) */
     uint32_t width, height, depth, pitch;
     uint32_t z_begin, z_end;
     int32_t device;
-    uint32_t reserved;
+    uint32_t caps;        /* WS3D_HALO_CAP_* */
+    uint32_t ghost_planes;  /* ghost planes per side in the field buffers */
+    float c_squared;      /* the slab's uniform c2 (desc.c_squared) */
 } ws3d_halo_handles;
 
 /* Export this slab's buffers and flags for its neighbours. */
@@ -302,6 +319,13 @@ WS3D_API ws3d_status ws3d_halo_attach(ws3d_ctx *ctx, const ws3d_halo_handles *lo
  * splits): no device-side waits; advance them together with ws3d_step_group
  * on one shared stream. */
 WS3D_API ws3d_status ws3d_halo_attach_local(ws3d_ctx *ctx, ws3d_ctx *lower, ws3d_ctx *upper);
+
+/* Steps per exchange after attach: 1 (default) or 2 (temporal blocking).  2
+ * needs this slab and both neighbours to be two-step capable, at least two
+ * owned planes on each, and the same c2-field presence; every rank of the
+ * decomposition must set the same depth (decide it from all ranks' exports).
+ * Fails with WS3D_EINVAL otherwise.  Call before ws3d_halo_sync. */
+WS3D_API ws3d_status ws3d_halo_set_depth(ws3d_ctx *ctx, uint32_t depth);
 
 /* Phase 0: wait for this slab's stream (no signal of an earlier step stays in
  * flight).  Phase 1: clear this slab's flags, copy its first and last planes

@@ -72,10 +72,15 @@ class ws3d_stats(C.Structure):
     ]
 
 
+HALO_CAP_TWO_STEP = 1
+HALO_CAP_C2_FIELD = 2
+
+
 class ws3d_halo_handles(C.Structure):
     _fields_ = [
-        ("buf", (C.c_uint8 * 64) * 2),
+        ("buf", (C.c_uint8 * 64) * 4),
         ("flags", C.c_uint8 * 64),
+        ("c2", C.c_uint8 * 64),
         ("width", C.c_uint32),
         ("height", C.c_uint32),
         ("depth", C.c_uint32),
@@ -83,7 +88,9 @@ class ws3d_halo_handles(C.Structure):
         ("z_begin", C.c_uint32),
         ("z_end", C.c_uint32),
         ("device", C.c_int32),
-        ("reserved", C.c_uint32),
+        ("caps", C.c_uint32),
+        ("ghost_planes", C.c_uint32),
+        ("c_squared", C.c_float),
     ]
 
 
@@ -220,6 +227,7 @@ SIGNATURES = {
                                    C.POINTER(ws3d_halo_handles)]),
     "ws3d_halo_attach_local": (C.c_int, [_CTX, _CTX, _CTX]),
     "ws3d_halo_sync": (C.c_int, [_CTX, C.c_uint32]),
+    "ws3d_halo_set_depth": (C.c_int, [_CTX, C.c_uint32]),
     "ws3d_step_group": (C.c_int, [C.POINTER(_CTX), C.c_uint32, C.c_uint64]),
     "ws3d_resident_start": (C.c_int, [_CTX, C.POINTER(ws3d_resident_config)]),
     "ws3d_resident_send": (C.c_int, [_CTX, C.POINTER(ws3d_h2k_msg)]),

@@ -37,8 +37,11 @@ struct ws3d_ctx {
     size_t slab = 0;        // (nz + 2) * plane floats (ghost below + owned + ghost above)
     // Field buffers: buf[ip] = pressure, buf[ipp] = pressure_prev.  Buffers 2
     // and 3 are allocated on first use of the two-step (temporally blocked)
-    // pass, which writes both new fields into free buffers.
+    // pass, which writes both new fields into free buffers.  buf[b] points at
+    // ghost plane -1; a z-slab's field buffers hold gd = 2 ghost planes per
+    // side (allocation base buf[b] - plane), one GPU's gd = 1.
     float* buf[4] = {nullptr, nullptr, nullptr, nullptr};
+    uint32_t gd = 1;
     int ip = 0, ipp = 1;
     float* c2f = nullptr;   // slab-shaped, or nullptr
     uint8_t* types = nullptr;
@@ -52,8 +55,16 @@ struct ws3d_ctx {
     float* wavelet = nullptr;
     uint32_t n_src = 0;
     uint64_t wl_len = 0;
-    long long* src_ghost = nullptr;   // per source: (row in the neighbour's ghost plane or -1, side)
+    long long* src_ghost = nullptr;   // per source: offsets in the lower / upper neighbour's copy, or -1
     std::vector<uint32_t> src_xyz;    // local sources, global coordinates
+    // the whole source list as given (all slabs get the same one): two-step
+    // launches on z-slabs also apply the sources of the ghost planes
+    std::vector<uint32_t> gsrc_xyz;
+    std::vector<float> gsrc_wl;
+    uint32_t n_src_global = 0;
+    uint64_t* tb_src_off = nullptr;   // z-slab two-step table: sources on planes -1 .. nz
+    float* tb_wavelet = nullptr;
+    uint32_t tb_n_src = 0;
     double* red_scratch = nullptr;  // reduction partials + result
     uint32_t red_blocks = 0;
     cudaStream_t own_stream = nullptr;
@@ -68,9 +79,18 @@ struct ws3d_ctx {
     bool halo = false;               // neighbours attached
     bool host_ordered = false;       // same-device neighbours: stream order, no device waits
     bool halo_synced = false;        // ghost planes hold the neighbours' current boundary planes
-    float* lo_base[2] = {nullptr, nullptr};  // lower neighbour's buffers (mapped)
-    float* hi_base[2] = {nullptr, nullptr};  // upper neighbour's buffers (mapped)
+    // neighbours' field buffers (mapped; their plane -1), permuted together
+    // with buf[] so that index k is the neighbour's buffer in the same role
+    float* lo_base[4] = {nullptr, nullptr, nullptr, nullptr};
+    float* hi_base[4] = {nullptr, nullptr, nullptr, nullptr};
+    const float* lo_c2 = nullptr;    // neighbours' c2 fields (plane -1), or null
+    const float* hi_c2 = nullptr;
+    uint32_t lo_caps = 0, hi_caps = 0;   // WS3D_HALO_CAP_* of the neighbours
+    uint32_t lo_nz = 0, hi_nz = 0;       // their owned planes
+    float lo_c2u = 0.f, hi_c2u = 0.f;    // their uniform c2
     uint64_t lo_ghost_off = 0;       // elements from lower's buffer base to its upper ghost
+    uint32_t hdepth = 1;             // steps per exchange (ws3d_halo_set_depth)
+    bool deep_ok = false;            // neighbours' copies of our two edge planes are current
     unsigned long long* flags = nullptr;     // [0] from lower, [1] from upper, [2] status
     unsigned long long* lo_flag = nullptr;   // lower neighbour's flags[1]
     unsigned long long* hi_flag = nullptr;   // upper neighbour's flags[0]
@@ -93,7 +113,7 @@ struct ws3d_ctx {
     bool tb_buffers = false;   // buffers 2 and 3 allocated, their maps encoded
     bool tb_failed = false;    // their allocation failed: run single steps
     int tma_grid[4] = {0, 0, 0, 0};  // co-resident CTAs: [c2 field + 2 * lean rule]
-    int tb_grid[2] = {0, 0};
+    int tb_grid[4] = {0, 0, 0, 0};  // [c2 field + 2 * slab]
     uint64_t tb_launches = 0;
     int async_grid[2] = {0, 0};
     uint32_t tma_min_chunk = 32;  // WS3D_TMA_MIN_CHUNK (schedule tuning), read at create
@@ -212,6 +232,26 @@ void dfree(ws3d_ctx* c, T*& p, size_t count) {
 inline float* owned0(const ws3d_ctx* c, float* base) { return base + c->plane; }
 inline size_t owned_elems(const ws3d_ctx* c) { return (size_t)c->nz * c->plane; }
 
+// Field buffer b: one allocation of nz + 2 * gd planes, buf[b] at plane -1.
+inline size_t fbuf_elems(const ws3d_ctx* c) { return (size_t)(c->nz + 2 * c->gd) * c->plane; }
+inline float* fbuf_base(const ws3d_ctx* c, int b) {
+    return c->buf[b] ? c->buf[b] - (size_t)(c->gd - 1) * c->plane : nullptr;
+}
+ws3d_status falloc(ws3d_ctx* c, int b, const char* what) {
+    float* q = nullptr;
+    ws3d_status s = dalloc(c, &q, fbuf_elems(c), what);
+    if (s != WS3D_OK) return s;
+    c->buf[b] = q + (size_t)(c->gd - 1) * c->plane;
+    cudaError_t e = cudaMemsetAsync(q, 0, fbuf_elems(c) * sizeof(float), c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, WS3D_EMEMORY, e, "cudaMemsetAsync(field)");
+    return WS3D_OK;
+}
+void ffree(ws3d_ctx* c, int b) {
+    float* q = fbuf_base(c, b);
+    dfree(c, q, fbuf_elems(c));
+    c->buf[b] = nullptr;
+}
+
 StepParams make_params(const ws3d_ctx* c) {
     StepParams a{};
     a.p = owned0(c, c->buf[c->ip]);
@@ -234,6 +274,10 @@ StepParams make_params(const ws3d_ctx* c) {
         const int nxt = c->ipp;   // the neighbour's buffer in the same role
         a.peer_lo = c->lo_base[nxt] ? c->lo_base[nxt] + c->lo_ghost_off : nullptr;
         a.peer_hi = c->hi_base[nxt];
+        if (c->hdepth == 2) {  // the neighbours' second ghost planes too
+            a.peer_lo2 = a.peer_lo ? a.peer_lo + c->plane : nullptr;
+            a.peer_hi2 = a.peer_hi ? a.peer_hi - c->plane : nullptr;
+        }
         if (!c->host_ordered) {
             a.wait_lo = c->lo_base[0] ? c->flags + 0 : nullptr;
             a.wait_hi = c->hi_base[0] ? c->flags + 1 : nullptr;
@@ -302,12 +346,13 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 3-D map over a slab-shaped buffer: dims {pitch, H, nz+2}, fp32, zero fill.
+// 3-D map over a slab-shaped buffer: dims {pitch, H, planes} (default nz+2
+// from ghost plane -1), fp32, zero fill.
 bool encode_slab_map(const ws3d_ctx* c, CUtensorMap* m, const float* base, uint32_t box_x,
-                     uint32_t box_y) {
+                     uint32_t box_y, uint64_t planes = 0) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
     if (!enc) return false;
-    const cuuint64_t dims[3] = {c->pitch, c->H, (cuuint64_t)c->nz + 2};
+    const cuuint64_t dims[3] = {c->pitch, c->H, planes ? planes : (cuuint64_t)c->nz + 2};
     const cuuint64_t strides[2] = {(cuuint64_t)c->pitch * 4, (cuuint64_t)c->plane * 4};
     const cuuint32_t box[3] = {box_x, box_y, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
@@ -321,7 +366,9 @@ bool encode_buffer_maps(ws3d_ctx* c, int b) {
     return encode_slab_map(c, &c->mapP[b], c->buf[b], TmaLayout<kTmaTY, true>::kPRow,
                            kTmaTY + 2) &&
            encode_slab_map(c, &c->mapT[b], c->buf[b], 128, kTmaTY) &&
-           encode_slab_map(c, &c->mapA[b], c->buf[b], kTbRow, kTbTY + 4) &&
+           // two-step pressure role: every ghost plane (tensor z = plane + gd)
+           encode_slab_map(c, &c->mapA[b], fbuf_base(c, b), kTbRow, kTbTY + 4,
+                           (uint64_t)c->nz + 2 * c->gd) &&
            encode_slab_map(c, &c->mapB[b], c->buf[b], kTbRow, kTbTY + 2);
 }
 
@@ -388,14 +435,13 @@ bool ensure_tb_buffers(ws3d_ctx* c) {
     if (c->tb_buffers) return true;
     if (c->tb_failed) return false;
     for (int b = 2; b < 4; ++b) {
-        if (!c->buf[b] && dalloc(c, &c->buf[b], c->slab, "pressure (two-step)") != WS3D_OK) {
+        if (!c->buf[b] && falloc(c, b, "pressure (two-step)") != WS3D_OK) {
+            cudaGetLastError();
             c->err.clear();
             c->tb_failed = true;
             return false;
         }
-        if (cudaMemsetAsync(c->buf[b], 0, c->slab * sizeof(float), c->stream) != cudaSuccess ||
-            !encode_buffer_maps(c, b)) {
-            cudaGetLastError();
+        if (!encode_buffer_maps(c, b)) {
             c->tb_failed = true;
             return false;
         }
@@ -404,11 +450,22 @@ bool ensure_tb_buffers(ws3d_ctx* c) {
     return true;
 }
 
-bool tb_eligible(ws3d_ctx* c) {
-    return !c->halo && tma_eligible(c) && c->sponge_monotone &&
-           c->sponge_w <= (uint32_t)kTbSpongeMax &&
-           c->n_src <= (uint32_t)kTbMaxSrc &&
+// The kernel's preconditions apart from the source count.
+bool tb_kernel_ok(ws3d_ctx* c) {
+    return tma_eligible(c) && c->sponge_monotone && c->sponge_w <= (uint32_t)kTbSpongeMax &&
            (!c->c2f || c->tma_c2_map) && ensure_tb_buffers(c);
+}
+
+bool two_step_variant(const ws3d_ctx* c) {
+    return c->desc.variant == WS3D_VARIANT_TMA2 || c->desc.variant == WS3D_VARIANT_AUTO;
+}
+
+// WS3D_HALO_CAP_* of this context (allocates the two-step buffers).
+uint32_t halo_caps(ws3d_ctx* c) {
+    uint32_t caps = 0;
+    if (two_step_variant(c) && c->nz >= 2 && tb_kernel_ok(c)) caps |= WS3D_HALO_CAP_TWO_STEP;
+    if (c->c2f) caps |= WS3D_HALO_CAP_C2_FIELD;
+    return caps;
 }
 
 template <bool kC2F>
@@ -416,14 +473,16 @@ ws3d_status launch_tb(ws3d_ctx* c) {
     using L = TbLayout<kC2F>;
     constexpr int kThreads = 32 * (kTbTY + 3);
     const int smem = L::smem_bytes();
-    int& grid = c->tb_grid[kC2F ? 1 : 0];
+    // one GPU and z-slabs run separate instances (the slab code stays out
+    // of the one-GPU item loop)
+    auto kern = c->halo ? k_step_tma2<kC2F, true> : k_step_tma2<kC2F, false>;
+    int& grid = c->tb_grid[(kC2F ? 1 : 0) + (c->halo ? 2 : 0)];
     if (grid == 0) {
-        cudaError_t e = cudaFuncSetAttribute(k_step_tma2<kC2F>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(c, WS3D_ELAUNCH, e, "cudaFuncSetAttribute(tma2)");
         int per_sm = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step_tma2<kC2F>, kThreads,
-                                                          smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
         if (e != cudaSuccess || per_sm < 1)
             return cuda_fail(c, WS3D_ELAUNCH, e, "occupancy(tma2)");
         grid = per_sm * std::max(1, c->sm_count);
@@ -432,28 +491,45 @@ ws3d_status launch_tb(ws3d_ctx* c) {
     g.a = make_params(c);
     g.X = owned0(c, c->buf[2]);
     g.Y = owned0(c, c->buf[3]);
-    g.src_off = c->src_off;
-    g.wavelet = c->wavelet;
-    g.n_src = c->n_src;
+    g.src_off = c->halo ? c->tb_src_off : c->src_off;
+    g.wavelet = c->halo ? c->tb_wavelet : c->wavelet;
+    g.n_src = c->halo ? c->tb_n_src : c->n_src;
     g.wl_len = c->wl_len;
     g.step1 = c->step + 1;
+    g.a_zoff = (int)c->gd;
+    if (c->halo) {
+        // neighbours' own p_{t-1} (role ipp) and c2 planes next to ours; Y goes
+        // into their Y buffers (index 3, same role on every rank)
+        const size_t P = c->plane;
+        if (c->lo_base[0]) {
+            g.rem_b_lo = c->lo_base[c->ipp] + (size_t)c->lo_nz * P;
+            g.rem_c_lo = c->lo_c2 ? c->lo_c2 + (size_t)c->lo_nz * P : nullptr;
+            g.peer_lo_y = c->lo_base[3] + c->lo_ghost_off;
+        }
+        if (c->hi_base[0]) {
+            g.rem_b_hi = c->hi_base[c->ipp] + P;
+            g.rem_c_hi = c->hi_c2 ? c->hi_c2 + P : nullptr;
+            g.peer_hi_y = c->hi_base[3];
+        }
+    }
     g.tiles_x = (c->pitch + 127) / 128;
     g.tiles = g.tiles_x * ((c->H + kTbTY - 1) / kTbTY);
     const TmaSchedule sch = tb_schedule(g.tiles, c->nz, (uint32_t)grid);
     g.clen = sch.clen;
     g.nitems = sch.nitems;
-    k_step_tma2<kC2F><<<sch.grid, kThreads, smem, c->stream>>>(c->mapA[c->ip], c->mapB[c->ipp],
-                                                               c->mapC2b, g);
+    kern<<<sch.grid, kThreads, smem, c->stream>>>(c->mapA[c->ip], c->mapB[c->ipp], c->mapC2b, g);
     ws3d_status s = check_launch(c, "k_step_tma2");
     if (s != WS3D_OK) return s;
     c->tb_launches++;
     // New roles: buffer 3 (p_{t+2}) is the pressure, buffer 2 (p_{t+1}) the
     // previous pressure; the old pair becomes the free pair.
     const int order[4] = {3, 2, c->ip, c->ipp};
-    float* nb[4];
+    float *nb[4], *nlo[4], *nhi[4];
     CUtensorMap nP[4], nT[4], nA[4], nB[4];
     for (int k = 0; k < 4; ++k) {
         nb[k] = c->buf[order[k]];
+        nlo[k] = c->lo_base[order[k]];
+        nhi[k] = c->hi_base[order[k]];
         nP[k] = c->mapP[order[k]];
         nT[k] = c->mapT[order[k]];
         nA[k] = c->mapA[order[k]];
@@ -461,6 +537,8 @@ ws3d_status launch_tb(ws3d_ctx* c) {
     }
     for (int k = 0; k < 4; ++k) {
         c->buf[k] = nb[k];
+        c->lo_base[k] = nlo[k];  // the neighbours permute theirs the same way
+        c->hi_base[k] = nhi[k];
         c->mapP[k] = nP[k];
         c->mapT[k] = nT[k];
         c->mapA[k] = nA[k];
@@ -530,6 +608,7 @@ ws3d_status launch_persistent(ws3d_ctx* c, uint64_t n) {
     }
     PersistentArgs q{};
     q.a = make_params(c);
+    q.a.peer_lo2 = q.a.peer_hi2 = nullptr;  // this kernel stores one plane per side
     // index 0 = pressure, 1 = pressure_prev at the start of the launch
     const int role[2] = {c->ip, c->ipp};
     for (int b = 0; b < 2; ++b) {
@@ -667,23 +746,27 @@ ws3d_status ensure_cell_arrays(ws3d_ctx* c) {
     return WS3D_OK;
 }
 
-// Per-source (row in the neighbour's ghost plane, side) for sources on the
-// first or last owned plane; -1 rows elsewhere or without neighbours.
+// Per source: the offset of its cell in the lower neighbour's copy (relative
+// to that buffer's plane -1) and in the upper one's (relative to its plane
+// -2), or -1.  The neighbours hold copies of our first / last plane, and of
+// the second / second-to-last one at temporal depth 2.
 ws3d_status rebuild_source_ghosts(ws3d_ctx* c) {
     dfree(c, c->src_ghost, 2 * (size_t)c->n_src);
     if (!c->halo || c->n_src == 0) return WS3D_OK;
     std::vector<long long> gr(2 * (size_t)c->n_src, -1);
     bool any = false;
+    const uint32_t depth = std::min(c->hdepth, c->nz);
+    const long long P = (long long)c->plane;
     for (uint32_t k = 0; k < c->n_src; ++k) {
         const uint32_t x = c->src_xyz[3 * k], y = c->src_xyz[3 * k + 1], z = c->src_xyz[3 * k + 2];
         const long long row = (long long)y * c->pitch + x;
-        if (z == c->z0 && c->lo_base[0]) {
-            gr[2 * k] = (long long)c->lo_ghost_off + row;  // relative to the lower buffer base
-            gr[2 * k + 1] = 0;
+        const uint32_t from_lo = z - c->z0, from_hi = c->z0 + c->nz - 1 - z;  // 0 = edge plane
+        if (c->lo_base[0] && from_lo < depth) {
+            gr[2 * k] = (long long)c->lo_ghost_off + (long long)from_lo * P + row;
             any = true;
-        } else if (z == c->z0 + c->nz - 1 && c->hi_base[0]) {
-            gr[2 * k] = row;                                 // upper's lower ghost = its base
-            gr[2 * k + 1] = 1;
+        }
+        if (c->hi_base[0] && from_hi < depth) {
+            gr[2 * k + 1] = (1 - (long long)from_hi) * P + row;  // plane -1 or -2
             any = true;
         }
     }
@@ -696,10 +779,40 @@ ws3d_status rebuild_source_ghosts(ws3d_ctx* c) {
     return WS3D_OK;
 }
 
+// The two-step kernel's source table on a z-slab at temporal depth 2: every
+// source on planes -1 .. nz (its own and the ghost planes it computes p_{t+1}
+// on), in the given order.
+ws3d_status rebuild_tb_sources(ws3d_ctx* c) {
+    dfree(c, c->tb_src_off, c->tb_n_src);
+    dfree(c, c->tb_wavelet, (size_t)c->tb_n_src * c->wl_len);
+    c->tb_n_src = 0;
+    if (!c->halo || c->hdepth != 2 || c->n_src_global == 0) return WS3D_OK;
+    std::vector<uint64_t> off;
+    std::vector<float> wl;
+    for (uint32_t k = 0; k < c->n_src_global; ++k) {
+        const uint32_t x = c->gsrc_xyz[3 * k], y = c->gsrc_xyz[3 * k + 1], z = c->gsrc_xyz[3 * k + 2];
+        if (z + 1 < c->z0 || z > c->z0 + c->nz) continue;
+        off.push_back((uint64_t)(z + 1 - c->z0) * c->plane + (uint64_t)y * c->pitch + x);
+        wl.insert(wl.end(), c->gsrc_wl.begin() + (size_t)k * c->wl_len,
+                  c->gsrc_wl.begin() + (size_t)(k + 1) * c->wl_len);
+    }
+    if (off.empty()) return WS3D_OK;
+    ws3d_status s;
+    if ((s = dalloc(c, &c->tb_src_off, off.size(), "two-step sources")) != WS3D_OK) return s;
+    if ((s = dalloc(c, &c->tb_wavelet, wl.size(), "two-step wavelet")) != WS3D_OK) return s;
+    WS3D_CUDA(c, cudaMemcpy(c->tb_src_off, off.data(), off.size() * 8, cudaMemcpyHostToDevice),
+              WS3D_EMEMORY);
+    WS3D_CUDA(c, cudaMemcpy(c->tb_wavelet, wl.data(), wl.size() * 4, cudaMemcpyHostToDevice),
+              WS3D_EMEMORY);
+    c->tb_n_src = (uint32_t)off.size();
+    return WS3D_OK;
+}
+
 ws3d_status launch_sources(ws3d_ctx* c) {
     if (!c->n_src) return WS3D_OK;
-    float* glo = c->lo_base[c->ip];  // neighbours' current pressure buffers
-    float* ghi = c->hi_base[c->ip];
+    // neighbours' current pressure buffers (lower: plane -1, upper: plane -2)
+    float* glo = c->lo_base[c->ip];
+    float* ghi = c->hi_base[c->ip] ? c->hi_base[c->ip] - c->plane : nullptr;
     k_inject_sources<<<1, 32, 0, c->stream>>>(c->buf[c->ip], c->buf[c->ipp], c->src_off,
                                               c->wavelet, c->n_src, c->wl_len, c->step,
                                               c->src_ghost, glo, ghi);
@@ -803,6 +916,7 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
     c->pitch = (c->W + 31u) & ~31u;
     c->plane = (size_t)c->H * c->pitch;
     c->slab = (size_t)(c->nz + 2) * c->plane;
+    c->gd = c->nz < c->Dg ? 2u : 1u;  // z-slab: room for temporal depth 2
 
     DeviceGuard g(desc->device);
     auto bail = [&](ws3d_status s) {
@@ -829,11 +943,7 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
 
     ws3d_status s;
     for (int b = 0; b < 2; ++b)
-        if ((s = dalloc(c, &c->buf[b], c->slab, "pressure")) != WS3D_OK) return bail(s);
-    for (int b = 0; b < 2; ++b) {
-        e = cudaMemsetAsync(c->buf[b], 0, c->slab * sizeof(float), c->stream);
-        if (e != cudaSuccess) return bail(cuda_fail(c, WS3D_EMEMORY, e, "cudaMemsetAsync"));
-    }
+        if ((s = falloc(c, b, "pressure")) != WS3D_OK) return bail(s);
     if (desc->sponge_width > 0) {
         c->sponge_w = desc->sponge_width;
         std::vector<float> tab(c->sponge_w);
@@ -879,7 +989,7 @@ void ws3d_destroy(ws3d_ctx* c) {
         } else {
             cudaDeviceSynchronize();
         }
-        for (int b = 0; b < 4; ++b) dfree(c, c->buf[b], c->slab);
+        for (int b = 0; b < 4; ++b) ffree(c, b);
         dfree(c, c->c2f, c->slab);
         dfree(c, c->types, c->slab);
         dfree(c, c->refl, c->slab);
@@ -888,6 +998,8 @@ void ws3d_destroy(ws3d_ctx* c) {
         dfree(c, c->wavelet, (size_t)c->n_src * c->wl_len);
         dfree(c, c->red_scratch, (size_t)c->red_blocks + 1);
         dfree(c, c->src_ghost, 2 * (size_t)c->n_src);
+        dfree(c, c->tb_src_off, c->tb_n_src);
+        dfree(c, c->tb_wavelet, (size_t)c->tb_n_src * c->wl_len);
         dfree(c, c->flags, kFlagWords);
         for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
         for (cudaEvent_t ev : c->tev) cudaEventDestroy(ev);
@@ -936,7 +1048,7 @@ ws3d_status ws3d_reset(ws3d_ctx* c, const float* p, const float* pp) {
     c->halo_synced = false;
     DeviceGuard g(c->desc.device);
     for (int b = 0; b < 2; ++b)
-        WS3D_CUDA(c, cudaMemsetAsync(c->buf[b], 0, c->slab * sizeof(float), c->stream),
+        WS3D_CUDA(c, cudaMemsetAsync(fbuf_base(c, b), 0, fbuf_elems(c) * sizeof(float), c->stream),
                   WS3D_EMEMORY);
     return ws3d_upload(c, p, pp);
 }
@@ -971,6 +1083,10 @@ ws3d_status ws3d_set_cells(ws3d_ctx* c, const uint8_t* types, const float* refl)
         c->cells_default = true;
         return WS3D_OK;
     }
+    if (c->halo && c->hdepth == 2)
+        return fail(c, WS3D_ECOMMAND,
+                    "set_cells: temporal depth 2 runs the TMA kernels, which take the default "
+                    "face layout only; set depth 1 first");
     for (size_t k = 0, n = (size_t)c->W * c->H * c->nz; k < n; ++k)
         if (types[k] > kObstacle)
             return fail(c, WS3D_EINVAL, "set_cells: cell type %u at index %zu is not 0..3",
@@ -991,6 +1107,10 @@ ws3d_status ws3d_set_cells(ws3d_ctx* c, const uint8_t* types, const float* refl)
 ws3d_status ws3d_set_c2_field(ws3d_ctx* c, const float* c2) {
     WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
+    if (c->halo && c->hdepth == 2 && (c2 == nullptr) != (c->c2f == nullptr))
+        return fail(c, WS3D_ECOMMAND,
+                    "set_c2_field: at temporal depth 2 the neighbours read this slab's c2 "
+                    "planes; set the field before ws3d_halo_export, and keep it");
     DeviceGuard g(c->desc.device);
     if (!c2) {
         WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EDEVICE);
@@ -1026,9 +1146,16 @@ ws3d_status ws3d_set_sources(ws3d_ctx* c, uint32_t n, const uint32_t* xyz, const
     dfree(c, c->src_off, c->n_src);
     dfree(c, c->wavelet, (size_t)c->n_src * c->wl_len);
     dfree(c, c->src_ghost, 2 * (size_t)c->n_src);
+    dfree(c, c->tb_src_off, c->tb_n_src);
+    dfree(c, c->tb_wavelet, (size_t)c->tb_n_src * c->wl_len);
     c->n_src = 0;
-    c->wl_len = 0;
+    c->tb_n_src = 0;
+    c->wl_len = n ? len : 0;
     c->src_xyz.clear();
+    // the whole list, for the ghost planes of two-step launches on z-slabs
+    c->n_src_global = n;
+    c->gsrc_xyz.assign(xyz, xyz + 3 * (size_t)n);
+    c->gsrc_wl.assign(wavelet, wavelet + (size_t)n * (n ? len : 0));
     // Keep only the sources inside the owned planes, in their given order.
     std::vector<uint64_t> off;
     std::vector<float> wl;
@@ -1039,28 +1166,36 @@ ws3d_status ws3d_set_sources(ws3d_ctx* c, uint32_t n, const uint32_t* xyz, const
         wl.insert(wl.end(), wavelet + (size_t)k * len, wavelet + (size_t)(k + 1) * len);
         c->src_xyz.insert(c->src_xyz.end(), {x, y, z});
     }
-    if (off.empty()) return WS3D_OK;
     ws3d_status s;
-    if ((s = dalloc(c, &c->src_off, off.size(), "sources")) != WS3D_OK) return s;
-    if ((s = dalloc(c, &c->wavelet, wl.size(), "wavelet")) != WS3D_OK) return s;
-    WS3D_CUDA(c, cudaMemcpy(c->src_off, off.data(), off.size() * 8, cudaMemcpyHostToDevice),
-              WS3D_EMEMORY);
-    WS3D_CUDA(c, cudaMemcpy(c->wavelet, wl.data(), wl.size() * 4, cudaMemcpyHostToDevice),
-              WS3D_EMEMORY);
-    c->n_src = (uint32_t)off.size();
-    c->wl_len = len;
-    return rebuild_source_ghosts(c);
+    if (!off.empty()) {
+        if ((s = dalloc(c, &c->src_off, off.size(), "sources")) != WS3D_OK) return s;
+        if ((s = dalloc(c, &c->wavelet, wl.size(), "wavelet")) != WS3D_OK) return s;
+        WS3D_CUDA(c, cudaMemcpy(c->src_off, off.data(), off.size() * 8, cudaMemcpyHostToDevice),
+                  WS3D_EMEMORY);
+        WS3D_CUDA(c, cudaMemcpy(c->wavelet, wl.data(), wl.size() * 4, cudaMemcpyHostToDevice),
+                  WS3D_EMEMORY);
+        c->n_src = (uint32_t)off.size();
+    }
+    if ((s = rebuild_source_ghosts(c)) != WS3D_OK) return s;
+    return rebuild_tb_sources(c);
 }
 
 namespace {
 // Two steps per launch for the auto and tma2 variants where the context
-// allows it (one GPU, default faces, TMA maps, at most 32 sources, a
-// monotone sponge of width <= 64, memory for two more field buffers);
-// otherwise single steps.  Measured on B200 at 512^3 (c2 field, sponge):
-// 0.64 ms per two-step launch against 2 x 0.359 ms for two TMA steps.
+// allows it (default faces, TMA maps, at most 32 sources, a monotone sponge
+// of width <= 64, memory for two more field buffers); otherwise single
+// steps.  Measured on B200 at 512^3 (c2 field, sponge): 0.64 ms per two-step
+// launch against 2 x 0.359 ms for two TMA steps.  On z-slabs only at
+// temporal depth 2, and by a rule every rank evaluates alike (the whole
+// source list, not this slab's share, decides), so that all ranks take the
+// same launches; the neighbours must hold our two edge planes (not so right
+// after persistent steps, which store one).
 bool use_two_step(ws3d_ctx* c) {
-    const uint32_t v = c->desc.variant;
-    return (v == WS3D_VARIANT_TMA2 || v == WS3D_VARIANT_AUTO) && tb_eligible(c);
+    if (!two_step_variant(c)) return false;
+    if (c->halo)
+        return c->hdepth == 2 && c->deep_ok && c->n_src_global <= (uint32_t)kTbMaxSrc &&
+               tb_kernel_ok(c);
+    return c->n_src <= (uint32_t)kTbMaxSrc && tb_kernel_ok(c);
 }
 
 // Advances n steps; with `timed`, records an event pair around every step
@@ -1077,35 +1212,36 @@ ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed, uint64_t* nlaunch = n
             c->tev.push_back(ev);
         }
     }
+    if (c->halo && c->hdepth == 2 && !tma_eligible(c))
+        return fail(c, WS3D_ECOMMAND,
+                    "step: temporal depth 2 needs the TMA kernels (default faces, W > 128, H >= 16)");
     uint64_t ev = 0;
     for (uint64_t i = 0; i < n;) {
         ws3d_status s = launch_sources(c);
         if (s != WS3D_OK) return s;
-        if (n - i >= 2 && use_two_step(c)) {
-            // sources of step t went into A and B above; the kernel applies
-            // those of step t+1 between its two steps
-            if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
-            s = c->c2f ? launch_tb<true>(c) : launch_tb<false>(c);
-            if (s != WS3D_OK) return s;
-            if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
-            c->step += 2;
-            i += 2;
-            continue;
-        }
+        const bool two = n - i >= 2 && use_two_step(c);
         if (c->halo) {
-            // Tell the neighbours that this slab finished its previous step (its
-            // ghost writes into them and its reads of its own ghosts) and that the
-            // sources of this step are in their ghost copies: their step may start.
+            // Tell the neighbours that this slab finished its previous launch (its
+            // ghost writes into them and its reads of its own ghosts and of
+            // their planes) and that the sources of this step are in their ghost
+            // copies: their launch may start.  One signal per launch.
             k_halo_signal<<<1, 32, 0, c->stream>>>(c->lo_flag, c->hi_flag, c->halo_steps + 1);
             if ((s = check_launch(c, "k_halo_signal")) != WS3D_OK) return s;
         }
         if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
-        if ((s = launch_step(c)) != WS3D_OK) return s;
+        if (two) {
+            // sources of step t went into A and B above; the kernel applies
+            // those of step t+1 between its two steps
+            s = c->c2f ? launch_tb<true>(c) : launch_tb<false>(c);
+        } else if ((s = launch_step(c)) == WS3D_OK) {
+            std::swap(c->ip, c->ipp);
+        }
+        if (s != WS3D_OK) return s;
         if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
-        std::swap(c->ip, c->ipp);
-        c->step++;
+        c->step += two ? 2 : 1;
+        i += two ? 2 : 1;
         c->halo_steps++;
-        ++i;
+        c->deep_ok = true;  // both launches store two edge planes at temporal depth 2
     }
     if (nlaunch) *nlaunch = ev / 2;
     return WS3D_OK;
@@ -1141,7 +1277,9 @@ ws3d_status ws3d_step_timed(ws3d_ctx* c, uint64_t n, double* kernel_ms) {
 
 namespace {
 // Add amp*factor to the listed cells (and amp*factor*0.5 to p_prev), and to
-// the neighbours' ghost copies of the cells on the first / last owned plane.
+// the neighbours' ghost copies of the cells on the edge planes (pressure
+// only: glo relative to the lower neighbour's first upper ghost plane, ghi
+// relative to the upper one's plane -2).
 ws3d_status apply_impulse_table(ws3d_ctx* c, const std::vector<uint64_t>& off,
                                 const std::vector<float>& fac, const std::vector<uint64_t>& glo,
                                 const std::vector<float>& flo, const std::vector<uint64_t>& ghi,
@@ -1149,7 +1287,7 @@ ws3d_status apply_impulse_table(ws3d_ctx* c, const std::vector<uint64_t>& off,
     struct Part { const std::vector<uint64_t>* o; const std::vector<float>* f; float* ghost; };
     const Part parts[3] = {{&off, &fac, nullptr},
                            {&glo, &flo, c->lo_base[c->ip] ? c->lo_base[c->ip] + c->lo_ghost_off : nullptr},
-                           {&ghi, &fhi, c->hi_base[c->ip]}};
+                           {&ghi, &fhi, c->hi_base[c->ip] ? c->hi_base[c->ip] - c->plane : nullptr}};
     ws3d_status s = WS3D_OK;
     for (int k = 0; k < 3 && s == WS3D_OK; ++k) {
         const Part& q = parts[k];
@@ -1192,8 +1330,16 @@ struct ImpulseCells {
         const uint64_t row = (uint64_t)y * c->pitch + x;
         off.push_back((uint64_t)(z - c->z0 + 1) * c->plane + row);
         fac.push_back(f);
-        if (z == c->z0 && c->lo_base[0]) { glo.push_back(row); flo.push_back(f); }
-        if (z + 1 == c->z0 + c->nz && c->hi_base[0]) { ghi.push_back(row); fhi.push_back(f); }
+        const uint32_t d = std::min(c->hdepth, c->nz);  // edge planes the neighbours hold
+        const uint32_t from_lo = z - c->z0, from_hi = c->z0 + c->nz - 1 - z;
+        if (from_lo < d && c->lo_base[0]) {
+            glo.push_back(from_lo * c->plane + row);
+            flo.push_back(f);
+        }
+        if (from_hi < d && c->hi_base[0]) {
+            ghi.push_back((1 - from_hi) * c->plane + row);
+            fhi.push_back(f);
+        }
     }
 };
 }  // namespace
@@ -1205,7 +1351,9 @@ ws3d_status ws3d_inject_impulse(ws3d_ctx* c, uint32_t x, uint32_t y, uint32_t z,
     if (z < c->z0 || z >= c->z0 + c->nz) return WS3D_OK;      // another slab owns it
     DeviceGuard g(c->desc.device);
     const uint64_t off = (uint64_t)(z - c->z0 + 1) * c->plane + (uint64_t)y * c->pitch + x;
-    const bool on_lo = z == c->z0 && c->lo_base[0], on_hi = z + 1 == c->z0 + c->nz && c->hi_base[0];
+    const uint32_t d = std::min(c->hdepth, c->nz);
+    const bool on_lo = z - c->z0 < d && c->lo_base[0];
+    const bool on_hi = c->z0 + c->nz - 1 - z < d && c->hi_base[0];
     if (!on_lo && !on_hi) {
         k_inject_point<<<1, 32, 0, c->stream>>>(c->buf[c->ip], c->buf[c->ipp], off, amp);
         return check_launch(c, "k_inject_point");
@@ -1347,6 +1495,7 @@ ws3d_status ws3d_step_persistent(ws3d_ctx* c, uint64_t n) {
     if (n & 1u) std::swap(c->ip, c->ipp);
     c->step += n;
     c->halo_steps += n;
+    c->deep_ok = false;  // one plane per side went to the neighbours: single steps next
     return WS3D_OK;
 }
 
@@ -1432,16 +1581,21 @@ ws3d_status ws3d_set_step(ws3d_ctx* c, uint64_t step) {
 // z-slab halo exchange.
 // ---------------------------------------------------------------------------
 namespace {
-ws3d_status attach_common(ws3d_ctx* c, bool has_lo, uint32_t lo_nz, bool has_hi) {
-    c->halo = has_lo || has_hi;
+// Called after the neighbours' pointers, caps and sizes are in place.
+ws3d_status attach_common(ws3d_ctx* c) {
+    c->halo = c->lo_base[0] != nullptr || c->hi_base[0] != nullptr;
     c->halo_synced = false;
     c->halo_steps = 0;
-    c->lo_ghost_off = has_lo ? (uint64_t)(lo_nz + 1) * c->plane : 0;
+    c->hdepth = 1;
+    c->deep_ok = false;
+    c->lo_ghost_off = c->lo_base[0] ? (uint64_t)(c->lo_nz + 1) * c->plane : 0;
     if (c->halo && c->desc.variant != WS3D_VARIANT_ZSTREAM &&
         c->desc.variant != WS3D_VARIANT_AUTO && c->desc.variant != WS3D_VARIANT_ASYNC &&
-        c->desc.variant != WS3D_VARIANT_TMA)
-        return fail(c, WS3D_EINVAL, "halo exchange needs the auto, tma, async or zstream variant");
-    return rebuild_source_ghosts(c);
+        c->desc.variant != WS3D_VARIANT_TMA && c->desc.variant != WS3D_VARIANT_TMA2)
+        return fail(c, WS3D_EINVAL,
+                    "halo exchange needs the auto, tma, tma2, async or zstream variant");
+    ws3d_status s = rebuild_source_ghosts(c);
+    return s == WS3D_OK ? rebuild_tb_sources(c) : s;
 }
 
 bool same_geometry(const ws3d_ctx* c, uint32_t W, uint32_t H, uint32_t D, uint32_t pitch) {
@@ -1453,15 +1607,22 @@ ws3d_status ws3d_halo_export(ws3d_ctx* c, ws3d_halo_handles* out) {
     WS3D_NOT_RESIDENT(c);
     if (!c || !out) return c ? fail(c, WS3D_EINVAL, "halo_export: out is NULL") : WS3D_EINVAL;
     static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    static_assert(sizeof(ws3d_halo_handles) == 424, "ws3d_halo_handles layout");
     DeviceGuard g(c->desc.device);
     std::memset(out, 0, sizeof *out);
+    const uint32_t caps = halo_caps(c);  // two-step capable: buffers 2 and 3 exist now
     cudaIpcMemHandle_t h;
-    for (int b = 0; b < 2; ++b) {
-        WS3D_CUDA(c, cudaIpcGetMemHandle(&h, c->buf[b]), WS3D_EPEER);
+    const int nb = (caps & WS3D_HALO_CAP_TWO_STEP) ? 4 : 2;
+    for (int b = 0; b < nb; ++b) {
+        WS3D_CUDA(c, cudaIpcGetMemHandle(&h, fbuf_base(c, b)), WS3D_EPEER);
         std::memcpy(out->buf[b], &h, 64);
     }
     WS3D_CUDA(c, cudaIpcGetMemHandle(&h, c->flags), WS3D_EPEER);
     std::memcpy(out->flags, &h, 64);
+    if (c->c2f) {
+        WS3D_CUDA(c, cudaIpcGetMemHandle(&h, c->c2f), WS3D_EPEER);
+        std::memcpy(out->c2, &h, 64);
+    }
     out->width = c->W;
     out->height = c->H;
     out->depth = c->Dg;
@@ -1469,6 +1630,9 @@ ws3d_status ws3d_halo_export(ws3d_ctx* c, ws3d_halo_handles* out) {
     out->z_begin = c->z0;
     out->z_end = c->z0 + c->nz;
     out->device = c->desc.device;
+    out->caps = caps;
+    out->ghost_planes = c->gd;
+    out->c_squared = c->desc.c_squared;
     return WS3D_OK;
 }
 
@@ -1486,6 +1650,10 @@ ws3d_status ws3d_halo_attach(ws3d_ctx* c, const ws3d_halo_handles* lo, const ws3
     if ((lo && c->z0 == 0) || (hi && c->z0 + c->nz == c->Dg) || (!lo && c->z0 > 0) ||
         (!hi && c->z0 + c->nz < c->Dg))
         return fail(c, WS3D_EINVAL, "halo_attach: neighbours do not match the slab position");
+    for (const ws3d_halo_handles* n : {lo, hi})
+        if (n && n->ghost_planes != c->gd)
+            return fail(c, WS3D_EINVAL, "halo_attach: neighbour buffers hold %u ghost planes per "
+                                        "side, this slab %u", n->ghost_planes, c->gd);
     DeviceGuard g(c->desc.device);
     auto open = [&](const uint8_t* bytes, void** ptr) -> ws3d_status {
         cudaIpcMemHandle_t h;
@@ -1495,26 +1663,39 @@ ws3d_status ws3d_halo_attach(ws3d_ctx* c, const ws3d_halo_handles* lo, const ws3
         c->ipc_opened.push_back(*ptr);
         return WS3D_OK;
     };
+    // one neighbour: its field buffers (plane -1 pointers), flags, c2 field
+    auto map = [&](const ws3d_halo_handles* n, float** base, const float** c2,
+                   unsigned long long** flag, int flag_word) -> ws3d_status {
+        ws3d_status s;
+        void* q = nullptr;
+        const int nb = (n->caps & WS3D_HALO_CAP_TWO_STEP) ? 4 : 2;
+        for (int b = 0; b < nb; ++b) {
+            if ((s = open(n->buf[b], &q)) != WS3D_OK) return s;
+            base[b] = static_cast<float*>(q) + (size_t)(n->ghost_planes - 1) * c->plane;
+        }
+        if ((s = open(n->flags, &q)) != WS3D_OK) return s;
+        *flag = static_cast<unsigned long long*>(q) + flag_word;
+        if (n->caps & WS3D_HALO_CAP_C2_FIELD) {
+            if ((s = open(n->c2, &q)) != WS3D_OK) return s;
+            *c2 = static_cast<const float*>(q);
+        }
+        return WS3D_OK;
+    };
     ws3d_status s;
-    void* q = nullptr;
-    if (lo) {
-        for (int b = 0; b < 2; ++b) {
-            if ((s = open(lo->buf[b], &q)) != WS3D_OK) return s;
-            c->lo_base[b] = static_cast<float*>(q);
-        }
-        if ((s = open(lo->flags, &q)) != WS3D_OK) return s;
-        c->lo_flag = static_cast<unsigned long long*>(q) + 1;  // I am its upper neighbour
+    if (lo) {  // I am its upper neighbour: I raise its flags[1]
+        if ((s = map(lo, c->lo_base, &c->lo_c2, &c->lo_flag, 1)) != WS3D_OK) return s;
+        c->lo_caps = lo->caps;
+        c->lo_nz = lo->z_end - lo->z_begin;
+        c->lo_c2u = lo->c_squared;
     }
-    if (hi) {
-        for (int b = 0; b < 2; ++b) {
-            if ((s = open(hi->buf[b], &q)) != WS3D_OK) return s;
-            c->hi_base[b] = static_cast<float*>(q);
-        }
-        if ((s = open(hi->flags, &q)) != WS3D_OK) return s;
-        c->hi_flag = static_cast<unsigned long long*>(q) + 0;  // I am its lower neighbour
+    if (hi) {  // I am its lower neighbour: I raise its flags[0]
+        if ((s = map(hi, c->hi_base, &c->hi_c2, &c->hi_flag, 0)) != WS3D_OK) return s;
+        c->hi_caps = hi->caps;
+        c->hi_nz = hi->z_end - hi->z_begin;
+        c->hi_c2u = hi->c_squared;
     }
     c->host_ordered = false;
-    return attach_common(c, lo != nullptr, lo ? lo->z_end - lo->z_begin : 0, hi != nullptr);
+    return attach_common(c);
 }
 
 ws3d_status ws3d_halo_attach_local(ws3d_ctx* c, ws3d_ctx* lo, ws3d_ctx* hi) {
@@ -1533,21 +1714,59 @@ ws3d_status ws3d_halo_attach_local(ws3d_ctx* c, ws3d_ctx* lo, ws3d_ctx* hi) {
     if ((lo && lo->z0 + lo->nz != c->z0) || (hi && hi->z0 != c->z0 + c->nz) ||
         (!lo && c->z0 > 0) || (!hi && c->z0 + c->nz < c->Dg))
         return fail(c, WS3D_EINVAL, "halo_attach_local: neighbours do not match the slab position");
+    DeviceGuard g(c->desc.device);
     if (lo) {
-        c->lo_base[0] = lo->buf[0];
-        c->lo_base[1] = lo->buf[1];
+        c->lo_caps = halo_caps(lo);  // allocates its two-step buffers when capable
+        for (int b = 0; b < 4; ++b) c->lo_base[b] = lo->buf[b];
+        c->lo_c2 = lo->c2f;
+        c->lo_nz = lo->nz;
+        c->lo_c2u = lo->desc.c_squared;
         c->lo_flag = lo->flags + 1;
     }
     if (hi) {
-        c->hi_base[0] = hi->buf[0];
-        c->hi_base[1] = hi->buf[1];
+        c->hi_caps = halo_caps(hi);
+        for (int b = 0; b < 4; ++b) c->hi_base[b] = hi->buf[b];
+        c->hi_c2 = hi->c2f;
+        c->hi_nz = hi->nz;
+        c->hi_c2u = hi->desc.c_squared;
         c->hi_flag = hi->flags + 0;
     }
     // Same device: the slabs advance in one stream through ws3d_step_group, so
     // stream order replaces the device-side flags (two kernels that wait on one
     // another never share a GPU).
     c->host_ordered = true;
-    return attach_common(c, lo != nullptr, lo ? lo->nz : 0, hi != nullptr);
+    return attach_common(c);
+}
+
+ws3d_status ws3d_halo_set_depth(ws3d_ctx* c, uint32_t depth) {
+    WS3D_NOT_RESIDENT(c);
+    if (!c) return WS3D_EINVAL;
+    if (depth != 1 && depth != 2)
+        return fail(c, WS3D_EINVAL, "halo_set_depth: depth %u is not 1 or 2", depth);
+    if (!c->halo) return fail(c, WS3D_ECOMMAND, "halo_set_depth: no neighbours attached");
+    DeviceGuard g(c->desc.device);
+    if (depth == 2) {
+        const uint32_t mine = halo_caps(c);
+        const bool c2 = (mine & WS3D_HALO_CAP_C2_FIELD) != 0;
+        // a neighbour fits when it is two-step capable, owns >= 2 planes, and
+        // its c2 is given the same way (field, or the same uniform value)
+        auto fits = [&](const float* base, uint32_t caps, uint32_t nz, float c2u) {
+            return !base || ((caps & WS3D_HALO_CAP_TWO_STEP) && nz >= 2 &&
+                             ((caps & WS3D_HALO_CAP_C2_FIELD) != 0) == c2 &&
+                             (c2 || c2u == c->desc.c_squared));
+        };
+        if (!(mine & WS3D_HALO_CAP_TWO_STEP) || !fits(c->lo_base[0], c->lo_caps, c->lo_nz, c->lo_c2u) ||
+            !fits(c->hi_base[0], c->hi_caps, c->hi_nz, c->hi_c2u))
+            return fail(c, WS3D_EINVAL,
+                        "halo_set_depth: temporal depth 2 needs this slab and its neighbours "
+                        "two-step capable (auto or tma2 variant, TMA kernels, monotone sponge of "
+                        "width <= 64, >= 2 planes each) with c2 given the same way");
+    }
+    c->hdepth = depth;
+    c->halo_synced = false;
+    c->deep_ok = false;
+    ws3d_status s = rebuild_source_ghosts(c);
+    return s == WS3D_OK ? rebuild_tb_sources(c) : s;
 }
 
 ws3d_status ws3d_halo_sync(ws3d_ctx* c, uint32_t phase) {
@@ -1562,21 +1781,25 @@ ws3d_status ws3d_halo_sync(ws3d_ctx* c, uint32_t phase) {
     c->halo_synced = false;
     if (phase == 0) return WS3D_OK;
     // Phase 1: clear this slab's flags, then fill the neighbours' ghost planes
-    // with this slab's first / last plane of the current field.
+    // with this slab's first / last plane (two of each at temporal depth 2)
+    // of the current field.
     WS3D_CUDA(c, cudaMemset(c->flags, 0, kFlagWords * sizeof(unsigned long long)), WS3D_EDEVICE);
     c->halo_steps = 0;
-    const size_t bytes = c->plane * sizeof(float);
-    float* P = c->buf[c->ip];
+    const size_t P = c->plane;
+    const uint32_t d = std::min(c->hdepth, c->nz);
+    const size_t bytes = d * P * sizeof(float);
+    float* B = c->buf[c->ip];
     if (c->lo_base[0])
-        WS3D_CUDA(c, cudaMemcpyAsync(c->lo_base[c->ip] + c->lo_ghost_off, P + c->plane, bytes,
+        WS3D_CUDA(c, cudaMemcpyAsync(c->lo_base[c->ip] + c->lo_ghost_off, B + P, bytes,
                                      cudaMemcpyDefault, c->stream),
                   WS3D_EPEER);
     if (c->hi_base[0])
-        WS3D_CUDA(c, cudaMemcpyAsync(c->hi_base[c->ip], P + (size_t)c->nz * c->plane, bytes,
-                                     cudaMemcpyDefault, c->stream),
+        WS3D_CUDA(c, cudaMemcpyAsync(c->hi_base[c->ip] - (d - 1) * P, B + (c->nz - d + 1) * P,
+                                     bytes, cudaMemcpyDefault, c->stream),
                   WS3D_EPEER);
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_EPEER);
     c->halo_synced = true;
+    c->deep_ok = c->hdepth == 2;
     return WS3D_OK;
 }
 
@@ -1592,23 +1815,36 @@ ws3d_status ws3d_step_group(ws3d_ctx* const* ctxs, uint32_t n, uint64_t steps) {
             return fail(c, WS3D_ECOMMAND, "step_group: fields changed since the last halo sync");
         if (c->ip != ctxs[0]->ip || c->step != ctxs[0]->step)
             return fail(c, WS3D_ECOMMAND, "step_group: contexts are at different steps");
+        if (c->halo && c->hdepth == 2 && !tma_eligible(c))
+            return fail(c, WS3D_ECOMMAND, "step_group: temporal depth 2 needs the TMA kernels");
     }
     DeviceGuard g(ctxs[0]->desc.device);
-    for (uint64_t s = 0; s < steps; ++s) {
-        // All sources first (they touch neighbours' ghost copies), then all steps.
+    for (uint64_t s = 0; s < steps;) {
+        // one- or two-step launches, the same for every context
+        const bool two = steps - s >= 2 && use_two_step(ctxs[0]);
+        for (uint32_t k = 1; k < n; ++k)
+            if (two != (steps - s >= 2 && use_two_step(ctxs[k])))
+                return fail(ctxs[k], WS3D_ECOMMAND,
+                            "step_group: contexts disagree on two-step launches");
+        // All sources first (they touch neighbours' ghost copies), then all launches.
         for (uint32_t k = 0; k < n; ++k) {
             ws3d_status st = launch_sources(ctxs[k]);
             if (st != WS3D_OK) return st;
         }
         for (uint32_t k = 0; k < n; ++k) {
-            ws3d_status st = launch_step(ctxs[k]);
+            ws3d_ctx* c = ctxs[k];
+            ws3d_status st = two ? (c->c2f ? launch_tb<true>(c) : launch_tb<false>(c))
+                                 : launch_step(c);
             if (st != WS3D_OK) return st;
         }
         for (uint32_t k = 0; k < n; ++k) {
-            std::swap(ctxs[k]->ip, ctxs[k]->ipp);
-            ctxs[k]->step++;
-            ctxs[k]->halo_steps++;
+            ws3d_ctx* c = ctxs[k];
+            if (!two) std::swap(c->ip, c->ipp);
+            c->step += two ? 2 : 1;
+            c->halo_steps++;
+            c->deep_ok = true;
         }
+        s += two ? 2 : 1;
     }
     return WS3D_OK;
 }

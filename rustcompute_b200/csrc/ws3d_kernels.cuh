@@ -41,6 +41,8 @@ struct StepParams {
     // z-slab halo exchange (all null / zero on a single GPU)
     float* peer_lo;                      // lower neighbour's upper ghost plane (new field)
     float* peer_hi;                      // upper neighbour's lower ghost plane (new field)
+    float* peer_lo2;                     // temporal depth 2: its second upper ghost plane, or null
+    float* peer_hi2;                     // temporal depth 2: its second lower ghost plane, or null
     const unsigned long long* wait_lo;   // flag the lower neighbour raises, or null
     const unsigned long long* wait_hi;   // flag the upper neighbour raises, or null
     unsigned long long wait_val;         // both flags must reach this value first
@@ -453,29 +455,31 @@ __global__ void __launch_bounds__(256) k_ref_boundary(float* pp, const uint8_t* 
 
 // Per-step point sources, applied in source order by one thread so that
 // coinciding sources add in the same order as the reference loop.  A source
-// on a slab's first or last plane is also added to the neighbour's ghost copy
-// of that plane (ghost_row >= 0, side 0 = lower neighbour, 1 = upper).
+// on a plane that a neighbouring slab holds as a ghost plane is also added to
+// that copy: ghost_off[2k] / [2k+1]: offset of source k's cell in the lower / upper
+// neighbour's copy (relative to ghost_lo = its plane -1, ghost_hi = its plane
+// -2), or -1 when that neighbour holds no copy of the cell.
 __device__ __forceinline__ void inject_sources_dev(float* p, float* pp, const uint64_t* off,
                                                    const float* wavelet, uint32_t n, uint64_t len,
-                                                   uint64_t step, const long long* ghost_row,
+                                                   uint64_t step, const long long* ghost_off,
                                                    float* ghost_lo, float* ghost_hi) {
     for (uint32_t k = 0; k < n; ++k) {
         const float amp = step < len ? wavelet[(uint64_t)k * len + step] : 0.0f;
         p[off[k]] = __fadd_rn(p[off[k]], amp);
         pp[off[k]] = __fadd_rn(pp[off[k]], __fmul_rn(amp, 0.5f));
-        if (ghost_row) {
-            const long long g = ghost_row[2 * k], side = ghost_row[2 * k + 1];
-            float* gp = side == 0 ? ghost_lo : ghost_hi;
-            if (g >= 0 && gp) gp[g] = __fadd_rn(gp[g], amp);
+        if (ghost_off) {
+            const long long gl = ghost_off[2 * k], gh = ghost_off[2 * k + 1];
+            if (gl >= 0 && ghost_lo) ghost_lo[gl] = __fadd_rn(ghost_lo[gl], amp);
+            if (gh >= 0 && ghost_hi) ghost_hi[gh] = __fadd_rn(ghost_hi[gh], amp);
         }
     }
 }
 
 __global__ void k_inject_sources(float* p, float* pp, const uint64_t* off, const float* wavelet,
                                  uint32_t n, uint64_t len, uint64_t step,
-                                 const long long* ghost_row, float* ghost_lo, float* ghost_hi) {
+                                 const long long* ghost_off, float* ghost_lo, float* ghost_hi) {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    inject_sources_dev(p, pp, off, wavelet, n, len, step, ghost_row, ghost_lo, ghost_hi);
+    inject_sources_dev(p, pp, off, wavelet, n, len, step, ghost_off, ghost_lo, ghost_hi);
 }
 
 // Impulse factors applied to a neighbour's ghost copy of a boundary plane

@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(32 * TY, 3) k_persistent(PersistentArgs q) {
             if (q.n_src)
                 inject_sources_dev(q.buf[cur], q.buf[cur ^ 1], q.src_off, q.wavelet, q.n_src,
                                    q.wl_len, q.step0 + s, q.src_ghost, q.lo_base[cur],
-                                   q.hi_base[cur]);
+                                   q.hi_base[0] ? q.hi_base[cur] - a.plane : nullptr);
             if (halo) {
                 __threadfence_system();
                 if (q.lo_flag) st_release_sys(q.lo_flag, q.halo_base + s + 1);

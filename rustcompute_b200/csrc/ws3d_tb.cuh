@@ -1,4 +1,5 @@
-// ws3d_tb.cuh -- two FDTD steps per launch (temporal blocking, depth 2), one GPU.
+// ws3d_tb.cuh -- two FDTD steps per launch (temporal blocking, depth 2), one
+// GPU or a z-slab.
 //
 // Inputs A = p_t (pressure), B = p_{t-1} (pressure_prev) and c2; outputs
 // X = p_{t+1} and Y = p_{t+2} go to two buffers that no CTA reads during the
@@ -35,12 +36,23 @@
 // two steps bit for bit.  At most 32 sources (a shared table; lane k reads
 // source k in tiles that hold one); the host checks.
 //
+// z-slabs (temporal depth 2, two ghost planes per side in every field
+// buffer): X is also computed on ghost planes -1 / nz, from the two ghost
+// planes of A on that side (stored there by the neighbour's previous launch)
+// and the neighbour's own B and c2 planes, which the consumer warps read over
+// NVLink into the staged rows before that item (B changes between launches
+// and only its owner updates it, so no copy of it is kept here).  Y of planes
+// 0, 1 / nz-2, nz-1 is also stored into the neighbour's Y buffer, i.e. its two
+// ghost planes of the next launch's A.  Runs that read ghost planes or store
+// into a neighbour wait (bounded) for its flag, raised before its launch;
+// those runs take a separate instance of the item code, interior runs the
+// one-GPU code.  Equal to single steps bit for bit.
+//
 // Every mbarrier wait is bounded.  The item's barrier is a vote
 // (bar.red.or): if any consumer warp's wait gave up, all consumer warps see
 // it and leave together, so no warp is left waiting at a barrier.
 // The producer waits (bounded) for the copies it issued before it exits.  TMA
-// loads read local memory only, without multicast; used only on one GPU with
-// the default face layout.
+// loads read this GPU's memory only, without multicast; default face layout.
 #pragma once
 
 #include "ws3d_lean.cuh"
@@ -77,13 +89,25 @@ struct TbArgs {
     StepParams a;             // p = A, pp = B (owned plane 0), c2f, geometry, sponge
     float* X;                 // owned plane 0 of the p_{t+1} output buffer
     float* Y;                 // owned plane 0 of the p_{t+2} output buffer
-    const uint64_t* src_off;  // n_src slab offsets ((z+1)*plane + y*pitch + x)
+    const uint64_t* src_off;  // n_src slab offsets ((z+1)*plane + y*pitch + x), z in [-1, nz]
     const float* wavelet;     // n_src x wl_len
     uint32_t n_src;
     uint64_t wl_len;
     uint64_t step1;           // global index of step t+1
     uint32_t tiles_x, tiles, clen, nitems;
+    int a_zoff;               // tensor-map z of A plane q is q + a_zoff
+    // z-slabs (all null on one GPU).  X is also computed on the ghost planes
+    // -1 / nz from the ghost planes of A and the neighbour's own B and c2
+    // planes (read in place over NVLink); Y of the two first / last planes is
+    // stored into the neighbour's Y buffer (its two ghost planes).
+    const float* rem_b_lo;    // lower neighbour's B at its last plane (= our plane -1)
+    const float* rem_b_hi;    // upper neighbour's B at its plane 0 (= our plane nz)
+    const float* rem_c_lo;    // the same planes of the neighbours' c2 fields (kC2F)
+    const float* rem_c_hi;
+    float* peer_lo_y;         // lower neighbour's Y buffer at its first upper ghost plane
+    float* peer_hi_y;         // upper neighbour's Y buffer at its first lower ghost plane
 };
+
 
 // Named barrier of the consumer warps that also ORs a predicate over them:
 // every consumer thread gets the same answer.
@@ -106,7 +130,9 @@ __device__ __forceinline__ float4 add_at(float4 v, int e, float d) {
     return v;
 }
 
-template <bool kC2F>
+// kSlab: the z-slab instance (ghost-plane X, neighbour waits, pushes); the
+// one-GPU instance compiles none of that into its item loop.
+template <bool kC2F, bool kSlab>
 __global__ void __launch_bounds__(32 * (kTbTY + 3), 2)
 k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmC2, TbArgs g) {
@@ -154,24 +180,42 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         uint32_t j = 0, s = 0, round = 0;  // items issued; stage and ring round of item j
         bool ok = true;
         for (uint32_t item = blockIdx.x; ok && item < g.nitems; item += gridDim.x) {
+            // chunk-major on slabs too: measured on two B200s at 512^3 per GPU,
+            // putting the boundary chunks last (as the one-step kernel does)
+            // was 2.5 % slower -- the neighbours' flags are up by the time
+            // the first chunk starts
             const uint32_t chunk = item / g.tiles, tile = item - chunk * g.tiles;
             const int zs = (int)(chunk * g.clen);
             const int ze = (int)min(a.nz, chunk * g.clen + g.clen);
             const int x0 = (int)((tile % g.tiles_x) * 128u), y0 = (int)((tile / g.tiles_x) * TY);
+            // Runs that read ghost planes (A down to zs-2 / up to ze+1, the
+            // neighbour's B and c2) or store into a neighbour's ghost planes
+            // (Y of planes 0, 1 / nz-2, nz-1) wait for that neighbour's flag.
+            const bool need_lo = kSlab && a.wait_lo && zs < 2;
+            const bool need_hi = kSlab && a.wait_hi && ze + 1 >= (int)a.nz;
+            if (need_lo || need_hi) {
+                unsigned int bad = 0;
+                if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns)) bad |= 1u;
+                if (need_hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns)) bad |= 2u;
+                if (bad) atomicOr(a.status, bad);
+                // the neighbour's stores into our ghost planes, acquired above,
+                // before our TMA loads of them
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
             for (int i = 0; i <= ze - zs + 3; ++i) {
                 if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u)) {
                     ok = false;
                     break;
                 }
                 unsigned char* st = smem + s * L::kStage;
-                const int zA = zs - 2 + i;  // A plane; tensor z = plane + 1
+                const int zA = zs - 2 + i;  // A plane; tensor z = plane + a_zoff
                 if (i < 2) {
                     mbar_expect_tx(&full[s], L::kABytes);
-                    tma_load_3d(st, &tmA, x0 - 4, y0 - 2, zA + 1, &full[s]);
+                    tma_load_3d(st, &tmA, x0 - 4, y0 - 2, zA + g.a_zoff, &full[s]);
                 } else {
                     const int q = zA - 1;
                     mbar_expect_tx(&full[s], L::kTx);
-                    tma_load_3d(st, &tmA, x0 - 4, y0 - 2, zA + 1, &full[s]);
+                    tma_load_3d(st, &tmA, x0 - 4, y0 - 2, zA + g.a_zoff, &full[s]);
                     tma_load_3d(st + L::kABytes, &tmB, x0 - 4, y0 - 1, q + 1, &full[s]);
                     if (kC2F)
                         tma_load_3d(st + L::kABytes + L::kBBytesPad, &tmC2, x0 - 4, y0 - 1, q + 1,
@@ -213,6 +257,9 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         return dz < a.sponge_w ? stab[dz] : 1.0f;
     };
 
+    // X planes this slab computes: its own, plus ghost plane -1 / nz next to a neighbour
+    const int xlo = kSlab && g.rem_b_lo ? -1 : 0;
+    const int xhi = (int)a.nz + (kSlab && g.rem_b_hi ? 1 : 0);
     uint32_t s = 0, ph = 0;  // stage and full-barrier parity of the current item
     for (uint32_t item = blockIdx.x; item < g.nitems; item += gridDim.x) {
         const uint32_t chunk = item / g.tiles, tile = item - chunk * g.tiles;
@@ -241,6 +288,9 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                                                    sc.y + 1 >= (int)y0 && sc.y <= (int)y0 + TY);
         }
         const int n = ze - zs;
+        // this run stores Y planes into a neighbour's ghost planes
+        const bool push_lo = kSlab && g.peer_lo_y != nullptr && zs < 2;
+        const bool push_hi = kSlab && g.peer_hi_y != nullptr && ze + 2 > (int)a.nz;
 
         // Ends an item: release the previous item's stage (this warp no longer
         // reads it), barrier with abort vote, next stage.  True = abort.
@@ -267,11 +317,14 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         // Item i >= 2: X(q), q = zs-3+i, from A(q-1) = a_m, A(q) = a_c and the
         // staged A(q+1) (kept in a_p); then Y(q-1) from X(q-2) = x_m,
         // X(q-1) = x_c and X(q) (kept in x_n).  Halo lanes: h_m, h_c, h_p.
-        // kSrc (compile time): the tile holds a source, so the sources of step
-        // t+1 are looked up; other tiles skip that code entirely.
-        auto body = [&](auto src_tag, int i, float4& a_m, float4& a_c, float4& a_p, float4& x_m,
+        // tag (compile time): bit 0 kSrc, the tile holds a source, so the
+        // sources of step t+1 are looked up (other tiles skip that code); bit
+        // 1 kEdge, a slab run next to a neighbour (ghost-plane X, stores into
+        // the neighbour) -- interior runs of a slab take the one-GPU code.
+        auto body = [&](auto tag, int i, float4& a_m, float4& a_c, float4& a_p, float4& x_m,
                         float4& x_c, float4& x_n, float& h_m, float& h_c, float& h_p) -> bool {
-            constexpr bool kSrc = decltype(src_tag)::value;
+            constexpr bool kSrc = (decltype(tag)::value & 1) != 0;
+            constexpr bool kEdge = kSlab && (decltype(tag)::value & 2) != 0;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph));
             if (ok) {
                 const int q = zs - 3 + i;
@@ -283,7 +336,7 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 a_p = *reinterpret_cast<const float4*>(Ac + arow + 4 + 4 * lane);
                 h_p = hlane ? Ac[hr] : 0.f;
                 x_n = z4;
-                if (q >= 0 && q < (int)a.nz) {
+                if (kEdge ? (q >= xlo && q < xhi) : (q >= 0 && q < (int)a.nz)) {
                     // ---- X(q) on extended row w
                     const uint32_t zg = a.z0 + (uint32_t)q;
                     const bool zin = zg >= 1 && zg + 1 < a.Dg;
@@ -373,30 +426,109 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     float4 yv = cells4_fast(wl, er, sv, nv, x_m, x_c, x_n, pv, c2y, damp);
                     yv = cells4_finish(yv, lr.fx, fzy, (zgy >= 1 && zgy + 1 < a.Dg) ? lr.bits : 0u,
                                        pv);
-                    if (act) st4(g.Y + zs_plane(qy, P) + row, yv);
+                    if (act) {
+                        st4(g.Y + zs_plane(qy, P) + row, yv);
+                        // the neighbours' two ghost planes of p_{t+2}
+                        if (kEdge && push_lo && qy < 2)
+                            st4(g.peer_lo_y + (int64_t)qy * P + row, yv);
+                        if (kEdge && push_hi && qy + 2 >= (int)a.nz)
+                            st4(g.peer_hi_y + ((int64_t)qy - (int64_t)a.nz + 1) * P + row, yv);
+                    }
                 }
             }
             return end_item(ok, true);
         };
 
+        // z-slabs: X on ghost plane q = -1 (item 2 of the first chunk) or
+        // q = nz (the last item of the last chunk) takes the neighbour's own B
+        // and c2 planes, read in place (the staged rows are our stale copy):
+        // warp w overwrites row w of the staged boxes (core and halo columns),
+        // then the consumer warps meet at a barrier before anyone reads them.
+        const int last = n + 3;
+        const bool fill_first = zs == 0 && g.rem_b_lo != nullptr;
+        const bool fill_last = ze == (int)a.nz && g.rem_b_hi != nullptr;
+        auto fill = [&](bool lo_side) {
+            const float* rb = lo_side ? g.rem_b_lo : g.rem_b_hi;
+            const float* rc = lo_side ? g.rem_c_lo : g.rem_c_hi;
+            if (__all_sync(0xffffffffu, mbar_wait(&full[s], ph))) {
+                float* Bq = reinterpret_cast<float*>(smem + s * L::kStage + L::kABytes);
+                float* Cq = Bq + L::kBBytesPad / 4;
+                const bool yin = y < a.H;  // row w of the boxes is y0 - 1 + w
+                const int64_t o = (int64_t)y * a.pitch;
+                // peer memory written before the flag the producer waited for: L2 path
+                float4 b4 = z4, c4 = z4;
+                if (yin && x < a.pitch) {
+                    b4 = __ldcg(reinterpret_cast<const float4*>(rb + o + x));
+                    if (kC2F) c4 = __ldcg(reinterpret_cast<const float4*>(rc + o + x));
+                }
+                *reinterpret_cast<float4*>(Bq + w * R + 4 + 4 * lane) = b4;
+                if (kC2F) *reinterpret_cast<float4*>(Cq + w * R + 4 + 4 * lane) = c4;
+                if (lane < 2) {  // halo columns x0-1, x0+128
+                    const uint32_t hx = lane == 0 ? x0 - 1u : x0 + 128u;
+                    const int col = lane == 0 ? 3 : 132;
+                    const bool in = yin && hx < a.pitch;
+                    Bq[w * R + col] = in ? __ldcg(rb + o + hx) : 0.f;
+                    if (kC2F) Cq[w * R + col] = in ? __ldcg(rc + o + hx) : 0.f;
+                }
+                // the producer's later TMA writes into this stage follow these stores
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            }
+            asm volatile("bar.sync 2, %0;" ::"n"(32 * (kTbTY + 2)) : "memory");
+        };
+
         float4 am = z4, ac = z4, ap = z4, xm = z4, xc = z4, xn = z4;
         float hm = 0.f, hc = 0.f, hp = 0.f;
+        // Items 2 .. last, three per iteration (the z queues rotate by
+        // renaming).  Slabs: the main loop leaves the last item to the tail,
+        // so that only the tail checks for the ghost-plane fill.
         auto run_items = [&](auto src_tag) -> bool {
             bool ab = false;
             int i = 2;
-            const int last = n + 3;
-            for (; !ab && i + 2 <= last; i += 3) {
-                ab = body(src_tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
-                     body(src_tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
-                     body(src_tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
+            if constexpr (!(kSlab && (decltype(src_tag)::value & 2) != 0)) {
+                for (; !ab && i + 2 <= last; i += 3) {
+                    ab = body(src_tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
+                         body(src_tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
+                         body(src_tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
+                }
+                if (!ab && i <= last) ab = body(src_tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
+                if (!ab && i <= last) ab = body(src_tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
+            } else {
+                for (; !ab && i + 3 <= last; i += 3) {
+                    ab = body(src_tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
+                         body(src_tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
+                         body(src_tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
+                }
+                if (!ab && i <= last) {
+                    if (i == last && fill_last) fill(false);
+                    ab = body(src_tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
+                }
+                if (!ab && i <= last) {
+                    if (i == last && fill_last) fill(false);
+                    ab = body(src_tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
+                }
+                if (!ab && i <= last) {
+                    if (fill_last) fill(false);  // i == last here
+                    ab = body(src_tag, i++, ap, am, ac, xn, xm, xc, hp, hm, hc);
+                }
             }
-            if (!ab && i <= last) ab = body(src_tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
-            if (!ab && i <= last) ab = body(src_tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
             return ab;
         };
         bool abort = prologue(am, hm, false) || prologue(ac, hc, true);
-        if (!abort)
-            abort = tile_src ? run_items(std::true_type{}) : run_items(std::false_type{});
+        if (kSlab && !abort && fill_first) fill(true);  // item 2: X on plane -1
+        if (!abort) {
+            using I0 = std::integral_constant<int, 0>;
+            using I1 = std::integral_constant<int, 1>;
+            if constexpr (kSlab) {
+                using I2 = std::integral_constant<int, 2>;
+                using I3 = std::integral_constant<int, 3>;
+                if (zs < 2 || ze + 2 > (int)a.nz)
+                    abort = tile_src ? run_items(I3{}) : run_items(I2{});
+                else
+                    abort = tile_src ? run_items(I1{}) : run_items(I0{});
+            } else {
+                abort = tile_src ? run_items(I1{}) : run_items(I0{});
+            }
+        }
         if (abort) {
             if (threadIdx.x == 0) atomicOr(a.status, 4u);
             return;  // every consumer thread saw the same vote
@@ -404,6 +536,7 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         // the run's last stage
         if (lane == 0) mbar_arrive(&empty[s == 0 ? S - 1 : s - 1]);
     }
+    if (kSlab && (g.peer_lo_y || g.peer_hi_y)) __threadfence_system();
 }
 
 }  // namespace ws3d

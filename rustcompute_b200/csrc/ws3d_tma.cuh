@@ -28,7 +28,8 @@
 // stores; consumers read the lower ghost plane through L2 after the run's
 // first stage arrived (ordered after that wait).  Boundary planes are stored
 // into the neighbours' ghost planes and fenced at system scope, like the
-// other slab kernels.  All TMA loads read this GPU's own memory (the ghost
+// other slab kernels; at temporal depth 2 the first two and last two planes
+// are (the neighbours' two-step launches read two ghost planes per side).  All TMA loads read this GPU's own memory (the ghost
 // planes are local buffers the neighbours write into); none uses multicast.
 #pragma once
 
@@ -163,7 +164,10 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
         bool ok = true;
         while (ok && next_run(item, nitems, tiles, clen, a.nz, halo, r)) {
             const int x0 = (int)((r.tile % tiles_x) * 128u), y0 = (int)((r.tile / tiles_x) * TY);
-            const bool need_lo = a.wait_lo && r.zs == 0, need_hi = a.wait_hi && r.ze == a.nz;
+            // runs that read a ghost plane or store into a neighbour's (two
+            // planes per side at temporal depth 2) wait for that neighbour
+            const bool need_lo = a.wait_lo && r.zs < (a.peer_lo2 ? 2u : 1u);
+            const bool need_hi = a.wait_hi && r.ze + (a.peer_hi2 ? 1u : 0u) >= a.nz;
             if (need_lo || need_hi) {
                 unsigned int bad = 0;
                 if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns)) bad |= 1u;
@@ -271,6 +275,8 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
                 st4(a.pp + zs_plane((int64_t)z, P) + row, out);
                 if (z == 0 && a.peer_lo) st4(a.peer_lo + row, out);
                 if (z + 1 == a.nz && a.peer_hi) st4(a.peer_hi + row, out);
+                if (z == 1 && a.peer_lo2) st4(a.peer_lo2 + row, out);
+                if (z + 2 == a.nz && a.peer_hi2) st4(a.peer_hi2 + row, out);
             }
             // The previous stage (plane z: neighbours, and this row's centre) is done.
             __syncwarp();

@@ -6,6 +6,10 @@ with one all_gather over torch.distributed (host plumbing only); from then on
 the halo moves inside the step kernel over NVLink (include/ws3d.h, section
 "z-slab decomposition").
 
+Temporal depth 2 (two steps per exchange, two ghost planes per side) is
+taken when every rank's export says it can: the choice must be the same on
+all ranks, so it is made from the gathered handles, not per rank.
+
 LocalSlabGroup runs the same decomposition inside one process on one GPU
 (stream-ordered, no device waits); it exists to test the slab arithmetic on a
 single device.
@@ -54,6 +58,24 @@ def attach(b: GpuBackend3D, lower: Optional[bytes], upper: Optional[bytes]) -> N
                                    C.byref(hi) if hi else None), "halo_attach")
 
 
+def temporal_depth(blobs: Sequence[bytes]) -> int:
+    """Steps per exchange all ranks can take: 2 when every slab is two-step
+    capable, owns >= 2 planes, and c2 is given the same way on all of them
+    (a field everywhere, or one uniform value), else 1."""
+    hs = [_handles(x) for x in blobs]
+    if len(hs) < 2:
+        return 1
+    two = all(h.caps & _ffi.HALO_CAP_TWO_STEP and h.z_end - h.z_begin >= 2 for h in hs)
+    fields = {bool(h.caps & _ffi.HALO_CAP_C2_FIELD) for h in hs}
+    uniform = {h.c_squared for h in hs}
+    same_c2 = fields == {True} or (fields == {False} and len(uniform) == 1)
+    return 2 if two and same_c2 else 1
+
+
+def set_depth(b: GpuBackend3D, depth: int) -> None:
+    b._chk(b._lib.ws3d_halo_set_depth(b._ctx, int(depth)), "halo_set_depth")
+
+
 def halo_sync(b: GpuBackend3D, barrier: Callable[[], None]) -> None:
     """Collective: clear flags, barrier, push boundary planes, barrier."""
     b._chk(b._lib.ws3d_halo_sync(b._ctx, 0), "halo_sync(0)")
@@ -70,18 +92,27 @@ def gather_handles(blob: bytes, rank: int, world: int, all_gather_object) -> lis
 
 
 def connect(b: GpuBackend3D, rank: int, world: int, all_gather_object,
-            barrier: Callable[[], None]) -> None:
-    """Exchange handles, attach both neighbours and synchronise the ghosts."""
+            barrier: Callable[[], None], depth: Optional[int] = None) -> int:
+    """Exchange handles, attach both neighbours, pick the temporal depth
+    (`depth`, or the largest every rank supports) and synchronise the
+    ghosts.  Returns the depth."""
     blobs = gather_handles(export_handles(b), rank, world, all_gather_object)
     lo, hi = neighbours(rank, world)
     attach(b, blobs[lo] if lo is not None else None, blobs[hi] if hi is not None else None)
+    d = temporal_depth(blobs) if depth is None else int(depth)
+    if world > 1:
+        set_depth(b, d)
     halo_sync(b, barrier)
+    return d if world > 1 else 1
 
 
 class LocalSlabGroup:
-    """Several slab contexts of one grid on one GPU, advanced in lockstep."""
+    """Several slab contexts of one grid on one GPU, advanced in lockstep.
 
-    def __init__(self, backends: Sequence[GpuBackend3D]):
+    depth: steps per exchange (1 or 2); None takes 2 when every context
+    accepts it, else 1."""
+
+    def __init__(self, backends: Sequence[GpuBackend3D], depth: Optional[int] = None):
         self.backends = list(backends)
         if not self.backends:
             raise ValueError("empty group")
@@ -92,6 +123,17 @@ class LocalSlabGroup:
             lo = self.backends[i - 1]._ctx if i > 0 else None
             hi = self.backends[i + 1]._ctx if i + 1 < len(self.backends) else None
             b._chk(b._lib.ws3d_halo_attach_local(b._ctx, lo, hi), "halo_attach_local")
+        self.depth = 1
+        if len(self.backends) > 1:
+            want = 2 if depth is None else int(depth)
+            if want == 2 and not all(b._lib.ws3d_halo_set_depth(b._ctx, 2) == _ffi.WS3D_OK
+                                     for b in self.backends):
+                if depth is not None:
+                    raise ValueError("temporal depth 2 is not possible for these slabs")
+                want = 1
+            for b in self.backends:
+                set_depth(b, want)
+            self.depth = want
         self.sync()
 
     def sync(self) -> None:

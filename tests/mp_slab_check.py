@@ -24,6 +24,8 @@ def main():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--persistent", action="store_true",
                     help="advance the slabs with ws3d_step_persistent")
+    ap.add_argument("--mixed", action="store_true",
+                    help="persistent steps first (one edge plane per side), then ws3d_step")
     args = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -55,14 +57,14 @@ def main():
         return b
 
     b = make(zb, ze, local)
-    connect(b, rank, world, dist.all_gather_object, dist.barrier)
+    depth = connect(b, rank, world, dist.all_gather_object, dist.barrier)
     # Impulses on both sides of every slab boundary exercise the ghost updates.
     for r in range(1, world):
         zc = slab_bounds(D, world, r)[0]
         b.inject_impulse(W // 3, H // 2, zc, 0.25)
         b.inject_impulse(W // 2, H // 3, zc - 1, -0.5)
     adv = b.step_persistent if args.persistent else (lambda n: b.step_n(None, n))
-    adv(7)
+    (b.step_persistent if args.mixed else adv)(7)
     b.inject_spherical_impulse(W // 2, H // 2, slab_bounds(D, world, world // 2)[0], 0.3, 3.0)
     adv(args.steps - 7)
     b.sync()
@@ -87,7 +89,7 @@ def main():
             np.array_equal(gpp.view(np.uint32), fpp.view(np.uint32))
         nbad = int(np.count_nonzero(gp != fp))
         print(f"SLAB-CHECK {'OK' if ok else 'FAIL'} world={world} grid={args.grid} "
-              f"steps={args.steps} differing cells={nbad}", flush=True)
+              f"steps={args.steps} depth={depth} differing cells={nbad}", flush=True)
         full.close()
     b.close()
     dist.barrier()

@@ -76,6 +76,8 @@ def test_ctx_struct_layout():
     assert C.sizeof(_ffi.ws3d_k2h_msg) == 64
     assert C.sizeof(_ffi.ws3d_resident_config) == 56
     assert C.sizeof(_ffi.ws3d_resident_stats) == 88
+    # z-slab exchange: four field buffers, flags, c2 field, geometry, caps
+    assert C.sizeof(_ffi.ws3d_halo_handles) == 424
 
 
 def test_no_cpu_fallback_in_package():

@@ -141,6 +141,112 @@ def _rank_main(rank, world, port, wl_args, result_q):
     dist.destroy_process_group()
 
 
+def _exchange(t_lo, t_hi, lo, hi, shape):
+    """Send t_lo to the lower neighbour and t_hi to the upper one; return what
+    they sent us (lower's, upper's).  gloo point-to-point."""
+    import torch
+    reqs = []
+    if lo is not None:
+        reqs.append(dist.isend(torch.from_numpy(np.ascontiguousarray(t_lo)), lo))
+    if hi is not None:
+        reqs.append(dist.isend(torch.from_numpy(np.ascontiguousarray(t_hi)), hi))
+    got_lo = got_hi = None
+    if lo is not None:
+        t = torch.empty(shape)
+        dist.recv(t, lo)
+        got_lo = t.numpy()
+    if hi is not None:
+        t = torch.empty(shape)
+        dist.recv(t, hi)
+        got_hi = t.numpy()
+    for r in reqs:
+        r.wait()
+    return got_lo, got_hi
+
+
+def _rank_main_depth2(rank, world, port, wl_args, result_q):
+    """Temporal depth 2 on z-slabs, the data flow of k_step_tma2 on slabs:
+    per pair of steps the ranks exchange two edge planes of p_t, and each
+    rank gets its neighbours' own p_{t-1} and c2 edge planes; it computes
+    p_{t+1} on its planes plus one ghost plane per side (sources of step t+1
+    included), then p_{t+2} on its own planes.  An odd last step is a single
+    step.  Must equal the single-domain oracle bit for bit."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import oracle
+    name, W, H, D, steps = wl_args
+    wl = configs.build(name, W, H, D, steps=steps)
+    zb, ze = slab_bounds(D, world, rank)
+    nz = ze - zb
+    lo, hi = neighbours(rank, world)
+    p, pp = wl.initial_fields(zb, ze)
+    P = p.reshape(nz, H, W).copy()
+    PP = pp.reshape(nz, H, W).copy()
+    c2f = wl.c2_field(zb, ze)
+    C2 = np.full((nz, H, W), f32(wl.c_squared)) if c2f is None else c2f.reshape(nz, H, W)
+    sponge = oracle.sponge_table(wl.sponge_width, wl.sponge_max) if wl.sponge_width \
+        else np.zeros(0, np.float32)
+    # the neighbours' c2 edge planes never change: fetch them once
+    c2_lo, c2_hi = _exchange(C2[0], C2[-1], lo, hi, (H, W))
+    xlo = -1 if lo is not None else 0           # X planes [xlo, xhi) in local z
+    xhi = nz + 1 if hi is not None else nz
+
+    def amp(k, s):
+        return wl.wavelet[k, s] if s < wl.wavelet.shape[1] else f32(0)
+
+    s = 0
+    while s < steps:
+        for k, (x, y, z) in enumerate(wl.sources.tolist()):   # sources of step s (host, own planes)
+            if zb <= z < ze:
+                P[z - zb, y, x] = P[z - zb, y, x] + amp(k, s)
+                PP[z - zb, y, x] = PP[z - zb, y, x] + amp(k, s) * f32(0.5)
+        # A: own planes plus two ghost planes per side (zeros beyond the grid)
+        g_lo, g_hi = _exchange(P[:2], P[-2:], lo, hi, (2, H, W))
+        A = np.zeros((nz + 4, H, W), np.float32)
+        A[2:-2] = P
+        if g_lo is not None:
+            A[:2] = g_lo
+        if g_hi is not None:
+            A[-2:] = g_hi
+        if steps - s == 1:   # single step
+            new = slab_step(A[1:-1], PP, C2, wl.damping, sponge, zb, D)
+            P, PP = new, P
+            s += 1
+            continue
+        # B and c2 on planes [xlo, xhi): the neighbours' own edge planes
+        b_lo, b_hi = _exchange(PP[0], PP[-1], lo, hi, (H, W))
+
+        def ext(own, below, above):   # planes [xlo, xhi)
+            return np.concatenate(([below[None]] if xlo < 0 else []) + [own] +
+                                  ([above[None]] if xhi > nz else []))
+        B = ext(PP, b_lo, b_hi)
+        Cx = ext(C2, c2_lo, c2_hi)
+        X = slab_step(A[xlo + 1:xhi + 3], B, Cx, wl.damping, sponge, zb + xlo, D)
+        Pm = P.copy()                                  # p_prev of the second step
+        for k, (x, y, z) in enumerate(wl.sources.tolist()):     # sources of step s+1
+            if zb + xlo <= z < zb + xhi:
+                X[z - zb - xlo, y, x] = X[z - zb - xlo, y, x] + amp(k, s + 1)
+            if zb <= z < ze:
+                Pm[z - zb, y, x] = Pm[z - zb, y, x] + amp(k, s + 1) * f32(0.5)
+        Xe = np.zeros((nz + 2, H, W), np.float32)      # X on planes -1 .. nz
+        Xe[1 + xlo:1 + xhi] = X
+        Y = slab_step(Xe, Pm, C2, wl.damping, sponge, zb, D)
+        P, PP = Y, X[-xlo:-xlo + nz]
+        s += 2
+    out = [None] * world
+    dist.all_gather_object(out, (zb, P.copy(), PP.copy()))
+    if rank == 0:
+        full_p = np.concatenate([o[1] for o in sorted(out, key=lambda t: t[0])]).reshape(-1)
+        full_pp = np.concatenate([o[2] for o in sorted(out, key=lambda t: t[0])]).reshape(-1)
+        ref = oracle.from_workload(wl)
+        ref.run(steps, 1)
+        result_q.put((bool(np.array_equal(full_p, ref.pressure)),
+                      bool(np.array_equal(full_pp, ref.pressure_prev))))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -165,3 +271,43 @@ def test_gloo_slab_emulation_matches_oracle(world, wl_args):
     codes = [p.exitcode for p in procs]
     assert codes == [0] * world, codes
     assert q.get(timeout=5) == (True, True)
+
+
+@pytest.mark.parametrize("world,wl_args", [
+    (2, ("c3", 40, 36, 30, 25)),     # heterogeneous + sponge + centred source, odd steps
+    (3, ("c2", 34, 30, 33, 40)),     # sources (also on ghost planes) + sponge
+    (3, ("c1", 24, 20, 7, 6)),       # 2-3 planes per slab: pushes reach both neighbours
+])
+def test_gloo_two_step_slab_emulation_matches_oracle(world, wl_args):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main_depth2, args=(r, world, port, wl_args, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    codes = [p.exitcode for p in procs]
+    assert codes == [0] * world, codes
+    assert q.get(timeout=5) == (True, True)
+
+
+def _blob(zb, ze, caps, c2=0.25):
+    from rustcompute_b200 import _ffi
+    h = _ffi.ws3d_halo_handles()
+    h.z_begin, h.z_end, h.caps, h.c_squared, h.ghost_planes = zb, ze, caps, c2, 2
+    return bytes(h)
+
+
+def test_temporal_depth_is_decided_from_every_rank():
+    from rustcompute_b200 import _ffi
+    from rustcompute_b200.slab import temporal_depth
+    T, F = _ffi.HALO_CAP_TWO_STEP, _ffi.HALO_CAP_C2_FIELD
+    assert temporal_depth([_blob(0, 8, T), _blob(8, 16, T)]) == 2
+    assert temporal_depth([_blob(0, 8, T | F), _blob(8, 16, T | F)]) == 2
+    assert temporal_depth([_blob(0, 8, T), _blob(8, 16, 0)]) == 1          # one rank cannot
+    assert temporal_depth([_blob(0, 8, T), _blob(8, 9, T), _blob(9, 16, T)]) == 1  # 1-plane slab
+    assert temporal_depth([_blob(0, 8, T | F), _blob(8, 16, T)]) == 1      # c2 field on one side
+    assert temporal_depth([_blob(0, 8, T, 0.25), _blob(8, 16, T, 0.2)]) == 1  # other uniform c2
+    assert temporal_depth([_blob(0, 16, T)]) == 1

@@ -40,14 +40,15 @@ def make(wl, zb, ze, device=0, budget_ns=0, variant="auto"):
     return b
 
 
-@pytest.mark.parametrize("variant", ["auto", "zstream", "tma"])
+@pytest.mark.parametrize("variant", ["auto", "zstream", "tma", "tma2"])
 @pytest.mark.parametrize("nslab", [2, 3, 4])
 @pytest.mark.parametrize("name,grid,steps", [("c3", (96, 72, 64), 50), ("c2", (48, 40, 37), 60),
-                                             ("c3", (160, 40, 45), 30), ("c2", (264, 24, 70), 24)])
+                                             ("c3", (160, 40, 45), 31), ("c2", (264, 24, 70), 24)])
 def test_local_slab_group_equals_single_context(nslab, name, grid, steps, variant):
     W, H, D = grid
-    if variant == "tma" and not (W > 128 and H >= 16):
-        pytest.skip("TMA kernel needs W > 128 and H >= 16")
+    tma_ok = W > 128 and H >= 16
+    if variant in ("tma", "tma2") and not tma_ok:
+        pytest.skip("TMA kernels need W > 128 and H >= 16")
     wl = configs.build(name, W, H, D, steps=steps)
     bounds = [slab_bounds(D, nslab, r) for r in range(nslab)]
     # put extra sources exactly on slab boundary planes (both sides)
@@ -58,6 +59,8 @@ def test_local_slab_group_equals_single_context(nslab, name, grid, steps, varian
     full = make(wl, 0, D)
     slabs = [make(wl, zb, ze, variant=variant) for zb, ze in bounds]
     grp = LocalSlabGroup(slabs)
+    # two steps per exchange wherever the two-step kernel runs
+    assert grp.depth == (2 if variant in ("auto", "tma2") and tma_ok else 1)
     full.step_n(None, steps // 2)
     grp.step_n(steps // 2)
     for b in [full] + slabs:   # impulses on boundary planes
@@ -127,7 +130,9 @@ def _gpu_count():
 @pytest.mark.parametrize("name,grid,steps,persistent", [("c3", "96x80x64", 60, False),
                                                         ("c2", "64x48x45", 50, False),
                                                         ("c5", "128x128x128", 200, True),
-                                                        ("c3", "160x64x64", 40, True)])
+                                                        ("c3", "160x64x64", 40, True),
+                                                        ("c3", "160x64x64", 41, False),
+                                                        ("c2", "264x24x70", 30, "mixed")])
 def test_multi_process_nvlink_slabs_equal_one_gpu(name, grid, steps, persistent):
     n = _gpu_count()
     if n < 2:
@@ -137,7 +142,49 @@ def test_multi_process_nvlink_slabs_equal_one_gpu(name, grid, steps, persistent)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", "--master-port", str(29400 + os.getpid() % 1000),
            os.path.join(ROOT, "tests", "mp_slab_check.py"), "--workload", name, "--grid", grid,
-           "--steps", str(steps)] + (["--persistent"] if persistent else [])
+           "--steps", str(steps)] + (["--persistent"] if persistent is True else []) + \
+        (["--mixed"] if persistent == "mixed" else [])
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, capture_output=True, text=True,
                        env=env)
     assert r.returncode == 0 and "SLAB-CHECK OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.parametrize("nslab,grid", [(3, (264, 24, 40)), (4, (160, 40, 9)), (2, (300, 17, 30))])
+def test_two_step_slabs_ghost_plane_sources_odd_counts_and_impulses(nslab, grid):
+    """Temporal depth 2 on same-device slabs: sources on every plane next to
+    a slab boundary (the ghost planes the kernel computes p_{t+1} on), odd
+    step counts (single steps storing two planes), impulses on the two edge
+    planes of each side between calls (mirrored two deep, no re-sync), c2
+    field and sponge.  Bit-identical to one context."""
+    W, H, D = grid
+    wl = configs.build("c3", W, H, D, steps=8)
+    bounds = [slab_bounds(D, nslab, r) for r in range(nslab)]
+    pts = []
+    for zb, _ in bounds[1:]:
+        for dz in (-2, -1, 0, 1):
+            pts.append([(W // 3 + 7 * dz) % W, (H // 2 + dz) % H, zb + dz])
+    pts.append(pts[1])                     # a coinciding pair on a ghost plane
+    rng = np.random.default_rng(D)
+    wl.sources = np.array(pts, np.uint32)
+    wl.wavelet = rng.standard_normal((len(pts), 11)).astype(np.float32)
+    full = make(wl, 0, D)
+    slabs = [make(wl, zb, ze) for zb, ze in bounds]
+    grp = LocalSlabGroup(slabs)
+    assert grp.depth == 2
+    for n, dz in ((5, 0), (6, -1), (1, 1), (4, -2), (3, 0)):
+        full.step_n(None, n)
+        grp.step_n(n)
+        for zb, _ in bounds[1:]:
+            for b in [full] + slabs:
+                b.inject_impulse(W // 2, H // 3, zb + dz, 0.4)
+                b.inject_spherical_impulse(W // 4, H // 2, zb - 1, -0.3, 2.0)
+    full.step_n(None, 7)
+    grp.step_n(7)
+    fp, fpp = full.download_field(with_prev=True)
+    gp = np.concatenate([b.download_field() for b in slabs])
+    gpp = np.concatenate([b.download_field(with_prev=True)[1] for b in slabs])
+    assert float(np.max(np.abs(fp))) > 1e-3
+    assert np.array_equal(gp.view(np.uint32), fp.view(np.uint32)), int((gp != fp).sum())
+    assert np.array_equal(gpp.view(np.uint32), fpp.view(np.uint32))
+    grp.close()
+    full.close()
