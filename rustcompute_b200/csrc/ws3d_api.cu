@@ -293,22 +293,31 @@ StepParams make_params(const ws3d_ctx* c) {
     return a;
 }
 
-// Copy a contiguous host array of nz planes (W x H each) into a pitched slab.
+// Copy a contiguous host array of nz planes (W x H each) into a pitched slab
+// (one linear copy when rows carry no padding, W a multiple of 32).
 template <class T>
 ws3d_status h2d_pitched(ws3d_ctx* c, T* dst_slab, const T* src) {
-    cudaError_t e = cudaMemcpy2DAsync(dst_slab + c->plane, c->pitch * sizeof(T), src,
-                                      c->W * sizeof(T), c->W * sizeof(T),
-                                      (size_t)c->H * c->nz, cudaMemcpyHostToDevice, c->stream);
-    if (e != cudaSuccess) return cuda_fail(c, WS3D_EMEMORY, e, "cudaMemcpy2DAsync(h2d)");
+    const size_t rows = (size_t)c->H * c->nz;
+    cudaError_t e =
+        c->pitch == c->W
+            ? cudaMemcpyAsync(dst_slab + c->plane, src, rows * c->W * sizeof(T),
+                              cudaMemcpyHostToDevice, c->stream)
+            : cudaMemcpy2DAsync(dst_slab + c->plane, c->pitch * sizeof(T), src, c->W * sizeof(T),
+                                c->W * sizeof(T), rows, cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, WS3D_EMEMORY, e, "cudaMemcpyAsync(h2d)");
     return WS3D_OK;
 }
 
 template <class T>
 ws3d_status d2h_pitched(ws3d_ctx* c, T* dst, const T* src_slab, ws3d_status code) {
-    cudaError_t e = cudaMemcpy2DAsync(dst, c->W * sizeof(T), src_slab + c->plane,
-                                      c->pitch * sizeof(T), c->W * sizeof(T),
-                                      (size_t)c->H * c->nz, cudaMemcpyDeviceToHost, c->stream);
-    if (e != cudaSuccess) return cuda_fail(c, code, e, "cudaMemcpy2DAsync(d2h)");
+    const size_t rows = (size_t)c->H * c->nz;
+    cudaError_t e =
+        c->pitch == c->W
+            ? cudaMemcpyAsync(dst, src_slab + c->plane, rows * c->W * sizeof(T),
+                              cudaMemcpyDeviceToHost, c->stream)
+            : cudaMemcpy2DAsync(dst, c->W * sizeof(T), src_slab + c->plane, c->pitch * sizeof(T),
+                                c->W * sizeof(T), rows, cudaMemcpyDeviceToHost, c->stream);
+    if (e != cudaSuccess) return cuda_fail(c, code, e, "cudaMemcpyAsync(d2h)");
     return WS3D_OK;
 }
 
