@@ -817,14 +817,26 @@ ws3d_status rebuild_tb_sources(ws3d_ctx* c) {
     return WS3D_OK;
 }
 
-ws3d_status launch_sources(ws3d_ctx* c) {
-    if (!c->n_src) return WS3D_OK;
+// Sources of the next step; with `signal` (a z-slab with device-side flags)
+// also raise the neighbours' flags for the next launch in the same kernel:
+// this slab finished its previous launch (its stores into them, its reads of
+// its own ghosts and of their planes) and this step's sources are in their
+// copies.
+ws3d_status launch_sources(ws3d_ctx* c, bool signal = false) {
+    unsigned long long* flo = signal ? c->lo_flag : nullptr;
+    unsigned long long* fhi = signal ? c->hi_flag : nullptr;
+    const unsigned long long v = c->halo_steps + 1;
+    if (!c->n_src) {
+        if (!flo && !fhi) return WS3D_OK;
+        k_halo_signal<<<1, 32, 0, c->stream>>>(flo, fhi, v);
+        return check_launch(c, "k_halo_signal");
+    }
     // neighbours' current pressure buffers (lower: plane -1, upper: plane -2)
     float* glo = c->lo_base[c->ip];
     float* ghi = c->hi_base[c->ip] ? c->hi_base[c->ip] - c->plane : nullptr;
     k_inject_sources<<<1, 32, 0, c->stream>>>(c->buf[c->ip], c->buf[c->ipp], c->src_off,
                                               c->wavelet, c->n_src, c->wl_len, c->step,
-                                              c->src_ghost, glo, ghi);
+                                              c->src_ghost, glo, ghi, flo, fhi, v);
     return check_launch(c, "k_inject_sources");
 }
 
@@ -1226,17 +1238,11 @@ ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed, uint64_t* nlaunch = n
                     "step: temporal depth 2 needs the TMA kernels (default faces, W > 128, H >= 16)");
     uint64_t ev = 0;
     for (uint64_t i = 0; i < n;) {
-        ws3d_status s = launch_sources(c);
+        // sources of this step and, on slabs, the one signal per launch that
+        // lets the neighbours' next launch start
+        ws3d_status s = launch_sources(c, c->halo);
         if (s != WS3D_OK) return s;
         const bool two = n - i >= 2 && use_two_step(c);
-        if (c->halo) {
-            // Tell the neighbours that this slab finished its previous launch (its
-            // ghost writes into them and its reads of its own ghosts and of
-            // their planes) and that the sources of this step are in their ghost
-            // copies: their launch may start.  One signal per launch.
-            k_halo_signal<<<1, 32, 0, c->stream>>>(c->lo_flag, c->hi_flag, c->halo_steps + 1);
-            if ((s = check_launch(c, "k_halo_signal")) != WS3D_OK) return s;
-        }
         if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
         if (two) {
             // sources of step t went into A and B above; the kernel applies

@@ -455,10 +455,11 @@ __global__ void __launch_bounds__(256) k_ref_boundary(float* pp, const uint8_t* 
 
 // Per-step point sources, applied in source order by one thread so that
 // coinciding sources add in the same order as the reference loop.  A source
-// on a plane that a neighbouring slab holds as a ghost plane is also added to
-// that copy: ghost_off[2k] / [2k+1]: offset of source k's cell in the lower / upper
-// neighbour's copy (relative to ghost_lo = its plane -1, ghost_hi = its plane
-// -2), or -1 when that neighbour holds no copy of the cell.
+// on a plane that a neighbouring slab holds as a ghost plane also updates that
+// copy: ghost_off[2k] / [2k+1] is the offset of source k's cell in the lower /
+// upper neighbour's copy (relative to ghost_lo = its plane -1, ghost_hi = its
+// plane -2), or -1 when that neighbour holds no copy of the cell.  A copy
+// equals the cell, so the new value is stored (no read over NVLink).
 __device__ __forceinline__ void inject_sources_dev(float* p, float* pp, const uint64_t* off,
                                                    const float* wavelet, uint32_t n, uint64_t len,
                                                    uint64_t step, const long long* ghost_off,
@@ -469,17 +470,26 @@ __device__ __forceinline__ void inject_sources_dev(float* p, float* pp, const ui
         pp[off[k]] = __fadd_rn(pp[off[k]], __fmul_rn(amp, 0.5f));
         if (ghost_off) {
             const long long gl = ghost_off[2 * k], gh = ghost_off[2 * k + 1];
-            if (gl >= 0 && ghost_lo) ghost_lo[gl] = __fadd_rn(ghost_lo[gl], amp);
-            if (gh >= 0 && ghost_hi) ghost_hi[gh] = __fadd_rn(ghost_hi[gh], amp);
+            if (gl >= 0 && ghost_lo) ghost_lo[gl] = p[off[k]];
+            if (gh >= 0 && ghost_hi) ghost_hi[gh] = p[off[k]];
         }
     }
 }
 
+// Sources of one step; on z-slabs also the halo signal of k_halo_signal
+// (flags non-null), after the sources reached the neighbours' copies.
 __global__ void k_inject_sources(float* p, float* pp, const uint64_t* off, const float* wavelet,
                                  uint32_t n, uint64_t len, uint64_t step,
-                                 const long long* ghost_off, float* ghost_lo, float* ghost_hi) {
+                                 const long long* ghost_off, float* ghost_lo, float* ghost_hi,
+                                 unsigned long long* flag_lo, unsigned long long* flag_hi,
+                                 unsigned long long flag_val) {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     inject_sources_dev(p, pp, off, wavelet, n, len, step, ghost_off, ghost_lo, ghost_hi);
+    if (flag_lo || flag_hi) {
+        __threadfence_system();
+        if (flag_lo) st_release_sys(flag_lo, flag_val);
+        if (flag_hi) st_release_sys(flag_hi, flag_val);
+    }
 }
 
 // Impulse factors applied to a neighbour's ghost copy of a boundary plane
