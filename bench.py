@@ -433,13 +433,25 @@ def run_ours(args, wl):
         barrier()
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        upload_inputs(b2, wl, *pins)
+        upload_inputs(b2, wl, *pins)            # synchronous
+        t1 = time.perf_counter()
+        conn = {}
         if world > 1:
             from rustcompute_b200.slab import connect
-            connect(b2, rank, world, pg.all_gather_object, barrier)
+            connect(b2, rank, world, pg.all_gather_object, barrier, timings=conn)
+        t2 = time.perf_counter()
         b2.step_n(None, args.steps)
+        b2.sync()                               # the download would wait for the steps anyway
+        t3 = time.perf_counter()
         b2.download_into(outp)
-        e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3)
+        t4 = time.perf_counter()
+        e2e_ms = max_over_ranks((t4 - t0) * 1e3)
+        phases = {k: max_over_ranks(v * 1e3) for k, v in
+                  (("upload", t1 - t0), ("connect", t2 - t1), ("steps", t3 - t2),
+                   ("download", t4 - t3))}
+        for k in ("export", "gather", "attach", "halo_sync"):   # same calls on every rank
+            if world > 1:
+                phases["connect_" + k] = max_over_ranks(conn[k])
         result["e2e"] = {"value": wl.cells * args.steps / (e2e_ms * 1e-3) / 1e6, "unit": UNIT,
                          "h2d_bytes_per_step": h2d * world // args.steps,
                          "d2h_bytes_per_step": d2h * world // args.steps,
@@ -447,7 +459,8 @@ def run_ours(args, wl):
                                 f"{', source wavelets' if len(wl.sources) else ''} from pinned "
                                 f"host memory; {args.steps} steps; download p"
                                 f"{'; slab handle exchange' if world > 1 else ''}",
-                         "job_ms": e2e_ms, "clock": "host wall clock, max over ranks"}
+                         "job_ms": e2e_ms, "phases_ms": phases,
+                         "clock": "host wall clock, max over ranks"}
         b2.close()
 
     if args.comparators and world == 1:

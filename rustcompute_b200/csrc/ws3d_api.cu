@@ -988,6 +988,12 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
         if (v >= 1 && v <= (1 << 20)) c->tma_min_chunk = (uint32_t)v;
     }
     build_tma_maps(c);
+    // The two-step buffers are part of the auto / tma2 working set: allocate
+    // them with the fields, not inside the first step (a failure only leaves
+    // the context on single steps).
+    if (two_step_variant(c) && c->tma_maps && c->sponge_monotone &&
+        c->sponge_w <= (uint32_t)kTbSpongeMax)
+        ensure_tb_buffers(c);
     c->red_blocks = (uint32_t)std::max(1, c->sm_count) * 4u;
     if ((s = dalloc(c, &c->red_scratch, (size_t)c->red_blocks + 1, "reduction")) != WS3D_OK)
         return bail(s);

@@ -17,6 +17,7 @@ single device.
 from __future__ import annotations
 
 import ctypes as C
+import time
 from typing import Callable, Optional, Sequence
 
 from . import _ffi
@@ -92,17 +93,28 @@ def gather_handles(blob: bytes, rank: int, world: int, all_gather_object) -> lis
 
 
 def connect(b: GpuBackend3D, rank: int, world: int, all_gather_object,
-            barrier: Callable[[], None], depth: Optional[int] = None) -> int:
+            barrier: Callable[[], None], depth: Optional[int] = None,
+            timings: Optional[dict] = None) -> int:
     """Exchange handles, attach both neighbours, pick the temporal depth
     (`depth`, or the largest every rank supports) and synchronise the
-    ghosts.  Returns the depth."""
-    blobs = gather_handles(export_handles(b), rank, world, all_gather_object)
+    ghosts.  Returns the depth; `timings` (optional) receives the host time
+    of each phase in ms."""
+    t = [time.perf_counter()]
+    blob = export_handles(b)
+    t.append(time.perf_counter())
+    blobs = gather_handles(blob, rank, world, all_gather_object)
+    t.append(time.perf_counter())
     lo, hi = neighbours(rank, world)
     attach(b, blobs[lo] if lo is not None else None, blobs[hi] if hi is not None else None)
     d = temporal_depth(blobs) if depth is None else int(depth)
     if world > 1:
         set_depth(b, d)
+    t.append(time.perf_counter())
     halo_sync(b, barrier)
+    t.append(time.perf_counter())
+    if timings is not None:
+        for k, name in enumerate(("export", "gather", "attach", "halo_sync")):
+            timings[name] = (t[k + 1] - t[k]) * 1e3
     return d if world > 1 else 1
 
 

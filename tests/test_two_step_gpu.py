@@ -138,14 +138,18 @@ def test_impulses_between_calls_and_split_calls():
 
 def test_two_step_memory_timing_and_launch_count():
     W, H, D = 256, 64, 64
+    one = make(W, H, D, "tma")
     two = make(W, H, D, "tma2")
+    # the two extra field buffers are allocated with the context, not in a step
+    slab = 256 * 64 * (64 + 2) * 4
+    assert two.memory_usage() - one.memory_usage() == 2 * slab
     before = two.memory_usage()
     l0 = two.stats()["kernel_launches"]
     ms = two.step_timed(10)       # 5 two-step launches
     assert ms > 0.0
     assert two.stats()["kernel_launches"] - l0 == 5
-    slab = 256 * 64 * (64 + 2) * 4
-    assert two.memory_usage() - before == 2 * slab
+    assert two.memory_usage() == before
+    one.close()
     two.step_n(None, 3)           # one two-step launch and one single step
     assert two.stats()["kernel_launches"] - l0 == 7
     assert two.stats()["step"] == 13
