@@ -393,6 +393,9 @@ def run_ours(args, wl):
                 "traffic": ncu_traffic(wl, kernel_name(args.variant, wl, world, depth=depth)),
                 "algorithmic_bytes_per_launch": alg_bytes,
                 "steps_per_launch": 2 if kname == "k_step_tma2" and args.mode == "step" else 1,
+                # algorithmic bytes per cell of one launch: one step moves bpc (read p,
+                # p_prev (+ c2), write one field); a two-step launch bpc + 4 (one more write)
+                "bytes_per_cell_per_launch": alg_bytes // max(local_cells, 1),
                 "bytes_per_cell_step": bpc,
                 "kernel_avg_ms": avg_kernel_ms,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"
