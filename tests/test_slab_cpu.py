@@ -1,7 +1,9 @@
 """Multi-GPU host logic on CPU: z-slab bounds, the handle exchange over
-torch.distributed (gloo, world sizes 2 and 3), and a slab-split emulation
-of the step with explicit ghost-plane exchange that must equal the
-single-domain oracle bit for bit.
+torch.distributed (gloo, world sizes 2 and 3), the temporal-depth decision,
+and slab-split emulations of the step with explicit ghost-plane exchange
+(one step per exchange; the two-step kernel's data flow; k steps with
+k-plane halos for k = 1 .. 4) that must equal the single-domain oracle bit
+for bit.
 """
 import os
 import socket
@@ -247,6 +249,102 @@ def _rank_main_depth2(rank, world, port, wl_args, result_q):
     dist.destroy_process_group()
 
 
+def _rank_main_depthk(rank, world, port, wl_args, k, result_q):
+    """Temporal depth k on z-slabs with k-cell halos (k = 1 .. 4).  Per
+    round of k steps a rank receives k edge planes of p_t and k-1 of p_{t-1}
+    from each neighbour (the c2 edge planes once), computes level j =
+    p_{t+j} on its planes plus k-j ghost planes per side that has a
+    neighbour (sources of step t+j: level j += a, the next level's p_prev =
+    level j-1 + a/2), and keeps levels k and k-1 of its own planes; a last
+    round of depth steps % k finishes.  The GPU kernel builds k = 2; this
+    pins the scheme for every k against the single-domain oracle."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import oracle
+    name, W, H, D, steps = wl_args
+    wl = configs.build(name, W, H, D, steps=steps)
+    zb, ze = slab_bounds(D, world, rank)
+    nz = ze - zb
+    lo, hi = neighbours(rank, world)
+    p, pp = wl.initial_fields(zb, ze)
+    P = p.reshape(nz, H, W).copy()
+    PP = pp.reshape(nz, H, W).copy()
+    c2f = wl.c2_field(zb, ze)
+    C2 = np.full((nz, H, W), f32(wl.c_squared)) if c2f is None else c2f.reshape(nz, H, W)
+    sponge = oracle.sponge_table(wl.sponge_width, wl.sponge_max) if wl.sponge_width \
+        else np.zeros(0, np.float32)
+    src = wl.sources.tolist()
+
+    def amp(j, step):
+        return wl.wavelet[j, step] if step < wl.wavelet.shape[1] else f32(0)
+
+    def span(e):   # global planes of a level with e ghost planes per neighbour side
+        return (zb - e if lo is not None else zb), (ze + e if hi is not None else ze)
+
+    def with_ghosts(own, below, above, e):
+        """(array, global start) of own planes plus e planes from each neighbour."""
+        parts = ([below] if lo is not None and e else []) + [own] + \
+            ([above] if hi is not None and e else [])
+        return np.concatenate(parts), span(e)[0]
+
+    def take(arr, start, z0, z1):
+        """planes [z0, z1) of arr (first plane = global start), zeros outside it."""
+        out = np.zeros((z1 - z0, H, W), np.float32)
+        a, b = max(z0, start), min(z1, start + arr.shape[0])
+        if b > a:
+            out[a - z0:b - z0] = arr[a - start:b - start]
+        return out
+
+    def add_sources(arr, start, step, scale):
+        for j, (x, y, z) in enumerate(src):
+            if start <= z < start + arr.shape[0]:
+                v = amp(j, step) if scale == 1 else amp(j, step) * f32(0.5)
+                arr[z - start, y, x] = arr[z - start, y, x] + v
+
+    g = max(k - 1, 0)
+    c2_lo, c2_hi = _exchange(C2[:g], C2[nz - g:], lo, hi, (g, H, W))
+    C2x, c2_start = with_ghosts(C2, c2_lo, c2_hi, g)
+    s = 0
+    while s < steps:
+        d = min(k, steps - s)
+        add_sources(P, zb, s, 1)                       # sources of step s (host, own planes)
+        add_sources(PP, zb, s, 0.5)
+        a_lo, a_hi = _exchange(P[:d], P[nz - d:], lo, hi, (d, H, W))
+        b_lo, b_hi = _exchange(PP[:d - 1], PP[nz - d + 1:], lo, hi, (d - 1, H, W))
+        lev = [with_ghosts(P, a_lo, a_hi, d)]           # (array, start) per level
+        prev = with_ghosts(PP, b_lo, b_hi, d - 1)       # p_prev of level 1
+        for j in range(1, d + 1):
+            z0, z1 = span(d - j)
+            src_arr, src_start = lev[j - 1]
+            Pe = take(src_arr, src_start, z0 - 1, z1 + 1)
+            pv = take(prev[0], prev[1], z0, z1)
+            c2j = take(C2x, c2_start, z0, z1)
+            out = slab_step(Pe, pv, c2j, wl.damping, sponge, z0, D)
+            if j < d:
+                add_sources(out, z0, s + j, 1)          # p_{s+j} += a
+                nz0, nz1 = span(d - j - 1)
+                nxt = take(src_arr, src_start, nz0, nz1)  # level j-1 as the next p_prev
+                add_sources(nxt, nz0, s + j, 0.5)
+                prev = (nxt, nz0)
+            lev.append((out, z0))
+        P = take(lev[d][0], lev[d][1], zb, ze)
+        PP = take(lev[d - 1][0], lev[d - 1][1], zb, ze)   # holds its step s+d-1 sources
+        s += d
+    out = [None] * world
+    dist.all_gather_object(out, (zb, P.copy(), PP.copy()))
+    if rank == 0:
+        full_p = np.concatenate([o[1] for o in sorted(out, key=lambda t: t[0])]).reshape(-1)
+        full_pp = np.concatenate([o[2] for o in sorted(out, key=lambda t: t[0])]).reshape(-1)
+        ref = oracle.from_workload(wl)
+        ref.run(steps, 1)
+        assert float(np.max(np.abs(ref.pressure))) > 1e-4   # a field worth comparing
+        result_q.put((bool(np.array_equal(full_p, ref.pressure)),
+                      bool(np.array_equal(full_pp, ref.pressure_prev))))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -311,3 +409,23 @@ def test_temporal_depth_is_decided_from_every_rank():
     assert temporal_depth([_blob(0, 8, T | F), _blob(8, 16, T)]) == 1      # c2 field on one side
     assert temporal_depth([_blob(0, 8, T, 0.25), _blob(8, 16, T, 0.2)]) == 1  # other uniform c2
     assert temporal_depth([_blob(0, 16, T)]) == 1
+
+
+@pytest.mark.parametrize("k", [1, 2, 3, 4])
+@pytest.mark.parametrize("world,wl_args", [
+    (3, ("c2", 34, 30, 33, 23)),     # sources (on ghost planes too) + sponge, 23 steps: ragged last round
+    (2, ("c3", 40, 36, 30, 18)),     # heterogeneous + sponge + centred source
+])
+def test_gloo_depth_k_slab_emulation_matches_oracle(world, wl_args, k):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main_depthk, args=(r, world, port, wl_args, k, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    codes = [p.exitcode for p in procs]
+    assert codes == [0] * world, codes
+    assert q.get(timeout=5) == (True, True)
