@@ -481,34 +481,34 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         // Items 2 .. last, three per iteration (the z queues rotate by
         // renaming).  Slabs: the main loop leaves the last item to the tail,
         // so that only the tail checks for the ghost-plane fill.
-        auto run_items = [&](auto src_tag) -> bool {
+        auto run_items = [&](auto tag) -> bool {
             bool ab = false;
             int i = 2;
-            if constexpr (!(kSlab && (decltype(src_tag)::value & 2) != 0)) {
+            if constexpr (!(kSlab && (decltype(tag)::value & 2) != 0)) {
                 for (; !ab && i + 2 <= last; i += 3) {
-                    ab = body(src_tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
-                         body(src_tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
-                         body(src_tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
+                    ab = body(tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
+                         body(tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
+                         body(tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
                 }
-                if (!ab && i <= last) ab = body(src_tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
-                if (!ab && i <= last) ab = body(src_tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
+                if (!ab && i <= last) ab = body(tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
+                if (!ab && i <= last) ab = body(tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
             } else {
                 for (; !ab && i + 3 <= last; i += 3) {
-                    ab = body(src_tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
-                         body(src_tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
-                         body(src_tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
+                    ab = body(tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
+                         body(tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
+                         body(tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
                 }
                 if (!ab && i <= last) {
                     if (i == last && fill_last) fill(false);
-                    ab = body(src_tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
+                    ab = body(tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
                 }
                 if (!ab && i <= last) {
                     if (i == last && fill_last) fill(false);
-                    ab = body(src_tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
+                    ab = body(tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
                 }
                 if (!ab && i <= last) {
                     if (fill_last) fill(false);  // i == last here
-                    ab = body(src_tag, i++, ap, am, ac, xn, xm, xc, hp, hm, hc);
+                    ab = body(tag, i++, ap, am, ac, xn, xm, xc, hp, hm, hc);
                 }
             }
             return ab;
