@@ -1,0 +1,53 @@
+"""bench.py's output contract, on CPU: the reference arm (the CPU step of the
+path, restated in oracle/) prints one JSON line with the keys the driver
+reads, and the roofline / kernel naming logic of our arm matches the library's
+launch choices.  No GPU is touched.
+"""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def run_bench(*args):
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.strip().splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    return json.loads(lines[0])
+
+
+def test_reference_arm_line():
+    d = run_bench("--impl", "reference", "--grid", "96x64x40", "--steps", "2", "--warmup", "1")
+    assert d["impl"] == "reference"
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["unit"] == "Mcells/s" and d["higher_is_better"] is True and d["value"] > 0
+    assert d["config"]["workload"] == "c3" and d["config"]["grid"] == [96, 64, 40]
+    cb = d["cpu_baseline"]
+    assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
+
+
+def test_kernel_name_follows_the_library_choice():
+    import bench
+    from rustcompute_b200 import configs
+    c3 = configs.build("c3", 512, 512, 512, steps=10)
+    narrow = configs.build("c3", 96, 64, 64, steps=10)
+    many = configs.build("c2", 256, 64, 64, steps=10)
+    many.sources = many.sources.repeat(4, axis=0)          # 40 sources: over the two-step table
+    assert bench.kernel_name("auto", c3, 1) == "k_step_tma2"
+    assert bench.kernel_name("auto", c3, 2) == "k_step_tma"              # slabs at depth 1
+    assert bench.kernel_name("auto", c3, 2, depth=2) == "k_step_tma2"    # slabs at depth 2
+    assert bench.kernel_name("auto", narrow, 1) == "k_step_zstream"      # boxes do not fit
+    assert bench.kernel_name("auto", many, 1) == "k_step_tma"
+    assert bench.kernel_name("tma", c3, 1) == "k_step_tma"
+    assert bench.kernel_name("auto", c3, 1, mode="persistent") == "k_persistent"
+    assert bench.kernel_name("auto", c3, 1, mode="resident") == "k_resident"
