@@ -1,8 +1,11 @@
-"""CPU bounds check of the step kernel's address arithmetic.
+"""CPU bounds check of the step kernels' address arithmetic.
 
 tests/index_check.cpp is compiled with g++ against the kernel's own index
 helpers (rustcompute_b200/csrc/ws3d_index.h) and replays every load and
-store of the z-streaming kernel for each launch shape below.
+store of the z-streaming and cp.async kernels for each launch shape below;
+tests/tb_index_check.cpp replays the two-step kernel's own global accesses
+(stores, stores into z-slab neighbours, loads of their edge planes) over its
+launch schedule.
 """
 import os
 import subprocess
@@ -69,3 +72,49 @@ def test_checker_catches_the_unsigned_wrap(checker, tmp_path):
     subprocess.run(["g++", "-O1", "-std=c++17", "-o", str(exe), str(probe)], check=True)
     r = subprocess.run([str(exe), "40", "36", "34", "148"], capture_output=True, text=True)
     assert r.returncode == 1 and "OUT OF BOUNDS" in r.stderr
+
+
+TB_SRC = os.path.join(ROOT, "tests", "tb_index_check.cpp")
+TB_BIN = os.path.join(ROOT, "tests", "_build", "tb_index_check")
+
+
+@pytest.fixture(scope="module")
+def tb_checker():
+    os.makedirs(os.path.dirname(TB_BIN), exist_ok=True)
+    inc = os.path.join(ROOT, "rustcompute_b200", "csrc")
+    hdr = os.path.join(inc, "ws3d_index.h")
+    if (not os.path.exists(TB_BIN) or os.path.getmtime(TB_BIN) < os.path.getmtime(TB_SRC)
+            or os.path.getmtime(TB_BIN) < os.path.getmtime(hdr)):
+        subprocess.run(["g++", "-O2", "-std=c++17", "-I", inc, "-o", TB_BIN, TB_SRC], check=True)
+    return TB_BIN
+
+
+# (W, H, nz, lower neighbour's nz, upper neighbour's nz): one GPU, first / middle / last
+# slabs, two- and three-plane slabs, ragged rows and columns, the bench sizes
+TB_CASES = [(512, 512, 512, 0, 0), (160, 24, 40, 0, 0), (129, 16, 3, 0, 0), (520, 17, 12, 0, 0),
+            (264, 24, 23, 0, 23), (264, 24, 23, 24, 23), (264, 24, 24, 23, 0),
+            (160, 40, 2, 3, 2), (160, 40, 3, 2, 2), (160, 17, 3, 2, 0), (300, 17, 30, 0, 30),
+            (384, 72, 100, 100, 100), (1024, 1024, 512, 512, 0)]
+
+
+@pytest.mark.parametrize("case", TB_CASES)
+def test_two_step_kernel_accesses_in_bounds(tb_checker, case):
+    r = subprocess.run([tb_checker, *map(str, case)], capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr + r.stdout
+
+
+def test_two_step_checker_catches_a_push_one_plane_too_far(tb_checker, tmp_path):
+    """Planted in a copy of the checker: the lower neighbour's second ghost
+    plane addressed one plane too high must be reported."""
+    src = open(TB_SRC).read()
+    bad = src.replace("(int64_t)(lo_nz + qy) * P + row", "(int64_t)(lo_nz + qy + 1) * P + row")
+    assert bad != src
+    f = tmp_path / "tb_bad.cpp"
+    f.write_text(bad)
+    exe = tmp_path / "tb_bad"
+    subprocess.run(["g++", "-O2", "-std=c++17", "-I",
+                    os.path.join(ROOT, "rustcompute_b200", "csrc"), "-o", str(exe), str(f)],
+                   check=True)
+    r = subprocess.run([str(exe), "264", "24", "23", "24", "23"], capture_output=True, text=True)
+    assert r.returncode == 1 and "Y push lo" in r.stderr
