@@ -70,6 +70,9 @@ def parse():
                     help="WxHxD: the workload's recipe at another size (profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-c5", action="store_true",
+                    help="skip the BASELINE config 5 latency figures (persistent launch vs one "
+                         "launch per step, 128^3) added to the line")
     ap.add_argument("--comparators", action="store_true",
                     help="also time the naive and reference-shaped kernels")
     return ap.parse_args()
@@ -157,80 +160,114 @@ class ClockSampler:
                 "reasons": names, "samples": len(self.samples)}
 
 
-def cpu_sample_run(wl, target_s: float = 12.0, nthreads: int = 0):
-    """Time the oracle (CPU port of the reference step, OpenMP over z-planes
-    like step_parallel) on a bounded sample of the workload: full-grid steps
-    filling ~target_s when one step takes < target_s/3, else a z-slab of the
-    same recipe."""
+def cpu_info() -> dict:
+    """CPU model and core counts of this host (recorded beside the CPU figures)."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "nproc": os.cpu_count(), "threads_allowed": host_threads()}
+
+
+def reference_sample(wl, steps: int, warmup: int, nthreads: int, budget_s: float = 150.0):
+    """The grid the CPU legs time per step: the full grid when warmup + steps
+    full-grid steps fit in about budget_s on this host, else a z-slab of the
+    same recipe (same per-cell work)."""
     import oracle
-    nthreads = nthreads or host_threads()
-    g = oracle.from_workload(wl)
-    # Step counts stay even: an odd count makes the oracle copy the fields
-    # back into the caller's arrays, which would be timed with the steps.
-    g.run(2, nthreads)                     # warm-up (first touch, thread pool)
-    # calibration: steady-state seconds per step over at least ~1 s of steps
-    n, t0 = 0, time.perf_counter()
-    while True:
-        g.run(2, nthreads)
-        n += 2
-        t1 = (time.perf_counter() - t0) / n
-        if n * t1 >= 1.0 or t1 * 3 > target_s:
-            break
-    if t1 * 3 <= target_s:
-        steps = max(2, int(target_s / max(t1, 1e-6)) // 2 * 2)
-        sample = f"{steps} full {wl.W}x{wl.H}x{wl.D} steps after {2 + n} untimed steps"
-        cells = wl.cells
-    else:
-        planes = max(8, min(wl.D, int(wl.D * target_s / 3 / t1)))
-        sub = wl.scaled(wl.W, wl.H, planes, steps=4)
-        g = oracle.from_workload(sub)
-        g.run(1, nthreads)
-        steps, cells = 2, sub.cells
-        sample = (f"2 steps of a {wl.W}x{wl.H}x{planes} slab of the {wl.name} recipe "
-                  "(same per-cell work) after 1 untimed step")
+    probe = wl.scaled(wl.W, wl.H, min(wl.D, 34), steps=4)
+    g = oracle.from_workload(probe)
+    g.run(2, nthreads)
     t0 = time.perf_counter()
-    g.run(steps, nthreads)
-    dt = time.perf_counter() - t0
-    return cells * steps / dt / 1e6, nthreads, sample, dt
+    g.run(2, nthreads)
+    rate = 2 * probe.cells / max(time.perf_counter() - t0, 1e-9)
+    budget = budget_s / max(steps + warmup, 1)
+    if wl.cells / rate <= budget:
+        return wl, f"full {wl.W}x{wl.H}x{wl.D} grid per step"
+    planes = max(8, min(wl.D, int(budget * rate / (wl.W * wl.H))))
+    sample = wl.scaled(wl.W, wl.H, planes, steps=steps + warmup + 1)
+    return sample, (f"{wl.W}x{wl.H}x{planes} z-slab of the {wl.name} recipe per step "
+                    "(bounded sample)")
+
+
+class ReferenceCpuRun:
+    """Steps warmup .. warmup + steps of `sample` on the CPU restatement of the
+    reference step (OpenMP over z-planes like step_parallel), from the
+    workload's initial state every run.
+
+    Both CPU legs time exactly these steps, because the CPU's cost per step
+    depends on where the simulation is: the spreading wave front leaves
+    subnormal values behind it (2.5 % of the cells of a 512 x 512 x 128 C3
+    grid after 300 steps), and the host pays a microcode assist for each
+    subnormal operand, so later steps run up to 2x slower (measured on the
+    oracle: 1.08 Gcells/s at step 10, 0.55 at step 312, 8 threads).  The GPU
+    handles subnormals at full rate."""
+
+    def __init__(self, sample, nthreads: int):
+        import oracle
+        self.sample, self.nthreads = sample, nthreads
+        self.g = oracle.from_workload(sample)
+        self.p0 = self.g.pressure.copy()
+        self.pp0 = self.g.pressure_prev.copy()
+
+    def run(self, steps: int, warmup: int) -> tuple[float, float]:
+        g = self.g
+        g.pressure[:] = self.p0
+        g.pressure_prev[:] = self.pp0
+        g.step, g.time = 0, np.float32(0.0)
+        g.run(warmup, self.nthreads)
+        t0 = time.perf_counter()
+        g.run(steps, self.nthreads)
+        dt = time.perf_counter() - t0
+        return self.sample.cells * steps / dt / 1e6, dt
+
+
+def cpu_baseline_leg(wl, steps: int, warmup: int, target_s: float = 10.0,
+                     max_runs: int = 25) -> dict:
+    """The bench line's cpu_baseline (rank 0, N = 1): the same steps of the same
+    sample as the reference arm (--impl reference), repeated from the initial
+    state until about target_s of timed CPU work; the median run is reported."""
+    nthreads = host_threads()
+    sample, desc = reference_sample(wl, steps, warmup, nthreads)
+    r = ReferenceCpuRun(sample, nthreads)
+    rates, secs = [], 0.0
+    while len(rates) < max_runs and (secs < target_s or not rates):
+        v, dt = r.run(steps, warmup)
+        rates.append(v)
+        secs += dt
+    return {"value": float(statistics.median(rates)), "unit": UNIT, "cores": nthreads,
+            "kind": "port",
+            "sample": f"{desc}; steps {warmup}..{warmup + steps} after {warmup} untimed steps "
+                      f"(the steps the reference arm times), median of {len(rates)} runs from "
+                      "the initial state",
+            "seconds": secs, "runs": len(rates), "min": min(rates), "max": max(rates),
+            **cpu_info()}
 
 
 def run_reference(args, wl):
     """--impl reference: the reference's CPU path (C restatement) on host cores."""
-    import oracle
     rank, world, _ = dist_env()
     if rank != 0:
         return
     nthreads = host_threads()
-    # One timed step = one full-grid step when affordable, else a z-slab sample.
-    probe = wl.scaled(wl.W, wl.H, min(wl.D, 34), steps=4)
-    g = oracle.from_workload(probe)
-    g.run(2, nthreads)                     # warm-up; even counts: no copy-back
-    t0 = time.perf_counter()
-    g.run(2, nthreads)
-    rate = 2 * probe.cells / max(time.perf_counter() - t0, 1e-9)
-    budget = 150.0 / max(args.steps + args.warmup, 1)
-    if wl.cells / rate <= budget:
-        sample, desc = wl, f"full {wl.W}x{wl.H}x{wl.D} grid per step"
-    else:
-        planes = max(8, min(wl.D, int(budget * rate / (wl.W * wl.H))))
-        sample = wl.scaled(wl.W, wl.H, planes, steps=args.steps + args.warmup + 1)
-        desc = f"{wl.W}x{wl.H}x{planes} z-slab of the {wl.name} recipe per step (bounded sample)"
-    g = oracle.from_workload(sample)
-    g.run(args.warmup, nthreads)
-    t0 = time.perf_counter()
-    g.run(args.steps, nthreads)
-    dt = time.perf_counter() - t0
-    val = sample.cells * args.steps / dt / 1e6
+    warmup = max(args.warmup, 3)
+    sample, desc = reference_sample(wl, args.steps, warmup, nthreads)
+    val, dt = ReferenceCpuRun(sample, nthreads).run(args.steps, warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+        "steps": args.steps, "warmup": warmup, "ms_per_step": dt * 1e3 / args.steps,
         "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded SplitMix64 medium and sources)",
         "config": {"workload": wl.name, "grid": [wl.W, wl.H, wl.D],
                    "heterogeneous": wl.heterogeneous, "sponge": wl.sponge_width,
                    "sources": int(len(wl.sources))},
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": nthreads, "kind": "port",
-                         "sample": desc},
+                         "sample": f"{desc}; steps {warmup}..{warmup + args.steps} after "
+                                   f"{warmup} untimed steps", **cpu_info()},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference Rust crate cannot be built in this image (no cargo, wgpu "
                 "dependency); this arm times its CPU step restated in C (oracle/)",
@@ -282,6 +319,99 @@ def kernel_name(variant, wl, world, mode="step", depth=1):
             "naive": "k_step_naive", "refshape": "k_ref_stencil+k_ref_boundary"}[variant]
 
 
+def plane_digests(field: np.ndarray, plane_cells: int) -> list:
+    """SHA-256 of every z-plane of a flat f32 field."""
+    import hashlib
+    mv = memoryview(np.ascontiguousarray(field)).cast("B")
+    step = plane_cells * 4
+    return [hashlib.sha256(mv[i:i + step]).hexdigest() for i in range(0, len(mv), step)]
+
+
+def slab_parity(b, wl, args, rank, world, local, pg, depth) -> dict:
+    """N > 1, after the timed region: every rank's slab of the final field
+    against ONE GPU (rank 0's) running the whole grid for the same number of
+    steps through the same public API, compared plane by plane via SHA-256
+    digests gathered over the process group (the reference checks its P2P
+    transfers byte for byte the same way, with a CRC, multi_gpu/runtime.rs).
+    One GPU's result equals the oracle bit for bit (tests/), so a match here
+    is bit-exactness of the z-slab exchange at this N."""
+    steps = max(args.warmup, 3) + args.steps
+    plane = wl.W * wl.H
+    mine = plane_digests(b.download_field(), plane)
+    gathered = [None] * world
+    pg.all_gather_object(gathered, mine)
+    out = {"reference": f"one GPU, whole {wl.W}x{wl.H}x{wl.D} grid, {steps} steps "
+                        "(variant auto)", "steps": steps, "halo_depth": depth}
+    if rank == 0:
+        full = make_backend(wl, "auto", local, 0, wl.D)
+        p, pp = wl.initial_fields()
+        full.upload_fields(p, pp)
+        del p, pp
+        c2 = wl.c2_field()
+        if c2 is not None:
+            full.set_c2_field(c2)
+        del c2
+        if len(wl.sources):
+            full.set_sources(wl.sources, wl.wavelet)
+        full.step_n(None, steps)
+        want = plane_digests(full.download_field(), plane)
+        full.close()
+        got = [d for r in range(world) for d in gathered[r]]
+        bad = [z for z in range(wl.D) if got[z] != want[z]]
+        out["result"] = "bit-exact" if not bad else "differs"
+        if bad:
+            out["first_differing_plane"] = bad[0]
+            out["differing_planes"] = len(bad)
+    pg.barrier()
+    return out
+
+
+def c5_latency(world, rank, local, pg, barrier, per_rank, stream, dev, device_gate) -> dict:
+    """BASELINE config 5 beside the main line: 128^3 uniform Gaussian on the same
+    GPUs (z-slabs at N > 1, halos by in-kernel peer stores and flags), all
+    10,000 steps in ONE persistent (cooperative) launch against one launch per
+    step; microseconds per step, max over ranks, CUDA events on the launch
+    stream after a device-side start gate."""
+    import torch
+    from rustcompute_b200 import configs
+    wl5 = configs.build("c5")
+    zb, ze = slab_bounds(wl5.D, world, rank)
+    b = make_backend(wl5, "auto", local, zb, ze)
+    b.set_stream(stream.cuda_stream)
+    p, pp = wl5.initial_fields(zb, ze)
+    b.upload_fields(p, pp)
+    if world > 1:
+        from rustcompute_b200.slab import connect
+        connect(b, rank, world, pg.all_gather_object, barrier)
+
+    def timed(fn) -> float:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        device_gate()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return max(per_rank(e0.elapsed_time(e1)))
+
+    b.step_n(None, 100)
+    n_launch = 2000
+    launch_ms = timed(lambda: b.step_n(None, n_launch))
+    b.step_persistent(100)
+    pers_ms = timed(lambda: b.step_persistent(wl5.steps))
+    b.sync()
+    b.close()
+    return {"grid": [wl5.W, wl5.H, wl5.D], "n_gpus": world,
+            "persistent_us_per_step": pers_ms * 1e3 / wl5.steps,
+            "persistent_steps": wl5.steps,
+            "launch_per_step_us_per_step": launch_ms * 1e3 / n_launch,
+            "launch_per_step_steps": n_launch,
+            "kernels": "k_persistent (one cooperative launch, one grid barrier per step) vs "
+                       "one k_step_zstream launch per step"}
+
+
 def run_ours(args, wl):
     import datetime
 
@@ -310,7 +440,27 @@ def run_ours(args, wl):
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         return float(t.item())
 
+    def per_rank(v: float) -> list:
+        """v from every rank, in rank order (host plumbing only)."""
+        if pg is None:
+            return [v]
+        t = torch.zeros(world, device=dev, dtype=torch.float64)
+        t[rank] = v
+        pg.all_reduce(t)
+        return [float(x) for x in t.tolist()]
+
     stream = torch.cuda.Stream(device=dev)   # a real stream (handle != 0) shared with the library
+    gate_t = torch.ones(1, device=dev)
+
+    def device_gate():
+        """N > 1: an all-reduce enqueued on the launch stream just before the
+        start event.  The event then fires on every rank when the collective
+        completes (within microseconds of each other), however far apart the
+        host threads reached this point, so no rank's timed region starts by
+        waiting for a neighbour that has not started yet."""
+        if pg is not None:
+            with torch.cuda.stream(stream):
+                pg.all_reduce(gate_t)
     p0, pp0 = wl.initial_fields(zb, ze)
     c20 = wl.c2_field(zb, ze)
 
@@ -341,11 +491,15 @@ def run_ours(args, wl):
         b._chk(b._lib.ws3d_resident_run_steps(b._ctx, max(args.warmup, 3)), "run_steps")
         b._chk(b._lib.ws3d_resident_wait_step(b._ctx, st0 + max(args.warmup, 3), 0), "wait")
     launches0 = b.stats()["kernel_launches"]
+    if world > 1:
+        b.halo_wait_stats(reset=True)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clk:
+        device_gate()
+        host_start = time.time()
         e0.record(stream)
         if args.mode == "resident":
             rs = _ffi.ws3d_resident_stats()
@@ -369,11 +523,17 @@ def run_ours(args, wl):
         torch.cuda.synchronize(dev)
     barrier()
     launches = b.stats()["kernel_launches"] - launches0
-    total_ms = max_over_ranks(host_ms if args.mode == "resident" else e0.elapsed_time(e1))
+    span_ms = per_rank(host_ms if args.mode == "resident" else e0.elapsed_time(e1))
+    total_ms = max(span_ms)
     value = wl.cells * args.steps / (total_ms * 1e-3) / 1e6
+    starts = per_rank(host_start)
+    waits = b.halo_wait_stats() if world > 1 else (0, 0)
+    wait_ns, wait_n = per_rank(float(waits[0])), per_rank(float(waits[1]))
 
     if kernel_ms is None:   # persistent / resident: the one launch is the whole timed region
-        kernel_ms = total_ms
+        kernel_ms = span_ms[rank]
+    kernel_ms_ranks = per_rank(kernel_ms)
+    kernel_ms = max(kernel_ms_ranks)   # the slowest rank's kernels
     bpc = wl.bytes_per_cell_step
     kname = kernel_name(args.variant, wl, world, args.mode, depth)
     if kname == "k_step_tma2" and args.mode == "step":
@@ -398,10 +558,11 @@ def run_ours(args, wl):
                 "bytes_per_cell_per_launch": alg_bytes // max(local_cells, 1),
                 "bytes_per_cell_step": bpc,
                 "kernel_avg_ms": avg_kernel_ms,
+                "kernel_avg_ms_per_rank": [v / n_launch for v in kernel_ms_ranks],
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"
                                if peaks["source"] == "measured" else "fallback",
                 "kernel": kernel_name(args.variant, wl, world, args.mode, depth),
-                "rank": rank}
+                "ranks": "kernel_avg_ms and frac: the slowest rank (max over ranks)"}
 
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -423,6 +584,17 @@ def run_ours(args, wl):
         "clocks": clk.summary(),
         "gpu_launches": int(launches),
     }
+    if world > 1:
+        result["ranks"] = {
+            "span_ms": span_ms,
+            "halo_wait_ms": [v * 1e-6 for v in wait_ns],
+            "halo_waits": [int(v) for v in wait_n],
+            "host_start_skew_ms": (max(starts) - min(starts)) * 1e3,
+            "start": "an all-reduce on the launch stream gates every rank's start event",
+            "note": "span = the rank's start-to-end event time; halo_wait = device time its "
+                    "step kernels spent in neighbour-flag waits that did not pass at once",
+        }
+        result["parity"] = slab_parity(b, wl, args, rank, world, local, pg, depth)
     b.close()
 
     # e2e: one whole job through the public API with pinned host buffers.
@@ -480,10 +652,12 @@ def run_ours(args, wl):
             bc.close()
         result["comparators"] = comps
 
+    if not args.no_c5 and args.mode == "step":
+        result["c5_latency"] = c5_latency(world, rank, local, pg, barrier, per_rank, stream, dev,
+                                          device_gate)
+
     if rank == 0 and world == 1 and not args.no_cpu:
-        val, cores, desc, secs = cpu_sample_run(wl)
-        result["cpu_baseline"] = {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
-                                  "sample": desc, "seconds": secs}
+        result["cpu_baseline"] = cpu_baseline_leg(wl, args.steps, max(args.warmup, 3))
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()

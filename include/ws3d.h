@@ -105,7 +105,8 @@ typedef struct ws3d_stats {
     uint32_t has_c2_field;
     uint32_t has_cell_field;
     uint32_t n_sources;
-    uint32_t reserved;
+    uint32_t two_step_launches;    /* two-step (temporally blocked) launches since create,
+                                      saturating at 2^32 - 1 */
 } ws3d_stats;
 
 typedef struct ws3d_ctx ws3d_ctx;
@@ -172,8 +173,19 @@ WS3D_API ws3d_status ws3d_step(ws3d_ctx *ctx, uint64_t n);
 /* ws3d_step plus CUDA-event timing of every step-kernel launch on the
  * context's stream; synchronises and returns the summed kernel time in ms
  * (benchmark support: bin/benchmark.rs:75-77 times step_n on the host
- * without a synchronise, this measures on the device).  n <= 2^20. */
+ * without a synchronise, this measures on the device).  n <= 2^20.  The
+ * events form a ring of 256 pairs: when the host gets 256 launches ahead it
+ * waits for the oldest one before reusing its pair. */
 WS3D_API ws3d_status ws3d_step_timed(ws3d_ctx *ctx, uint64_t n, double *kernel_ms);
+
+/* z-slab diagnostics: device nanoseconds this slab's step kernels spent in
+ * neighbour-flag waits that did not pass at once, and how many such waits
+ * there were, summed since the last reset (ws3d_halo_sync also clears them).
+ * reset != 0 clears both after reading.  Synchronises the context's stream.
+ * The reference has no device-side waits to account (its multi-GPU runtime
+ * synchronises on the host, ringkernel-cuda multi_gpu/runtime.rs:782-870). */
+WS3D_API ws3d_status ws3d_halo_wait_stats(ws3d_ctx *ctx, uint64_t *wait_ns, uint64_t *waits,
+                                          int reset);
 
 /* PersistentBackend::step (persistent_backend.rs:269-336): n steps inside ONE
  * cooperative launch (the reference's persistent kernel, generated by
@@ -201,11 +213,11 @@ WS3D_API ws3d_status ws3d_inject_spherical_impulse(ws3d_ctx *ctx, uint32_t cx, u
 WS3D_API ws3d_status ws3d_energy(ws3d_ctx *ctx, double *sum_sq);
 
 /* Energy (sum of p^2, accumulated in f64) of a caller-owned device field,
- * for callers that cannot allocate device memory when they need it: work
- * being recorded into a CUDA graph (stream capture rejects cudaMalloc),
- * real-time loops that must not block on the device synchronisation that
- * cudaMalloc/cudaFree imply, and host applications that own all device memory
- * and forbid libraries from allocating.  No counterpart in the reference.
+ * for callers that cannot allocate device memory when they need it: real-time
+ * loops (an audio callback sampling the field) that must not block on the
+ * device synchronisation cudaMalloc/cudaFree can imply, and host applications
+ * that own all device memory through their own pool and forbid libraries from
+ * allocating.  No counterpart in the reference.
  *
  * field:  device pointer, nz planes of height rows, row pitch `pitch` floats
  *         (pitch >= width; pitch == width for a dense z-major array).
@@ -217,7 +229,11 @@ WS3D_API ws3d_status ws3d_energy(ws3d_ctx *ctx, double *sum_sq);
  * WS3D_STATIC_ENERGY_MAX_PLANES doubles (one per plane, 64 KiB) that every
  * GPU loading this library holds until exit; nz above that limit is
  * rejected with WS3D_EINVAL.  The first call on a device resolves the
- * array's device address: make that first call outside any stream capture.
+ * array's device address (set-up, once per device): make that first call
+ * before any stream capture.  The address stays cached, so calls after a
+ * cudaDeviceReset of that device are not supported.  A CUDA error that is
+ * already pending when the call starts is reported (WS3D_ELAUNCH) and left
+ * pending; nothing is launched then.
  * All calls on a device share the array, so calls that overlap on the GPU
  * (different streams, no ordering between them) race; each call writes every
  * entry it reads, so nothing carries over from an earlier call. */

@@ -68,7 +68,7 @@ class ws3d_stats(C.Structure):
         ("has_c2_field", C.c_uint32),
         ("has_cell_field", C.c_uint32),
         ("n_sources", C.c_uint32),
-        ("reserved", C.c_uint32),
+        ("two_step_launches", C.c_uint32),
     ]
 
 
@@ -207,6 +207,8 @@ SIGNATURES = {
     "ws3d_set_sources": (C.c_int, [_CTX, C.c_uint32, _U32, _F, C.c_uint64]),
     "ws3d_step": (C.c_int, [_CTX, C.c_uint64]),
     "ws3d_step_timed": (C.c_int, [_CTX, C.c_uint64, C.POINTER(C.c_double)]),
+    "ws3d_halo_wait_stats": (C.c_int, [_CTX, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                       C.c_int]),
     "ws3d_step_persistent": (C.c_int, [_CTX, C.c_uint64]),
     "ws3d_inject_impulse": (C.c_int, [_CTX, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float]),
     "ws3d_inject_spherical_impulse": (

@@ -203,6 +203,14 @@ class GpuBackend3D:
         self._chk(self._lib.ws3d_step_timed(self._ctx, int(n), C.byref(out)), "step_timed")
         return float(out.value)
 
+    def halo_wait_stats(self, reset: bool = False) -> tuple[int, int]:
+        """z-slabs: (device ns spent in neighbour-flag waits that did not pass at
+        once, number of such waits) since the last reset.  Synchronises."""
+        ns, cnt = C.c_uint64(), C.c_uint64()
+        self._chk(self._lib.ws3d_halo_wait_stats(self._ctx, C.byref(ns), C.byref(cnt),
+                                                 1 if reset else 0), "halo_wait_stats")
+        return int(ns.value), int(cnt.value)
+
     def download_pressure(self, grid: SimulationGrid3D, with_prev: bool = False) -> None:
         """gpu_backend.rs:383-388 (synchronous)."""
         p = np.empty(self.n_local, dtype=np.float32)

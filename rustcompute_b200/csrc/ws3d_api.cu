@@ -6,6 +6,7 @@
 // instead of copying, exactly like gpu_backend.rs:372.
 #include "ws3d.h"
 #include "ws3d_kernels.cuh"
+#include "ws3d_nvtx.h"
 #include "ws3d_async.cuh"
 #include "ws3d_persistent.cuh"
 #include "ws3d_tb.cuh"
@@ -98,8 +99,12 @@ struct ws3d_ctx {
     uint64_t halo_steps = 0;         // steps since the last halo sync
     uint64_t budget_ns = 2000000000ull;
 
-    // optional per-launch timing of the step kernel (ws3d_step_timed)
+    // optional per-launch timing of the step kernel (ws3d_step_timed): a ring
+    // of kTimedRing event pairs; tev_rec launches recorded, the first
+    // tev_done of them already summed into tev_ms
     std::vector<cudaEvent_t> tev;
+    uint64_t tev_rec = 0, tev_done = 0;
+    double tev_ms = 0.0;
 
     // TMA kernels: tensor maps of every field buffer in every role and of c2
     // (index = buffer; permuted together with buf[] after a two-step launch)
@@ -152,6 +157,12 @@ struct ws3d_ctx {
 };
 
 namespace {
+
+constexpr size_t kFlagWords = 32;
+// Flag block words: 0 / 1 the lower / upper neighbour's flag, 2 status, 4 / 5
+// the persistent grid barrier, 6 the resident kernel's decision, 8 / 9 the
+// neighbour-wait accumulators (ns, count).
+constexpr size_t kWaitAccWord = 8;
 
 struct DeviceGuard {
     int prev = -1;
@@ -290,6 +301,7 @@ StepParams make_params(const ws3d_ctx* c) {
     // of the persistent and resident kernels (one GPU too)
     a.budget_ns = c->budget_ns;
     a.status = reinterpret_cast<unsigned int*>(c->flags + 2);
+    a.wait_acc = c->flags + kWaitAccWord;
     return a;
 }
 
@@ -323,7 +335,7 @@ ws3d_status d2h_pitched(ws3d_ctx* c, T* dst, const T* src_slab, ws3d_status code
 
 // Halo flag block: [0] raised by the lower neighbour, [1] by the upper one,
 // [2] status word; padded to 256 bytes.
-constexpr size_t kFlagWords = 32;
+
 
 // Launch geometry of the z-streaming kernel (ws3d_index.h).
 constexpr int kTY = 8;
@@ -1046,6 +1058,7 @@ const char* ws3d_last_error(const ws3d_ctx* c) { return c ? c->err.c_str() : "";
 ws3d_status ws3d_upload(ws3d_ctx* c, const float* p, const float* pp) {
     WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
+    NvtxRange nv("ws3d.upload", kNvtxTransfer);
     DeviceGuard g(c->desc.device);
     ws3d_status s = WS3D_OK;
     if (p && (s = h2d_pitched(c, c->buf[c->ip], p)) != WS3D_OK) return s;
@@ -1058,6 +1071,7 @@ ws3d_status ws3d_upload(ws3d_ctx* c, const float* p, const float* pp) {
 ws3d_status ws3d_download(ws3d_ctx* c, float* p, float* pp) {
     WS3D_NOT_RESIDENT(c);
     if (!c || !p) return c ? fail(c, WS3D_EINVAL, "download: pressure is NULL") : WS3D_EINVAL;
+    NvtxRange nv("ws3d.download", kNvtxTransfer);
     DeviceGuard g(c->desc.device);
     ws3d_status s = d2h_pitched(c, p, c->buf[c->ip], WS3D_EMEMORY);
     if (s == WS3D_OK && pp) s = d2h_pitched(c, pp, c->buf[c->ipp], WS3D_EMEMORY);
@@ -1225,31 +1239,62 @@ bool use_two_step(ws3d_ctx* c) {
     return c->n_src <= (uint32_t)kTbMaxSrc && tb_kernel_ok(c);
 }
 
-// Advances n steps; with `timed`, records an event pair around every step
-// launch and returns the number of launches in *nlaunch.
-ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed, uint64_t* nlaunch = nullptr) {
-    if (c->halo && c->host_ordered)
-        return fail(c, WS3D_ECOMMAND, "step: same-device slabs advance through ws3d_step_group");
-    if (c->halo && !c->halo_synced)
-        return fail(c, WS3D_ECOMMAND, "step: fields changed since the last ws3d_halo_sync");
-    if (timed) {
-        while (c->tev.size() < 2 * n) {
+// Timed launches keep their event pairs in a ring of kTimedRing slots: a
+// slot is reused only after the pair recorded in it kTimedRing launches
+// earlier has been read (the host waits for that old launch, which leaves
+// kTimedRing - 1 launches queued), so the event count stays bounded.
+constexpr uint64_t kTimedRing = 256;
+
+// Sum the elapsed time of up to `max` of the oldest unread pairs into tev_ms.
+ws3d_status timed_fold(ws3d_ctx* c, uint64_t max) {
+    for (; c->tev_done < c->tev_rec && max > 0; --max) {
+        const size_t slot = (size_t)(c->tev_done % kTimedRing);
+        WS3D_CUDA(c, cudaEventSynchronize(c->tev[2 * slot + 1]), WS3D_ELAUNCH);
+        float ms = 0.f;
+        WS3D_CUDA(c, cudaEventElapsedTime(&ms, c->tev[2 * slot], c->tev[2 * slot + 1]),
+                  WS3D_EDEVICE);
+        c->tev_ms += ms;
+        c->tev_done++;
+    }
+    return WS3D_OK;
+}
+
+// Record the start (end = false) or end event of timed launch tev_rec.
+ws3d_status timed_mark(ws3d_ctx* c, bool end) {
+    const size_t slot = (size_t)(c->tev_rec % kTimedRing);
+    if (!end) {
+        if (c->tev_rec - c->tev_done >= kTimedRing) {
+            ws3d_status s = timed_fold(c, 1);
+            if (s != WS3D_OK) return s;
+        }
+        while (c->tev.size() < 2 * (slot + 1)) {
             cudaEvent_t ev;
             WS3D_CUDA(c, cudaEventCreate(&ev), WS3D_EDEVICE);
             c->tev.push_back(ev);
         }
     }
+    WS3D_CUDA(c, cudaEventRecord(c->tev[2 * slot + (end ? 1 : 0)], c->stream), WS3D_EDEVICE);
+    if (end) c->tev_rec++;
+    return WS3D_OK;
+}
+
+// Advances n steps; with `timed`, records an event pair around every step
+// launch (timed_mark).
+ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed) {
+    if (c->halo && c->host_ordered)
+        return fail(c, WS3D_ECOMMAND, "step: same-device slabs advance through ws3d_step_group");
+    if (c->halo && !c->halo_synced)
+        return fail(c, WS3D_ECOMMAND, "step: fields changed since the last ws3d_halo_sync");
     if (c->halo && c->hdepth == 2 && !tma_eligible(c))
         return fail(c, WS3D_ECOMMAND,
                     "step: temporal depth 2 needs the TMA kernels (default faces, W > 128, H >= 16)");
-    uint64_t ev = 0;
     for (uint64_t i = 0; i < n;) {
         // sources of this step and, on slabs, the one signal per launch that
         // lets the neighbours' next launch start
         ws3d_status s = launch_sources(c, c->halo);
         if (s != WS3D_OK) return s;
         const bool two = n - i >= 2 && use_two_step(c);
-        if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
+        if (timed && (s = timed_mark(c, false)) != WS3D_OK) return s;
         if (two) {
             // sources of step t went into A and B above; the kernel applies
             // those of step t+1 between its two steps
@@ -1258,13 +1303,12 @@ ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed, uint64_t* nlaunch = n
             std::swap(c->ip, c->ipp);
         }
         if (s != WS3D_OK) return s;
-        if (timed) WS3D_CUDA(c, cudaEventRecord(c->tev[ev++], c->stream), WS3D_EDEVICE);
+        if (timed && (s = timed_mark(c, true)) != WS3D_OK) return s;
         c->step += two ? 2 : 1;
         i += two ? 2 : 1;
         c->halo_steps++;
         c->deep_ok = true;  // both launches store two edge planes at temporal depth 2
     }
-    if (nlaunch) *nlaunch = ev / 2;
     return WS3D_OK;
 }
 }  // namespace
@@ -1272,6 +1316,7 @@ ws3d_status step_impl(ws3d_ctx* c, uint64_t n, bool timed, uint64_t* nlaunch = n
 ws3d_status ws3d_step(ws3d_ctx* c, uint64_t n) {
     WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
+    NvtxRange nv("ws3d.steps", kNvtxKernel);
     DeviceGuard g(c->desc.device);
     return step_impl(c, n, false);
 }
@@ -1281,19 +1326,30 @@ ws3d_status ws3d_step_timed(ws3d_ctx* c, uint64_t n, double* kernel_ms) {
     if (!c || !kernel_ms) return c ? fail(c, WS3D_EINVAL, "step_timed: kernel_ms is NULL")
                                    : WS3D_EINVAL;
     if (n > (1u << 20)) return fail(c, WS3D_EINVAL, "step_timed: more than 2^20 steps");
+    NvtxRange nv("ws3d.steps_timed", kNvtxKernel);
     DeviceGuard g(c->desc.device);
-    uint64_t nl = 0;
-    ws3d_status s = step_impl(c, n, true, &nl);
+    c->tev_rec = c->tev_done = 0;
+    c->tev_ms = 0.0;
+    ws3d_status s = step_impl(c, n, true);
     if (s != WS3D_OK) return s;
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_ELAUNCH);
-    double tot = 0.0;
-    for (uint64_t i = 0; i < nl; ++i) {
-        float ms = 0.f;
-        WS3D_CUDA(c, cudaEventElapsedTime(&ms, c->tev[2 * i], c->tev[2 * i + 1]), WS3D_EDEVICE);
-        tot += ms;
-    }
-    *kernel_ms = tot;
+    if ((s = timed_fold(c, c->tev_rec)) != WS3D_OK) return s;
+    *kernel_ms = c->tev_ms;
     return check_device_status(c);
+}
+
+ws3d_status ws3d_halo_wait_stats(ws3d_ctx* c, uint64_t* wait_ns, uint64_t* waits, int reset) {
+    if (!c) return WS3D_EINVAL;
+    DeviceGuard g(c->desc.device);
+    unsigned long long v[2] = {0, 0};
+    WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_ELAUNCH);
+    WS3D_CUDA(c, cudaMemcpy(v, c->flags + kWaitAccWord, sizeof v, cudaMemcpyDeviceToHost),
+              WS3D_EDEVICE);
+    if (wait_ns) *wait_ns = v[0];
+    if (waits) *waits = v[1];
+    if (reset)
+        WS3D_CUDA(c, cudaMemset(c->flags + kWaitAccWord, 0, sizeof v), WS3D_EDEVICE);
+    return WS3D_OK;
 }
 
 namespace {
@@ -1492,6 +1548,7 @@ ws3d_status ws3d_stats_get(const ws3d_ctx* c, ws3d_stats* o) {
     o->has_c2_field = c->c2f != nullptr;
     o->has_cell_field = !c->cells_default;
     o->n_sources = c->n_src;
+    o->two_step_launches = (uint32_t)std::min<uint64_t>(c->tb_launches, 0xffffffffull);
     return WS3D_OK;
 }
 
@@ -1499,6 +1556,7 @@ ws3d_status ws3d_stats_get(const ws3d_ctx* c, ws3d_stats* o) {
 ws3d_status ws3d_step_persistent(ws3d_ctx* c, uint64_t n) {
     WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
+    NvtxRange nv("ws3d.steps_persistent", kNvtxKernel);
     if (c->halo && c->host_ordered)
         return fail(c, WS3D_ECOMMAND, "step_persistent: same-device slab groups step through "
                                       "ws3d_step_group");
@@ -1627,6 +1685,7 @@ bool same_geometry(const ws3d_ctx* c, uint32_t W, uint32_t H, uint32_t D, uint32
 ws3d_status ws3d_halo_export(ws3d_ctx* c, ws3d_halo_handles* out) {
     WS3D_NOT_RESIDENT(c);
     if (!c || !out) return c ? fail(c, WS3D_EINVAL, "halo_export: out is NULL") : WS3D_EINVAL;
+    NvtxRange nv("ws3d.connect.export", kNvtxSync);
     static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
     static_assert(sizeof(ws3d_halo_handles) == 424, "ws3d_halo_handles layout");
     DeviceGuard g(c->desc.device);
@@ -1660,6 +1719,7 @@ ws3d_status ws3d_halo_export(ws3d_ctx* c, ws3d_halo_handles* out) {
 ws3d_status ws3d_halo_attach(ws3d_ctx* c, const ws3d_halo_handles* lo, const ws3d_halo_handles* hi) {
     WS3D_NOT_RESIDENT(c);
     if (!c) return WS3D_EINVAL;
+    NvtxRange nv("ws3d.connect.attach", kNvtxSync);
     if (c->halo) return fail(c, WS3D_EPEER, "halo_attach: neighbours already attached");
     if (lo && (!same_geometry(c, lo->width, lo->height, lo->depth, lo->pitch) || lo->z_end != c->z0))
         return fail(c, WS3D_EINVAL, "halo_attach: lower slab [%u,%u) does not end at %u or differs in shape",
@@ -1795,6 +1855,7 @@ ws3d_status ws3d_halo_sync(ws3d_ctx* c, uint32_t phase) {
     if (!c) return WS3D_EINVAL;
     if (!c->halo) return WS3D_OK;
     if (phase > 1) return fail(c, WS3D_EINVAL, "halo_sync: phase must be 0 or 1");
+    NvtxRange nv(phase == 0 ? "ws3d.connect.quiesce" : "ws3d.connect.halo_sync", kNvtxSync);
     DeviceGuard g(c->desc.device);
     // Phase 0: quiesce -- after it (and the barrier that follows on every
     // rank) no signal of an earlier step is still in flight towards anyone.

@@ -132,9 +132,9 @@ k_step_async(StepParams a, AsyncSched sc) {
                 ((a.wait_lo && is.zs == 0) || (a.wait_hi && is.ze == a.nz))) {
                 if (lane == 0) {
                     unsigned int bad = 0;
-                    if (a.wait_lo && is.zs == 0 && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns))
+                    if (a.wait_lo && is.zs == 0 && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns, a.wait_acc))
                         bad |= 1u;
-                    if (a.wait_hi && is.ze == a.nz && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns))
+                    if (a.wait_hi && is.ze == a.nz && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns, a.wait_acc))
                         bad |= 2u;
                     if (bad) atomicOr(a.status, bad);
                 }

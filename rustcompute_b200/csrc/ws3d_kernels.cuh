@@ -48,6 +48,9 @@ struct StepParams {
     unsigned long long wait_val;         // both flags must reach this value first
     unsigned long long budget_ns;        // bounded wait
     unsigned int* status;                // error word (bit 0: lower wait, bit 1: upper wait)
+    // [0] device ns spent in neighbour-flag waits that did not pass at once,
+    // [1] the number of such waits (both summed over launches; z-slabs)
+    unsigned long long* wait_acc;
 };
 
 // ---------------------------------------------------------------------------
@@ -69,16 +72,27 @@ __device__ __forceinline__ unsigned long long global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// `acc` (optional): a wait that did not pass at once adds its duration in ns
+// to acc[0] and 1 to acc[1].
 __device__ __noinline__ bool wait_flag_geq(const unsigned long long* f, unsigned long long v,
-                                           unsigned long long budget_ns) {
+                                           unsigned long long budget_ns,
+                                           unsigned long long* acc = nullptr) {
     if (ld_acquire_sys(f) >= v) return true;
     const unsigned long long t0 = global_ns();
+    bool ok = false;
     for (unsigned int it = 1; it < (1u << 26); ++it) {
         __nanosleep(128);
-        if (ld_acquire_sys(f) >= v) return true;
-        if ((it & 31u) == 0 && global_ns() - t0 > budget_ns) return false;
+        if (ld_acquire_sys(f) >= v) {
+            ok = true;
+            break;
+        }
+        if ((it & 31u) == 0 && global_ns() - t0 > budget_ns) break;
     }
-    return false;
+    if (acc) {
+        atomicAdd(acc, global_ns() - t0);
+        atomicAdd(acc + 1, 1ull);
+    }
+    return ok;
 }
 
 // Raise the neighbours' flags after this GPU's step kernel has completed
@@ -260,8 +274,8 @@ __device__ __forceinline__ void zs_tile(const StepParams& a, uint32_t bx, uint32
         if (need_lo || need_hi) {
             if (threadIdx.x == 0 && threadIdx.y == 0) {
                 unsigned int bad = 0;
-                if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns)) bad |= 1u;
-                if (need_hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns)) bad |= 2u;
+                if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns, a.wait_acc)) bad |= 1u;
+                if (need_hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns, a.wait_acc)) bad |= 2u;
                 if (bad) atomicOr(a.status, bad);
             }
             __syncthreads();

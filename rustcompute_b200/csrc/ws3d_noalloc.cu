@@ -2,14 +2,18 @@
 //
 // ws3d_energy() reduces through a scratch buffer that ws3d_create() obtained
 // with cudaMalloc.  Some callers cannot allocate device memory at the point
-// where they want this number: code being recorded into a CUDA graph (stream
-// capture rejects cudaMalloc/cudaFree), a real-time loop such as an audio
-// callback that must never block on the implicit device synchronisation of
-// cudaMalloc/cudaFree, or a host application that owns every byte of device
-// memory through its own pool and forbids libraries from allocating.  For
-// them, ws3d_field_energy_static() reduces a caller-owned device field into a
+// where they want this number: a real-time loop such as an audio callback
+// that must never block on the device synchronisation cudaMalloc/cudaFree
+// can imply, or a host application that owns every byte of device memory
+// through its own pool and forbids libraries from allocating.  For them,
+// ws3d_field_energy_static() reduces a caller-owned device field into a
 // caller-owned device result and keeps its scratch in the fixed array below,
 // which every GPU that loads this library holds until the process exits.
+//
+// The array's device address is looked up once per device and cached; a
+// cudaDeviceReset() of that device destroys the module that holds it, so
+// calls after such a reset are not supported (the rest of the library's
+// device state does not survive a reset either).
 #include "ws3d.h"
 
 #include <cuda_runtime.h>
@@ -54,17 +58,21 @@ __device__ double block_sum(double v) {
 
 // Block z sums p^2 over plane z (W x H cells, row pitch `pitch` floats) and
 // writes partials[z]; every partial the fold reads is written by this launch.
+// Each warp walks whole rows (warp w takes rows w, w + 16, ...), its lanes
+// stride along the row: coalesced, and no per-element index division.
 __global__ void __launch_bounds__(kThreads) k_plane_energy(const float* __restrict__ field,
                                                            uint32_t W, uint32_t H,
                                                            uint32_t pitch, double* partials) {
     const uint32_t z = blockIdx.x;
     const float* plane = field + (size_t)z * H * pitch;
     double acc = 0.0;
-    const uint64_t n = (uint64_t)W * H;
-    for (uint64_t i = threadIdx.x; i < n; i += kThreads) {
-        const uint64_t y = i / W, x = i - y * W;
-        const float v = plane[y * pitch + x];
-        acc += (double)v * (double)v;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    for (uint32_t y = warp; y < H; y += kThreads / 32) {
+        const float* row = plane + (size_t)y * pitch;
+        for (uint32_t x = lane; x < W; x += 32) {
+            const float v = row[x];
+            acc += (double)v * (double)v;
+        }
     }
     acc = block_sum(acc);
     if (threadIdx.x == 0) partials[z] = acc;
@@ -105,8 +113,15 @@ extern "C" ws3d_status ws3d_field_energy_static(const float* field, uint32_t wid
     if (pitch < width)
         return report(errbuf, errlen, WS3D_EINVAL,
                       "field_energy_static: pitch %u is smaller than width %u", pitch, width);
+    // An error the caller's own earlier work left pending is reported, not
+    // consumed: it stays pending for the caller, and nothing is launched.
+    cudaError_t e = cudaPeekAtLastError();
+    if (e != cudaSuccess)
+        return report(errbuf, errlen, WS3D_ELAUNCH,
+                      "field_energy_static: a CUDA error was already pending before this call "
+                      "(%s); nothing was launched", cudaGetErrorString(e));
     int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
+    e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
         return report(errbuf, errlen, WS3D_EDEVICE, "field_energy_static: no current device (%s)",
                       cudaGetErrorString(e));
@@ -115,8 +130,8 @@ extern "C" ws3d_status ws3d_field_energy_static(const float* field, uint32_t wid
         std::lock_guard<std::mutex> lock(g_setup_mutex);
         if (!g_partials_addr[dev]) {
             // First call on this device: resolve the array's device address
-            // with the device current.  Not capturable: make this first call
-            // outside any stream capture.
+            // with the device current.  This set-up belongs before any stream
+            // capture: make the first call on each device outside one.
             void* addr = nullptr;
             e = cudaGetSymbolAddress(&addr, g_plane_partials);
             if (e != cudaSuccess || !addr)

@@ -195,8 +195,8 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const bool need_hi = kSlab && a.wait_hi && ze + 1 >= (int)a.nz;
             if (need_lo || need_hi) {
                 unsigned int bad = 0;
-                if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns)) bad |= 1u;
-                if (need_hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns)) bad |= 2u;
+                if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns, a.wait_acc)) bad |= 1u;
+                if (need_hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns, a.wait_acc)) bad |= 2u;
                 if (bad) atomicOr(a.status, bad);
                 // the neighbour's stores into our ghost planes, acquired above,
                 // before our TMA loads of them

@@ -170,8 +170,8 @@ k_step_tma(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUte
             const bool need_hi = a.wait_hi && r.ze + (a.peer_hi2 ? 1u : 0u) >= a.nz;
             if (need_lo || need_hi) {
                 unsigned int bad = 0;
-                if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns)) bad |= 1u;
-                if (need_hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns)) bad |= 2u;
+                if (need_lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns, a.wait_acc)) bad |= 1u;
+                if (need_hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns, a.wait_acc)) bad |= 2u;
                 if (bad) atomicOr(a.status, bad);
                 // the neighbour's ghost-plane stores, acquired above, before our TMA loads
                 asm volatile("fence.proxy.async.global;" ::: "memory");

@@ -1,6 +1,7 @@
 """Regenerate the golden fixtures in this directory from the CPU oracle.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py          # golden.json, slices, ragged case
+    python tests/golden/make_golden.py --full   # golden_full.json (minutes, ~40 GB RAM)
 
 The reference ships no field dumps for this path (its tests check only
 qualitative properties), and its Rust crate cannot be built in this image, so
@@ -8,6 +9,12 @@ the fixtures are produced by the pinned C restatement in oracle/.  Each case
 stores SHA-256 digests of the final pressure / pressure_prev bytes plus energy
 and peak; the C1 case also stores its three centre slices, and one ragged case
 stores its whole fields.
+
+`--full` runs the five BASELINE configurations at their stated sizes and step
+counts (C2 256^3 x 1000, C3 512^3 x 500, C4 1024^3 x 200, C5 128^3 x 10,000;
+C1 is in golden.json already) on all host threads and stores the same digests
+in golden_full.json.  tests/test_full_configs_gpu.py checks the CUDA path
+against them and, in the same run, against the oracle on the GPU box's cores.
 """
 import hashlib
 import json
@@ -63,7 +70,45 @@ def workload(name, dims):
     return configs.build(name, W, H, D, steps=steps)
 
 
+FULL_CASES = [
+    ("c2_full", "c2"),
+    ("c3_full", "c3"),
+    ("c4_full", "c4"),
+    ("c5_full", "c5"),
+]
+
+
+def full_main():
+    import time
+    path = os.path.join(HERE, "golden_full.json")
+    out = {}
+    if os.path.exists(path):
+        with open(path) as fh:
+            out = json.load(fh)
+    only = [a for a in sys.argv[1:] if not a.startswith("--")]
+    for key, name in FULL_CASES:
+        if only and key not in only:
+            continue
+        wl = configs.build(name)
+        t0 = time.perf_counter()
+        g = oracle.from_workload(wl)
+        g.run(wl.steps, oracle.max_threads())
+        out[key] = {"workload": name, "grid": [wl.W, wl.H, wl.D], "steps": wl.steps,
+                    "sha256_pressure": digest(g.pressure),
+                    "sha256_pressure_prev": digest(g.pressure_prev),
+                    "energy": float(np.dot(g.pressure.astype(np.float64),
+                                           g.pressure.astype(np.float64))),
+                    "max_pressure": float(np.max(np.abs(g.pressure)))}
+        print(key, f"{time.perf_counter() - t0:.1f} s", json.dumps(out[key]), flush=True)
+        del g
+        with open(path, "w") as fh:
+            json.dump(out, fh, indent=1, sort_keys=True)
+
+
 def main():
+    if "--full" in sys.argv:
+        full_main()
+        return
     out = {}
     for key, name, dims in CASES:
         wl = workload(name, dims)

@@ -88,10 +88,3 @@ def test_no_cpu_fallback_in_package():
             if f.endswith(".py"):
                 src = open(os.path.join(dirpath, f)).read()
                 assert "import oracle" not in src and "from oracle" not in src, f
-
-
-def test_integration_doc_binds_every_entry_point():
-    """INTEGRATION.md's Rust binding names every function include/ws3d.h declares."""
-    names = header_functions(os.path.join(ROOT, "include", "ws3d.h"))
-    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    assert [n for n in names if f"fn {n}(" not in doc and n not in doc] == []

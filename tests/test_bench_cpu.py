@@ -51,3 +51,27 @@ def test_kernel_name_follows_the_library_choice():
     assert bench.kernel_name("tma", c3, 1) == "k_step_tma"
     assert bench.kernel_name("auto", c3, 1, mode="persistent") == "k_persistent"
     assert bench.kernel_name("auto", c3, 1, mode="resident") == "k_resident"
+
+
+def test_cpu_legs_time_the_same_steps_from_the_initial_state():
+    """cpu_baseline and the reference arm time steps W..W+K of the same sample;
+    every cpu_baseline run restarts from the workload's initial state, so each
+    run computes the same fields."""
+    import numpy as np
+
+    import bench
+    from rustcompute_b200 import configs
+    wl = configs.build("c3", 64, 48, 40, steps=12)
+    sample, desc = bench.reference_sample(wl, 6, 3, 2)
+    assert sample is wl and desc.startswith("full 64x48x40")
+    r = bench.ReferenceCpuRun(sample, 2)
+    v1, dt1 = r.run(6, 3)
+    p1 = r.g.pressure.copy()
+    v2, dt2 = r.run(6, 3)
+    assert v1 > 0 and v2 > 0 and dt1 > 0 and dt2 > 0
+    assert r.g.step == 9
+    assert np.array_equal(p1.view(np.uint32), r.g.pressure.view(np.uint32))
+    cb = bench.cpu_baseline_leg(wl, 6, 3, target_s=0.05, max_runs=3)
+    assert cb["kind"] == "port" and cb["unit"] == "Mcells/s" and 1 <= cb["runs"] <= 3
+    assert cb["min"] <= cb["value"] <= cb["max"]
+    assert "steps 3..9" in cb["sample"] and cb["nproc"] >= 1

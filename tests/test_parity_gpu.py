@@ -266,9 +266,11 @@ def test_errors_are_raised_not_swallowed():
 
 def test_full_size_c3_kernels_agree_and_match_oracle():
     """BASELINE config 3 at full size (512^3, heterogeneous, sponge, source):
-    size-independent checks -- three independent kernels (TMA pipeline,
-    z-stream, one thread per cell) agree bit for bit after 20 steps, and the
-    TMA kernel agrees with the oracle (all host threads) after 2."""
+    size-independent checks -- independent kernels (TMA pipeline, z-stream,
+    one thread per cell, and the auto path bench.py times, which runs the
+    two-step kernel for every pair of steps) agree bit for bit after 20
+    steps, and the TMA kernel agrees with the oracle (all host threads) after
+    2.  The full 500 steps against the oracle are in test_full_configs_gpu.py."""
     wl = configs.build("c3")
     gt, bt = gpu_for(wl, "tma")
     bt.step_n(gt, 2)
@@ -280,9 +282,11 @@ def test_full_size_c3_kernels_agree_and_match_oracle():
     bt.step_n(gt, 18)
     pt = bt.download_field()
     bt.close()
-    for v in ("async", "zstream", "naive"):
+    for v in ("auto", "tma2", "async", "zstream", "naive"):
         g, b = gpu_for(wl, v)
         b.step_n(g, 20)
+        if v in ("auto", "tma2"):
+            assert b.stats()["two_step_launches"] == 10, v
         assert np.array_equal(b.download_field().view(np.uint32), pt.view(np.uint32)), v
         b.close()
     assert float(np.max(np.abs(pt))) > 0

@@ -1,7 +1,7 @@
 """ws3d_field_energy_static: the energy reduction for callers that cannot
-allocate device memory (graph capture, real-time loops, hosts that own all
-device memory).  Its scratch is a fixed device array inside the library; the
-caller passes the field and the result slot.
+allocate device memory (real-time loops that must not block on cudaMalloc,
+hosts that own all device memory).  Its scratch is a fixed device array inside
+the library; the caller passes the field and the result slot.
 
 Checked against the existing entry point (ws3d_energy, which reduces through
 scratch allocated at context creation) on two calls in a row, with the
