@@ -11,10 +11,17 @@ id) plus raw data.  The state of a leapfrog step is the pair (pressure,
 pressure_prev) plus the step counter; both fields are stored as
 DeviceMemory chunks (type 5) in z-major f32, "pressure" first.
 
-Chunk ids: the reference hashes the region name with Rust's DefaultHasher;
-here the id is the 64-bit FNV-1a hash of the name (readers select the
-DeviceMemory chunks by order).  Like the reference's reader, files above
-1 GiB are refused unless allow_large=True (the reference cannot read them).
+Chunk ids: the reference ids a DeviceMemory chunk by hashing its region
+name with Rust's std DefaultHasher (checkpoint.rs:600-606), which is
+SipHash-1-3 with both keys zero over the name's UTF-8 bytes followed by one
+0xFF byte (str's Hash writes the bytes and a 0xFF terminator).  The same id
+is computed here (`region_id`, SipHash restated from Aumasson & Bernstein,
+"SipHash: a fast short-input PRF", 2012), so chunk_identity (:783-797),
+content_digest (:806-818) and delta diffing agree with checkpoints the
+reference writes for the same region names.  restore() picks the fields by
+id, and by order for files whose ids it does not know.  Like the reference's
+reader, files above 1 GiB are refused unless allow_large=True (the reference
+cannot read them).
 """
 from __future__ import annotations
 
@@ -32,11 +39,112 @@ CHUNK_DEVICE_MEMORY = 5
 CHUNK_CUSTOM = 100
 
 
-def fnv1a64(name: str) -> int:
-    h = 0xCBF29CE484222325
-    for b in name.encode():
-        h = ((h ^ b) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
-    return h
+MASK64 = 0xFFFFFFFFFFFFFFFF
+DELTA_PARENT_DIGEST_KEY = "ringkernel.delta.parent_digest"   # checkpoint.rs:776
+
+
+def _rotl(x: int, b: int) -> int:
+    return ((x << b) | (x >> (64 - b))) & MASK64
+
+
+def siphash(k0: int, k1: int, data: bytes, c_rounds: int = 1, d_rounds: int = 3) -> int:
+    """SipHash-c-d of `data` under the 128-bit key (k0, k1), little-endian words,
+    as the SipHash paper specifies it: four 64-bit state words initialised from
+    the key and the constants "somepseudorandomlygeneratedbytes", c SipRounds
+    per 8-byte message word, the last word carrying len mod 256 in its top
+    byte, then 0xff xored into v2 and d SipRounds.  c = 1, d = 3 is Rust's
+    DefaultHasher; c = 2, d = 4 the paper's recommended instance."""
+    v0 = k0 ^ 0x736F6D6570736575
+    v1 = k1 ^ 0x646F72616E646F6D
+    v2 = k0 ^ 0x6C7967656E657261
+    v3 = k1 ^ 0x7465646279746573
+
+    def rounds(n):
+        nonlocal v0, v1, v2, v3
+        for _ in range(n):
+            v0 = (v0 + v1) & MASK64
+            v1 = _rotl(v1, 13) ^ v0
+            v0 = _rotl(v0, 32)
+            v2 = (v2 + v3) & MASK64
+            v3 = _rotl(v3, 16) ^ v2
+            v0 = (v0 + v3) & MASK64
+            v3 = _rotl(v3, 21) ^ v0
+            v2 = (v2 + v1) & MASK64
+            v1 = _rotl(v1, 17) ^ v2
+            v2 = _rotl(v2, 32)
+
+    n = len(data)
+    full = n - n % 8
+    for i in range(0, full, 8):
+        m = int.from_bytes(data[i:i + 8], "little")
+        v3 ^= m
+        rounds(c_rounds)
+        v0 ^= m
+    last = ((n & 0xFF) << 56) | int.from_bytes(data[full:], "little")
+    v3 ^= last
+    rounds(c_rounds)
+    v0 ^= last
+    v2 ^= 0xFF
+    rounds(d_rounds)
+    return v0 ^ v1 ^ v2 ^ v3
+
+
+def region_id(name: str) -> int:
+    """The reference's DeviceMemory chunk id of region `name`: Rust's
+    DefaultHasher (SipHash-1-3, zero keys) over the str, i.e. its bytes and a
+    0xFF terminator (checkpoint.rs:600-606)."""
+    return siphash(0, 0, name.encode() + b"\xff", 1, 3)
+
+
+def chunk_identity(ctype: int, cid: int):
+    """(kind, id) as checkpoint.rs:783-797: the id counts for DeviceMemory and
+    Custom chunks only."""
+    return (ctype, cid if ctype in (CHUNK_DEVICE_MEMORY, CHUNK_CUSTOM) else None)
+
+
+def content_digest(chunks: list) -> str:
+    """checkpoint.rs:806-818: CRC-32/IEEE, continued over every chunk's 16-byte
+    identity header (kind u32, id u64, 4 zero bytes; little-endian) and its
+    data, as 8 lower-case hex digits.  chunks: [(type, id, bytes)]."""
+    crc = 0
+    for ctype, cid, data in chunks:
+        kind, ident = chunk_identity(ctype, cid)
+        crc = zlib.crc32(struct.pack("<IQ4x", kind, ident or 0), crc)
+        crc = zlib.crc32(data, crc)
+    return f"{crc & 0xFFFFFFFF:08x}"
+
+
+def delta_from(base_meta: "CheckpointMetadata", base_chunks: list,
+               new_meta: "CheckpointMetadata", new_chunks: list):
+    """checkpoint.rs:829-852: the chunks of `new` whose bytes differ from the
+    chunk of the same identity in `base`, or that `base` lacks; the base's
+    content digest is recorded under DELTA_PARENT_DIGEST_KEY."""
+    index = {chunk_identity(t, i): d for t, i, d in base_chunks}
+    meta = CheckpointMetadata(**{**new_meta.__dict__, "custom": dict(new_meta.custom)})
+    meta.custom[DELTA_PARENT_DIGEST_KEY] = content_digest(base_chunks)
+    out = [(t, i, d) for t, i, d in new_chunks if index.get(chunk_identity(t, i)) != d]
+    return meta, out
+
+
+def applied_with_delta(base_chunks: list, delta_meta: "CheckpointMetadata", delta_chunks: list):
+    """checkpoint.rs:862-903: base chunks replaced by the delta's chunks of
+    the same identity, then the delta's new chunks; refuses a delta whose
+    recorded parent digest is not the base's."""
+    want = delta_meta.custom.get(DELTA_PARENT_DIGEST_KEY)
+    have = content_digest(base_chunks)
+    if want is not None and want != have:
+        raise ValueError(f"delta parent digest mismatch: expected {want}, got {have}")
+    index = {chunk_identity(t, i): (t, i, d) for t, i, d in delta_chunks}
+    out, used = [], set()
+    for t, i, d in base_chunks:
+        key = chunk_identity(t, i)
+        if key in index:
+            out.append(index[key])
+            used.add(key)
+        else:
+            out.append((t, i, d))
+    out += [c for c in delta_chunks if chunk_identity(c[0], c[1]) not in used]
+    return delta_meta, out
 
 
 @dataclass
@@ -146,8 +254,8 @@ def save(backend, path: str, allow_large: bool = False) -> CheckpointMetadata:
                               grid_size=(backend.width, backend.height, backend.depth),
                               custom={"z_begin": str(backend.z_begin), "z_end": str(backend.z_end),
                                       "layout": "z-major f32"})
-    chunks = [(CHUNK_DEVICE_MEMORY, fnv1a64("pressure"), p.tobytes()),
-              (CHUNK_DEVICE_MEMORY, fnv1a64("pressure_prev"), pp.tobytes())]
+    chunks = [(CHUNK_DEVICE_MEMORY, region_id("pressure"), p.tobytes()),
+              (CHUNK_DEVICE_MEMORY, region_id("pressure_prev"), pp.tobytes())]
     with open(path, "wb") as f:
         f.write(to_bytes(meta, chunks, allow_large))
     return meta
@@ -159,7 +267,12 @@ def restore(backend, path: str, allow_large: bool = False) -> CheckpointMetadata
         meta, chunks = from_bytes(f.read(), allow_large)
     if tuple(meta.grid_size) != (backend.width, backend.height, backend.depth):
         raise ValueError(f"checkpoint grid {meta.grid_size} does not match the backend")
-    mem = [d for t, _, d in chunks if t == CHUNK_DEVICE_MEMORY]
+    by_id = {i: d for t, i, d in chunks if t == CHUNK_DEVICE_MEMORY}
+    pid, ppid = region_id("pressure"), region_id("pressure_prev")
+    if pid in by_id and ppid in by_id:
+        mem = [by_id[pid], by_id[ppid]]
+    else:   # ids this reader does not know: the first two DeviceMemory chunks
+        mem = [d for t, _, d in chunks if t == CHUNK_DEVICE_MEMORY]
     if len(mem) < 2:
         raise ValueError("checkpoint lacks the pressure / pressure_prev chunks")
     p = np.frombuffer(mem[0], dtype=np.float32)

@@ -383,14 +383,18 @@ bool encode_slab_map(const ws3d_ctx* c, CUtensorMap* m, const float* base, uint3
     return r == CUDA_SUCCESS;
 }
 
+// Grids the two-step kernel's boxes fit (136 x (TY + 4) rows at most).
+bool tb_shape_ok(const ws3d_ctx* c) { return c->pitch >= 160 && c->H >= (uint32_t)kTbTY + 4; }
+
 bool encode_buffer_maps(ws3d_ctx* c, int b) {
     return encode_slab_map(c, &c->mapP[b], c->buf[b], TmaLayout<kTmaTY, true>::kPRow,
                            kTmaTY + 2) &&
            encode_slab_map(c, &c->mapT[b], c->buf[b], 128, kTmaTY) &&
            // two-step pressure role: every ghost plane (tensor z = plane + gd)
-           encode_slab_map(c, &c->mapA[b], fbuf_base(c, b), kTbRow, kTbTY + 4,
-                           (uint64_t)c->nz + 2 * c->gd) &&
-           encode_slab_map(c, &c->mapB[b], c->buf[b], kTbRow, kTbTY + 2);
+           (!tb_shape_ok(c) ||
+            (encode_slab_map(c, &c->mapA[b], fbuf_base(c, b), kTbRow, kTbTY + 4,
+                             (uint64_t)c->nz + 2 * c->gd) &&
+             encode_slab_map(c, &c->mapB[b], c->buf[b], kTbRow, kTbTY + 2)));
 }
 
 void build_tma_maps(ws3d_ctx* c) {
@@ -404,7 +408,7 @@ void build_tma_maps(ws3d_ctx* c) {
 void build_tma_c2_map(ws3d_ctx* c) {
     c->tma_c2_map = c->c2f && c->tma_maps &&
                     encode_slab_map(c, &c->mapC2, c->c2f, 128, kTmaTY) &&
-                    encode_slab_map(c, &c->mapC2b, c->c2f, kTbRow, kTbTY + 2);
+                    (!tb_shape_ok(c) || encode_slab_map(c, &c->mapC2b, c->c2f, kTbRow, kTbTY + 2));
 }
 
 // The TMA kernel serves one GPU and z-slabs (its loads read only this GPU's
@@ -473,7 +477,8 @@ bool ensure_tb_buffers(ws3d_ctx* c) {
 
 // The kernel's preconditions apart from the source count.
 bool tb_kernel_ok(ws3d_ctx* c) {
-    return tma_eligible(c) && c->sponge_monotone && c->sponge_w <= (uint32_t)kTbSpongeMax &&
+    return tma_eligible(c) && tb_shape_ok(c) && c->sponge_monotone &&
+           c->sponge_w <= (uint32_t)kTbSpongeMax &&
            (!c->c2f || c->tma_c2_map) && ensure_tb_buffers(c);
 }
 

@@ -20,6 +20,17 @@ namespace ws3d {
 
 constexpr int kZsTileX = 128;  // cells per CTA row (32 lanes x float4)
 
+// Two-step kernel (k_step_tma2): tile height in rows and co-resident CTAs per
+// SM.  TY + 2 consumer warps (one extended row each) plus one producer warp
+// per CTA; a tile of 16 rows takes one CTA of 19 warps per SM (shared memory),
+// a tile of 8 rows two CTAs of 11 warps.
+#ifndef WS3D_TB_TY
+#define WS3D_TB_TY 8
+#endif
+constexpr int kTbTY = WS3D_TB_TY;
+constexpr int kTbCtasPerSm = kTbTY >= 16 ? 1 : 2;
+static_assert(kTbTY % 2 == 0 && kTbTY >= 8 && kTbTY <= 28, "two-step tile height");
+
 // Per-thread constants of the z-streaming kernel.
 struct ZsLane {
     int64_t row;    // offset of this thread's float4 inside a plane

@@ -60,8 +60,10 @@
 
 namespace ws3d {
 
-constexpr int kTbTY = 8;
-constexpr int kTbStages = 5;
+#ifndef WS3D_TB_STAGES
+#define WS3D_TB_STAGES 5
+#endif
+constexpr int kTbStages = WS3D_TB_STAGES;
 constexpr int kTbRow = 136;       // floats per staged row (x0-4 .. x0+131)
 constexpr int kTbMaxSrc = 32;     // sources per launch (one per lane)
 constexpr int kTbSpongeMax = 64;  // sponge widths the kernel takes (table in shared memory)
@@ -75,7 +77,7 @@ struct TbLayout {
     static constexpr int kTx = kABytes + kBBytes * (kC2F ? 2 : 1);
     static constexpr int kRingPlane = 128 * (kTbTY + 2);                 // floats
     static constexpr int kRingBytes = 2 * kRingPlane * 4;
-    static constexpr int kHaloBytes = 256;                               // 2 x (TY+2) x 2 floats
+    static constexpr int kHaloBytes = (2 * (kTbTY + 2) * 2 * 4 + 127) / 128 * 128;  // [2][TY+2][2]
     static constexpr int kTabBytes = kTbSpongeMax * 4;
     static constexpr int kSrcBytes = kTbMaxSrc * 16;
     // stages | X ring | X halo columns | sponge table | sources | 2*S mbarriers | slack
@@ -133,7 +135,7 @@ __device__ __forceinline__ float4 add_at(float4 v, int e, float d) {
 // kSlab: the z-slab instance (ghost-plane X, neighbour waits, pushes); the
 // one-GPU instance compiles none of that into its item loop.
 template <bool kC2F, bool kSlab>
-__global__ void __launch_bounds__(32 * (kTbTY + 3), 2)
+__global__ void __launch_bounds__(32 * (kTbTY + 3), kTbCtasPerSm)
 k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmC2, TbArgs g) {
     using L = TbLayout<kC2F>;

@@ -52,12 +52,12 @@ int main(int argc, char** argv) {
     const bool has_lo = lo_nz > 0, has_hi = hi_nz > 0;
     const bool slab = has_lo || has_hi;
     const int gd = slab ? 2 : 1;
-    constexpr int TY = 8;
+    constexpr int TY = kTbTY;
     const uint32_t pitch = (W + 31u) & ~31u;
     const int64_t P = (int64_t)H * pitch;
     const uint32_t tiles_x = (pitch + 127) / 128;
     const uint32_t tiles = tiles_x * ((H + TY - 1) / TY);
-    const TmaSchedule sch = tb_schedule(tiles, nz, (uint32_t)(2 * sms));
+    const TmaSchedule sch = tb_schedule(tiles, nz, (uint32_t)(kTbCtasPerSm * sms));
     for (uint32_t item = 0; item < sch.nitems; ++item) {
         const uint32_t chunk = item / tiles, tile = item - chunk * tiles;
         const int zs = (int)(chunk * sch.clen);
