@@ -25,6 +25,9 @@ WS3D_ETIMEOUT = 9
 WS3D_EPEER = 10
 
 WS3D_STATIC_ENERGY_MAX_PLANES = 8192   # include/ws3d.h
+# rows of a two-step (k_step_tma2) tile, kTbTY in csrc/ws3d_index.h: the two-step
+# kernel takes grids with W > 128 and H >= WS3D_TWO_STEP_ROWS + 4
+WS3D_TWO_STEP_ROWS = 16
 
 WS3D_VARIANT_AUTO = 0
 WS3D_VARIANT_ZSTREAM = 1

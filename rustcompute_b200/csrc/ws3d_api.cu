@@ -620,10 +620,13 @@ ws3d_status ensure_cell_arrays(ws3d_ctx* c);
 // ---- persistent mode --------------------------------------------------------
 constexpr int kPersTY = 8;
 
+// Default face layout: the row-parallel body (k_persistent_rows, one L2
+// round trip per step); per-cell boundary arrays: the z-streaming body.
 template <bool kC2F, bool kCells>
 ws3d_status launch_persistent(ws3d_ctx* c, uint64_t n) {
-    auto kern = k_persistent<kC2F, kCells, kPersTY>;
-    const int threads = 32 * kPersTY;
+    const void* kern = kCells ? (const void*)k_persistent<kC2F, kCells, kPersTY>
+                              : (const void*)k_persistent_rows<kC2F>;
+    const int threads = kCells ? 32 * kPersTY : kRowThreads;
     int& resident = c->pers_resident[(kC2F ? 2 : 0) + (kCells ? 1 : 0)];
     if (resident == 0) {
         int per_sm = 0;
@@ -664,8 +667,12 @@ ws3d_status launch_persistent(ws3d_ctx* c, uint64_t n) {
     q.clen = sch.clen;
     q.nitems = sch.nitems;
     void* args[] = {&q};
-    cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, dim3(sch.grid),
-                                                dim3(32, kPersTY, 1), args, 0, c->stream);
+    // the row body: every co-resident CTA (rows are spread over all warps)
+    const uint64_t rows = (uint64_t)c->nz * c->H * q.tiles_x;
+    const uint64_t row_ctas = (rows + kRowThreads / 32 - 1) / (kRowThreads / 32);
+    const dim3 grid = kCells ? dim3(sch.grid) : dim3((unsigned)std::min<uint64_t>(resident, row_ctas));
+    const dim3 block = kCells ? dim3(32, kPersTY, 1) : dim3(kRowThreads, 1, 1);
+    cudaError_t e = cudaLaunchCooperativeKernel(kern, grid, block, args, 0, c->stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return cuda_fail(c, e == cudaErrorCooperativeLaunchTooLarge ? WS3D_ELAUNCH : WS3D_ELAUNCH,

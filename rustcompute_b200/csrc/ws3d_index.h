@@ -23,9 +23,12 @@ constexpr int kZsTileX = 128;  // cells per CTA row (32 lanes x float4)
 // Two-step kernel (k_step_tma2): tile height in rows and co-resident CTAs per
 // SM.  TY + 2 consumer warps (one extended row each) plus one producer warp
 // per CTA; a tile of 16 rows takes one CTA of 19 warps per SM (shared memory),
-// a tile of 8 rows two CTAs of 11 warps.
+// a tile of 8 rows two CTAs of 11 warps.  Measured on B200 (C3 512^3 / C4
+// 1024^3, 4 stages): 16 rows 514 / 4122 us per launch, 8 rows (2 CTAs, 5
+// stages) 568 / 4753 us -- half the halo rows and halo columns per core cell,
+// and 96 registers without spills instead of 80 with spills.
 #ifndef WS3D_TB_TY
-#define WS3D_TB_TY 8
+#define WS3D_TB_TY 16
 #endif
 constexpr int kTbTY = WS3D_TB_TY;
 constexpr int kTbCtasPerSm = kTbTY >= 16 ? 1 : 2;
@@ -68,6 +71,25 @@ WS3D_HD ZsLane zs_lane(uint32_t bx, uint32_t by, int lane, int w, uint32_t W, ui
 
 // Offset of plane `z` (may be -1 or nz: the ghosts).
 WS3D_HD int64_t zs_plane(int64_t z, int64_t plane) { return z * plane; }
+
+// Row-parallel persistent body (k_persistent_rows): row r of a step is
+// x-tile tx of row y of plane z, 128 cells.  On z-slabs the interior planes
+// 1 .. nz-2 come first, then plane 0, then plane nz-1 (their waits for the
+// neighbours' flags overlap the interior rows).
+struct RowCoord {
+    uint32_t z, y, tx;
+};
+WS3D_HD RowCoord row_coord(uint64_t r, uint32_t H, uint32_t tiles_x, uint32_t nz, bool slab) {
+    const uint64_t per_plane = (uint64_t)H * tiles_x;
+    const uint64_t k = r / per_plane;
+    const uint32_t rem = (uint32_t)(r - k * per_plane);
+    RowCoord c;
+    c.z = (uint32_t)k;
+    if (slab && nz > 1) c.z = k + 2 < nz ? (uint32_t)k + 1u : (k + 2 == nz ? 0u : nz - 1);
+    c.y = rem / tiles_x;
+    c.tx = rem - c.y * tiles_x;
+    return c;
+}
 
 // Order in which z-chunks are assigned to blockIdx.z.  With a halo exchange,
 // chunk 0 and the last chunk (the ones that wait for a neighbour) go last.

@@ -127,6 +127,130 @@ __global__ void __launch_bounds__(32 * TY, 3) k_persistent(PersistentArgs q) {
 }
 
 // ---------------------------------------------------------------------------
+// Row-parallel persistent step (default face layout).
+//
+// k_persistent's z-streaming items walk a run of planes through a register
+// queue: on a small, L2-resident grid (config 5, 128^3) every step is then a
+// chain of dependent plane loads per CTA.  Here a step is a flat set of rows
+// -- 128 cells of one (y, z) at one x-tile, a float4 per lane -- spread over
+// every warp of the grid; each row issues all its loads at once (centre, z
+// and y neighbours, p_prev, c2, the two x-halo cells), so a step costs about
+// one L2 round trip plus the grid barrier.  The cell rule is cells4_default,
+// the same operations in the same order as every other kernel here.
+//
+// Fields are rewritten every step inside the launch, so they are read
+// through L2 (ld.global.cg): no SM's L1 can hold a value from an earlier
+// step.  On z-slabs the rows of the first and last owned plane (they read
+// the ghost planes a neighbour stores into, and store into the neighbour's
+// ghost planes) run after the interior rows of the step; a warp waits
+// (bounded) for the neighbour's flag once before its first such row.
+// ---------------------------------------------------------------------------
+constexpr int kRowThreads = 512;
+
+__device__ __forceinline__ float4 ldcg4(const float* p) {
+    return __ldcg(reinterpret_cast<const float4*>(p));
+}
+
+// One step over rows gw, gw + G, ... of the step's row list.
+template <bool kC2F>
+__device__ __forceinline__ void step_rows(const StepParams& a, uint32_t tiles_x, bool halo,
+                                          uint32_t gw, uint32_t G) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint64_t nrows = (uint64_t)a.H * tiles_x * a.nz;
+    const int64_t P = (int64_t)a.plane;
+    const float* __restrict__ p = a.p;
+    float* __restrict__ pp = a.pp;
+    bool waited_lo = a.wait_lo == nullptr, waited_hi = a.wait_hi == nullptr;
+    for (uint64_t r = gw; r < nrows; r += G) {
+        const RowCoord rc = row_coord(r, a.H, tiles_x, a.nz, halo);
+        const uint32_t z = rc.z, y = rc.y;
+        const uint32_t x0 = rc.tx * 128u, x = x0 + 4u * lane;
+        if (halo) {
+            const bool lo = z == 0 && !waited_lo, hi = z + 1 == a.nz && !waited_hi;
+            if (lo || hi) {
+                if (lane == 0) {
+                    unsigned int bad = 0;
+                    if (lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns, a.wait_acc))
+                        bad |= 1u;
+                    if (hi && !wait_flag_geq(a.wait_hi, a.wait_val, a.budget_ns, a.wait_acc))
+                        bad |= 2u;
+                    if (bad) atomicOr(a.status, bad);
+                }
+                __syncwarp();
+                waited_lo = waited_lo || lo;
+                waited_hi = waited_hi || hi;
+            }
+        }
+        const bool act = x < a.pitch;
+        const int64_t o = (int64_t)z * P + (int64_t)y * a.pitch + x;
+        const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 pc = z4, pm = z4, pn = z4, S = z4, N = z4, vpp = z4;
+        float4 c2v = make_float4(a.c2, a.c2, a.c2, a.c2);
+        float hl = 0.f, hr = 0.f;
+        if (act) {
+            // rows y - 1 / y + 1 of plane z exist in the allocation (the ghost
+            // planes frame it); at y = 0 / H - 1 the cells are faces and the
+            // values are not used
+            pc = ldcg4(p + o);
+            pm = ldcg4(p + o - P);
+            pn = ldcg4(p + o + P);
+            S = ldcg4(p + o - (int64_t)a.pitch);
+            N = ldcg4(p + o + (int64_t)a.pitch);
+            vpp = ldcg4(pp + o);
+            if (kC2F) c2v = __ldg(reinterpret_cast<const float4*>(a.c2f + o));
+        }
+        if (lane == 0 && x0 > 0) hl = __ldcg(p + o - 1);
+        if (lane == 31 && x0 + 128u < a.pitch) hr = __ldcg(p + o + 4);
+        float wl = __shfl_up_sync(0xffffffffu, pc.w, 1);
+        float er = __shfl_down_sync(0xffffffffu, pc.x, 1);
+        if (lane == 0) wl = hl;
+        if (lane == 31) er = hr;
+        if (act) {
+            const XYPre xy = make_xypre(x, y, a);
+            const float4 out = cells4_default(xy, a.z0 + z, wl, er, S, N, pm, pc, pn, vpp, c2v, a);
+            st4(pp + o, out);
+            const int64_t ro = (int64_t)y * a.pitch + x;
+            if (z == 0 && a.peer_lo) st4(a.peer_lo + ro, out);
+            if (z + 1 == a.nz && a.peer_hi) st4(a.peer_hi + ro, out);
+        }
+    }
+}
+
+template <bool kC2F>
+__global__ void __launch_bounds__(kRowThreads, 2) k_persistent_rows(PersistentArgs q) {
+    __shared__ int s_ok;
+    const unsigned int nb = gridDim.x;
+    const bool leader = blockIdx.x == 0 && threadIdx.x == 0;
+    const bool halo = q.lo_base[0] != nullptr || q.hi_base[0] != nullptr;
+    const uint32_t G = nb * (kRowThreads / 32);
+    const uint32_t gw = blockIdx.x * (kRowThreads / 32) + (threadIdx.x >> 5);
+    for (uint64_t s = 0; s < q.nsteps; ++s) {
+        const int cur = (int)((q.cur0 + s) & 1u);
+        StepParams a = q.a;
+        a.p = q.buf[cur] + a.plane;
+        a.pp = q.buf[cur ^ 1] + a.plane;
+        a.peer_lo = q.lo_base[0] ? q.lo_base[cur ^ 1] + q.lo_ghost_off : nullptr;
+        a.peer_hi = q.hi_base[0] ? q.hi_base[cur ^ 1] : nullptr;
+        a.wait_val = q.halo_base + s + 1;
+        if (leader) {
+            if (q.n_src)
+                inject_sources_dev(q.buf[cur], q.buf[cur ^ 1], q.src_off, q.wavelet, q.n_src,
+                                   q.wl_len, q.step0 + s, q.src_ghost, q.lo_base[cur],
+                                   q.hi_base[0] ? q.hi_base[cur] - a.plane : nullptr);
+            if (halo) {
+                __threadfence_system();
+                if (q.lo_flag) st_release_sys(q.lo_flag, q.halo_base + s + 1);
+                if (q.hi_flag) st_release_sys(q.hi_flag, q.halo_base + s + 1);
+            }
+        }
+        if (q.n_src && !grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok))
+            return;
+        step_rows<kC2F>(a, q.tiles_x, halo, gw, G);
+        if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok)) return;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Resident (command-driven) kernel.
 //
 // The reference keeps its persistent kernel running and feeds it commands

@@ -60,8 +60,12 @@
 
 namespace ws3d {
 
+// Pipeline depth.  With 16-row tiles (one CTA per SM) 4 stages measured
+// best: 5 took the same time at C3 but 15 % longer at C4 1024^3, 6 longer
+// still -- more planes in flight per SM evict the halo rows neighbouring
+// tiles would have read from L2.
 #ifndef WS3D_TB_STAGES
-#define WS3D_TB_STAGES 5
+#define WS3D_TB_STAGES 4
 #endif
 constexpr int kTbStages = WS3D_TB_STAGES;
 constexpr int kTbRow = 136;       // floats per staged row (x0-4 .. x0+131)

@@ -6,7 +6,7 @@
 // that each access lies inside its allocation, is 16-byte aligned for float4
 // accesses and does not straddle a row.  Exit code 0 = all accesses in bounds.
 //
-// Usage: index_check W H nz sm_count [TY [halo [kernel: 0 zstream, 1 async]]]
+// Usage: index_check W H nz sm_count [TY [halo [kernel: 0 zstream, 1 async, 2 rows]]]
 #include <cstdio>
 #include <cstdlib>
 #include <vector>
@@ -174,6 +174,56 @@ static void run_async(uint32_t W, uint32_t H, uint32_t nz, int sms, bool halo) {
     }
 }
 
+// k_persistent_rows: every row of one step (row_coord, the kernel's own
+// mapping), every lane: the seven float4 loads, the two x-halo loads, the
+// store and the z-slab peer stores.
+static void run_rows(uint32_t W, uint32_t H, uint32_t nz, bool slab) {
+    const uint32_t pitch = (W + 31u) & ~31u;
+    const int64_t P = (int64_t)H * pitch;
+    const uint32_t tiles_x = (pitch + 127u) / 128u;
+    const uint64_t nrows = (uint64_t)H * tiles_x * nz;
+    const Field fp{"p", true}, fpp{"pp", false}, fc2{"c2", false}, fpeer{"peer plane", false};
+    std::vector<unsigned char> seen((size_t)nrows * 32, 0);
+    for (uint64_t r = 0; r < nrows; ++r) {
+        const RowCoord rc = row_coord(r, H, tiles_x, nz, slab);
+        const uint32_t x0 = rc.tx * 128u;
+        for (int lane = 0; lane < 32; ++lane) {
+            const uint32_t x = x0 + 4u * (uint32_t)lane;
+            const int64_t o = (int64_t)rc.z * P + (int64_t)rc.y * pitch + x;
+            if (x < pitch) {
+                const size_t cell = ((size_t)rc.z * H + rc.y) * pitch + x;
+                if (cell / 4 < seen.size()) seen[cell / 4]++;
+                check(fp, o, 4, pitch, nz, P, "rows centre", rc.tx, rc.y, rc.z, lane, 0);
+                check(fp, o - P, 4, pitch, nz, P, "rows z-1", rc.tx, rc.y, rc.z, lane, 0);
+                check(fp, o + P, 4, pitch, nz, P, "rows z+1", rc.tx, rc.y, rc.z, lane, 0);
+                check(fp, o - (int64_t)pitch, 4, pitch, nz, P, "rows y-1", rc.tx, rc.y, rc.z, lane, 0);
+                check(fp, o + (int64_t)pitch, 4, pitch, nz, P, "rows y+1", rc.tx, rc.y, rc.z, lane, 0);
+                check(fpp, o, 4, pitch, nz, P, "rows p_prev / store", rc.tx, rc.y, rc.z, lane, 0);
+                check(fc2, o, 4, pitch, nz, P, "rows c2", rc.tx, rc.y, rc.z, lane, 0);
+                if (slab && (rc.z == 0 || rc.z + 1 == nz))
+                    check(fpeer, (int64_t)rc.y * pitch + x, 4, pitch, 1, P, "rows peer store", rc.tx,
+                          rc.y, rc.z, lane, 0);
+            }
+            if (lane == 0 && x0 > 0)
+                check(fp, o - 1, 1, pitch, nz, P, "rows x-1", rc.tx, rc.y, rc.z, lane, 0);
+            if (lane == 31 && x0 + 128u < pitch)
+                check(fp, o + 4, 1, pitch, nz, P, "rows x+128", rc.tx, rc.y, rc.z, lane, 0);
+        }
+    }
+    // every float4 of the owned planes exactly once per step
+    for (uint32_t z = 0; z < nz; ++z)
+        for (uint32_t y = 0; y < H; ++y)
+            for (uint32_t x = 0; x < pitch; x += 4) {
+                const size_t cell = ((size_t)z * H + y) * pitch + x;
+                if (seen[cell / 4] != 1) {
+                    if (g_bad < 20)
+                        fprintf(stderr, "rows: float4 at (%u,%u,%u) covered %d times\n", x, y, z,
+                                seen[cell / 4]);
+                    ++g_bad;
+                }
+            }
+}
+
 int main(int argc, char** argv) {
     if (argc < 5) {
         fprintf(stderr, "usage: %s W H nz sm_count [TY]\n", argv[0]);
@@ -184,6 +234,11 @@ int main(int argc, char** argv) {
     const int sms = atoi(argv[4]);
     const int ty = argc > 5 ? atoi(argv[5]) : 8;
     const bool halo = argc > 6 && atoi(argv[6]) != 0;
+    if (argc > 7 && atoi(argv[7]) == 2) {
+        run_rows(W, H, nz, halo);
+        printf("checked %lld accesses, %d out of bounds\n", g_checked, g_bad);
+        return g_bad == 0 ? 0 : 1;
+    }
     if (argc > 7 && atoi(argv[7]) == 1) {
         run_async(W, H, nz, sms, halo);
         printf("checked %lld accesses, %d out of bounds\n", g_checked, g_bad);

@@ -88,3 +88,13 @@ def test_no_cpu_fallback_in_package():
             if f.endswith(".py"):
                 src = open(os.path.join(dirpath, f)).read()
                 assert "import oracle" not in src and "from oracle" not in src, f
+
+
+def test_two_step_rows_constant_matches_the_kernel():
+    """_ffi.WS3D_TWO_STEP_ROWS mirrors the default tile height in ws3d_index.h."""
+    import re
+
+    from rustcompute_b200 import _ffi
+    src = open(os.path.join(ROOT, "rustcompute_b200", "csrc", "ws3d_index.h")).read()
+    m = re.search(r"#define WS3D_TB_TY (\d+)", src)
+    assert m and int(m.group(1)) == _ffi.WS3D_TWO_STEP_ROWS

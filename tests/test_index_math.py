@@ -56,6 +56,21 @@ def test_async_kernel_accesses_in_bounds(checker, shape, halo):
     assert r.returncode == 0, r.stderr + r.stdout
 
 
+ROW_SHAPES = [(13, 7, 5), (130, 9, 20), (257, 11, 6), (3, 3, 3), (128, 128, 128), (160, 70, 37),
+              (1, 1, 1), (31, 1, 2), (520, 9, 30), (256, 256, 64)]
+
+
+@pytest.mark.parametrize("shape", ROW_SHAPES)
+@pytest.mark.parametrize("halo", [0, 1])
+def test_persistent_row_kernel_accesses_in_bounds(checker, shape, halo):
+    """k_persistent_rows: every access in bounds and every float4 of the owned
+    planes written exactly once per step."""
+    W, H, nz = shape
+    r = subprocess.run([checker, str(W), str(H), str(nz), "148", "8", str(halo), "2"],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr + r.stdout
+
+
 def test_checker_catches_the_unsigned_wrap(checker, tmp_path):
     """The check must flag the bug class it exists for: a ghost-plane offset
     computed in uint32 (zb - 1 wrapping to 2^32 - 1)."""

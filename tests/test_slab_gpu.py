@@ -17,7 +17,7 @@ import time
 import numpy as np
 import pytest
 
-from rustcompute_b200 import GpuBackend3D, TimeoutError_, configs
+from rustcompute_b200 import GpuBackend3D, TimeoutError_, _ffi, configs
 from rustcompute_b200.slab import LocalSlabGroup, attach, export_handles, slab_bounds
 
 pytestmark = pytest.mark.gpu
@@ -47,6 +47,7 @@ def make(wl, zb, ze, device=0, budget_ns=0, variant="auto"):
 def test_local_slab_group_equals_single_context(nslab, name, grid, steps, variant):
     W, H, D = grid
     tma_ok = W > 128 and H >= 16
+    two_ok = tma_ok and H >= _ffi.WS3D_TWO_STEP_ROWS + 4
     if variant in ("tma", "tma2") and not tma_ok:
         pytest.skip("TMA kernels need W > 128 and H >= 16")
     wl = configs.build(name, W, H, D, steps=steps)
@@ -60,7 +61,7 @@ def test_local_slab_group_equals_single_context(nslab, name, grid, steps, varian
     slabs = [make(wl, zb, ze, variant=variant) for zb, ze in bounds]
     grp = LocalSlabGroup(slabs)
     # two steps per exchange wherever the two-step kernel runs
-    assert grp.depth == (2 if variant in ("auto", "tma2") and tma_ok else 1)
+    assert grp.depth == (2 if variant in ("auto", "tma2") and two_ok else 1)
     full.step_n(None, steps // 2)
     grp.step_n(steps // 2)
     for b in [full] + slabs:   # impulses on boundary planes
@@ -149,7 +150,7 @@ def test_multi_process_nvlink_slabs_equal_one_gpu(name, grid, steps, persistent)
     assert r.returncode == 0 and "SLAB-CHECK OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
 
 
-@pytest.mark.parametrize("nslab,grid", [(3, (264, 24, 40)), (4, (160, 40, 9)), (2, (300, 17, 30))])
+@pytest.mark.parametrize("nslab,grid", [(3, (264, 24, 40)), (4, (160, 40, 9)), (2, (300, 21, 30))])
 def test_two_step_slabs_ghost_plane_sources_odd_counts_and_impulses(nslab, grid):
     """Temporal depth 2 on same-device slabs: sources on every plane next to
     a slab boundary (the ghost planes the kernel computes p_{t+1} on), odd

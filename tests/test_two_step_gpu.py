@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 import oracle
-from rustcompute_b200 import GpuBackend3D, configs
+from rustcompute_b200 import GpuBackend3D, _ffi, configs
 from rustcompute_b200.grid import AcousticParams3D
 
 pytestmark = pytest.mark.gpu
@@ -41,7 +41,7 @@ def edge_sources(W, H, D, n, rng):
     """Sources on tile borders (x = 127/128/129, y = 7/8/9, ...), the grid
     faces, z-chunk borders, plus two coinciding pairs."""
     xs = [1, 2, 126, 127, 128, 129, 130, 255, 256, 257, W - 2, W - 1]
-    ys = [1, 7, 8, 9, 15, 16, H - 2, H - 1]
+    ys = [1, 7, 8, 9, 15, 16, 17, 31, 32, 33, H - 2, H - 1]
     zs = [0, 1, 2, D // 2, D // 2 + 1, D - 2, D - 1]
     pts = [[xs[k % len(xs)] % W, ys[(3 * k) % len(ys)] % H, zs[(5 * k) % len(zs)] % D]
            for k in range(n - 2)]
@@ -49,8 +49,9 @@ def edge_sources(W, H, D, n, rng):
     return np.array(pts, np.uint32), rng.standard_normal((n, 9)).astype(np.float32)
 
 
-@pytest.mark.parametrize("shape", [(256, 32, 40), (300, 40, 33), (129, 16, 3), (160, 24, 1),
-                                   (160, 24, 2), (520, 17, 12), (384, 72, 100)])
+@pytest.mark.parametrize("shape", [(256, 32, 40), (300, 40, 33), (129, 20, 3), (160, 24, 1),
+                                   (160, 24, 2), (520, 21, 12), (384, 72, 100), (200, 37, 9),
+                                   (264, 50, 21)])
 @pytest.mark.parametrize("c2f,sponge", [(False, 0), (True, 3)])
 @pytest.mark.parametrize("steps", [2, 7, 12])
 def test_two_step_equals_one_step(shape, c2f, sponge, steps):
@@ -68,6 +69,8 @@ def test_two_step_equals_one_step(shape, c2f, sponge, steps):
     assert same_bits(p2, p1), f"pressure differs in {(p1 != p2).sum()} cells"
     assert same_bits(pp2, pp1), f"pressure_prev differs in {(pp1 != pp2).sum()} cells"
     assert two.stats()["step"] == steps
+    if H >= _ffi.WS3D_TWO_STEP_ROWS + 4:   # the two-step kernel's boxes fit: it ran
+        assert two.stats()["two_step_launches"] == steps // 2
     one.close()
     two.close()
 
