@@ -94,15 +94,18 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def ncu_traffic(wl, kernel: str):
+def ncu_traffic(wl, kernel: str, slab_planes: int = 0):
     """DRAM bytes per launch of the step kernel from a committed ncu summary
-    (profiles/traffic.json, keyed by workload, grid and kernel), or None."""
+    (profiles/traffic.json, keyed by workload, grid and kernel; z-slabs by the
+    slab's own size, `slab_planes` > 0), or None."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(path):
         return None
     with open(path) as f:
         d = json.load(f)
-    e = d.get(f"{wl.name}/{wl.W}x{wl.H}x{wl.D}/{kernel}")
+    key = (f"{wl.name}/slab{wl.W}x{wl.H}x{slab_planes}/{kernel}" if slab_planes
+           else f"{wl.name}/{wl.W}x{wl.H}x{wl.D}/{kernel}")
+    e = d.get(key)
     return None if e is None else e.get("dram_bytes_per_launch")
 
 
@@ -310,9 +313,10 @@ def kernel_name(variant, wl, world, mode="step", depth=1):
     if mode == "resident":
         return "k_resident"
     if variant in ("auto", "tma2"):   # mirrors the library's choice for the default faces
+        from rustcompute_b200 import _ffi
         tma_ok = wl.W > 128 and wl.H >= 16
         two_step = (world == 1 or depth == 2) and tma_ok and len(wl.sources) <= 32 and \
-            wl.sponge_width <= 64
+            wl.sponge_width <= 64 and wl.H >= _ffi.WS3D_TWO_STEP_ROWS + 4
         variant = "tma2" if two_step else ("tma" if tma_ok else "zstream")
     return {"tma": "k_step_tma", "tma2": "k_step_tma2", "async": "k_step_async",
             "zstream": "k_step_zstream",
@@ -335,6 +339,7 @@ def slab_parity(b, wl, args, rank, world, local, pg, depth) -> dict:
     transfers byte for byte the same way, with a CRC, multi_gpu/runtime.rs).
     One GPU's result equals the oracle bit for bit (tests/), so a match here
     is bit-exactness of the z-slab exchange at this N."""
+    import torch
     steps = max(args.warmup, 3) + args.steps
     plane = wl.W * wl.H
     mine = plane_digests(b.download_field(), plane)
@@ -342,7 +347,16 @@ def slab_parity(b, wl, args, rank, world, local, pg, depth) -> dict:
     pg.all_gather_object(gathered, mine)
     out = {"reference": f"one GPU, whole {wl.W}x{wl.H}x{wl.D} grid, {steps} steps "
                         "(variant auto)", "steps": steps, "halo_depth": depth}
-    if rank == 0:
+    # the whole grid on one GPU: five field-sized buffers (p, p_prev, two
+    # two-step outputs, c2) beside this rank's own slab context, and about 24
+    # host bytes per cell to build its inputs
+    need = 5 * 4 * wl.cells
+    free = torch.cuda.mem_get_info(local)[0] if rank == 0 else 0
+    if rank == 0 and (need > 0.9 * free or wl.cells > (1 << 31)):
+        out["result"] = "skipped"
+        out["why"] = (f"the whole grid ({wl.cells} cells, {need / 2 ** 30:.1f} GiB on the device) "
+                      "does not fit one GPU beside its slab")
+    elif rank == 0:
         full = make_backend(wl, "auto", local, 0, wl.D)
         p, pp = wl.initial_fields()
         full.upload_fields(p, pp)
@@ -550,7 +564,8 @@ def run_ours(args, wl):
     achieved = total_bytes / (kernel_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"],
-                "traffic": ncu_traffic(wl, kernel_name(args.variant, wl, world, depth=depth)),
+                "traffic": ncu_traffic(wl, kernel_name(args.variant, wl, world, depth=depth),
+                                       ze - zb if world > 1 else 0),
                 "algorithmic_bytes_per_launch": alg_bytes,
                 "steps_per_launch": 2 if kname == "k_step_tma2" and args.mode == "step" else 1,
                 # algorithmic bytes per cell of one launch: one step moves bpc (read p,
@@ -595,6 +610,18 @@ def run_ours(args, wl):
                     "step kernels spent in neighbour-flag waits that did not pass at once",
         }
         result["parity"] = slab_parity(b, wl, args, rank, world, local, pg, depth)
+        # NVLink halo bytes per launch of an interior slab (two neighbours),
+        # algorithmic: a two-step launch stores p_{t+2} of two edge planes into
+        # each neighbour and reads the neighbour's p_{t-1} (and c2) edge plane;
+        # a one-step launch stores one edge plane per neighbour
+        plane_b = wl.W * wl.H * 4
+        two = kname == "k_step_tma2" and args.mode == "step"
+        per_nb = (2 + 1 + (1 if wl.heterogeneous else 0)) * plane_b if two else plane_b
+        result["halo"] = {"nvlink_bytes_per_launch_interior_slab": 2 * per_nb,
+                          "per_neighbour": {"stored": (2 if two else 1) * plane_b,
+                                            "loaded": (per_nb - 2 * plane_b) if two else 0},
+                          "steps_per_exchange": 2 if two else 1,
+                          "note": "algorithmic; kernel peer stores and loads, no copies"}
     b.close()
 
     # e2e: one whole job through the public API with pinned host buffers.

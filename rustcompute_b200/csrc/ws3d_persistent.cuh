@@ -259,7 +259,8 @@ __global__ void __launch_bounds__(kRowThreads, 2) k_persistent_rows(PersistentAr
 // does the same on one GPU: between steps the leader thread (CTA 0, thread 0)
 // drains the H2K queue, decides "step", "idle" or "exit" and publishes the
 // decision before the per-step grid barrier; the step itself is the
-// z-streaming cell body of k_persistent, so fields are bit-identical to
+// row-parallel body of k_persistent_rows (default faces) or the z-streaming
+// body of k_persistent (cell arrays), so fields are bit-identical to
 // ws3d_step.  Every progress_interval steps all CTAs sum p^2 (fixed order,
 // double) and the leader posts a PROGRESS message.  Waits are bounded: the
 // grid barrier as in k_persistent, and an idle kernel (no steps, not paused
@@ -554,10 +555,15 @@ __global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
                 break;
             }
         }
-        for (uint32_t item = blockIdx.x; item < q.nitems; item += nb) {
-            const uint32_t chunk = item / q.tiles, tile = item - chunk * q.tiles;
-            const uint32_t zs = chunk * q.clen, ze = min(a.nz, zs + q.clen);
-            zs_tile<kC2F, kCells, TY>(a, tile % q.tiles_x, tile / q.tiles_x, zs, ze);
+        if constexpr (!kCells) {
+            // default faces: the row-parallel body (one warp per row of 128 cells)
+            step_rows<kC2F>(a, q.tiles_x, false, blockIdx.x * TY + threadIdx.y, nb * TY);
+        } else {
+            for (uint32_t item = blockIdx.x; item < q.nitems; item += nb) {
+                const uint32_t chunk = item / q.tiles, tile = item - chunk * q.tiles;
+                const uint32_t zs = chunk * q.clen, ze = min(a.nz, zs + q.clen);
+                zs_tile<kC2F, kCells, TY>(a, tile % q.tiles_x, tile / q.tiles_x, zs, ze);
+            }
         }
         cur ^= 1;
         ++ran;
