@@ -114,6 +114,12 @@ struct ws3d_ctx {
     CUtensorMap mapA[4];   // two steps, pressure role: box 136 x (TY+4) x 1
     CUtensorMap mapB[4];   // two steps, p_prev role:   box 136 x (TY+2) x 1
     CUtensorMap mapC2b;    // two steps, c2:            box 136 x (TY+2) x 1
+    // z-slabs at temporal depth 2: the neighbours' field buffers (index as
+    // lo_base / hi_base, permuted with them) and c2 fields in the p_prev role,
+    // over their planes -1 .. nz: the two-step kernel stages their edge planes
+    // of p_{t-1} and c2 from these (plain TMA loads of peer memory)
+    CUtensorMap mapBlo[4], mapBhi[4], mapC2lo, mapC2hi;
+    bool peer_maps = false;
     bool tma_maps = false, tma_c2_map = false;
     bool tb_buffers = false;   // buffers 2 and 3 allocated, their maps encoded
     bool tb_failed = false;    // their allocation failed: run single steps
@@ -523,19 +529,28 @@ ws3d_status launch_tb(ws3d_ctx* c) {
     g.wl_len = c->wl_len;
     g.step1 = c->step + 1;
     g.a_zoff = (int)c->gd;
+    // neighbours' own p_{t-1} (role ipp) and c2 planes next to ours come by
+    // TMA through the peer maps; Y goes into their Y buffers (index 3, same
+    // role on every rank).  One GPU: the own maps stand in (never read).
+    const CUtensorMap* mbl = &c->mapB[c->ipp];
+    const CUtensorMap* mbh = &c->mapB[c->ipp];
+    const CUtensorMap* mcl = &c->mapC2b;
+    const CUtensorMap* mch = &c->mapC2b;
     if (c->halo) {
-        // neighbours' own p_{t-1} (role ipp) and c2 planes next to ours; Y goes
-        // into their Y buffers (index 3, same role on every rank)
-        const size_t P = c->plane;
+        if (!c->peer_maps)
+            return fail(c, WS3D_EPEER, "two-step slab launch without tensor maps of the neighbours");
         if (c->lo_base[0]) {
-            g.rem_b_lo = c->lo_base[c->ipp] + (size_t)c->lo_nz * P;
-            g.rem_c_lo = c->lo_c2 ? c->lo_c2 + (size_t)c->lo_nz * P : nullptr;
+            g.has_lo = 1;
+            g.lo_nz = c->lo_nz;
             g.peer_lo_y = c->lo_base[3] + c->lo_ghost_off;
+            mbl = &c->mapBlo[c->ipp];
+            if (kC2F) mcl = &c->mapC2lo;
         }
         if (c->hi_base[0]) {
-            g.rem_b_hi = c->hi_base[c->ipp] + P;
-            g.rem_c_hi = c->hi_c2 ? c->hi_c2 + P : nullptr;
+            g.has_hi = 1;
             g.peer_hi_y = c->hi_base[3];
+            mbh = &c->mapBhi[c->ipp];
+            if (kC2F) mch = &c->mapC2hi;
         }
     }
     g.tiles_x = (c->pitch + 127) / 128;
@@ -543,7 +558,8 @@ ws3d_status launch_tb(ws3d_ctx* c) {
     const TmaSchedule sch = tb_schedule(g.tiles, c->nz, (uint32_t)grid);
     g.clen = sch.clen;
     g.nitems = sch.nitems;
-    kern<<<sch.grid, kThreads, smem, c->stream>>>(c->mapA[c->ip], c->mapB[c->ipp], c->mapC2b, g);
+    kern<<<sch.grid, kThreads, smem, c->stream>>>(c->mapA[c->ip], c->mapB[c->ipp], c->mapC2b, *mbl,
+                                                  *mbh, *mcl, *mch, g);
     ws3d_status s = check_launch(c, "k_step_tma2");
     if (s != WS3D_OK) return s;
     c->tb_launches++;
@@ -551,7 +567,7 @@ ws3d_status launch_tb(ws3d_ctx* c) {
     // previous pressure; the old pair becomes the free pair.
     const int order[4] = {3, 2, c->ip, c->ipp};
     float *nb[4], *nlo[4], *nhi[4];
-    CUtensorMap nP[4], nT[4], nA[4], nB[4];
+    CUtensorMap nP[4], nT[4], nA[4], nB[4], nBl[4], nBh[4];
     for (int k = 0; k < 4; ++k) {
         nb[k] = c->buf[order[k]];
         nlo[k] = c->lo_base[order[k]];
@@ -560,6 +576,8 @@ ws3d_status launch_tb(ws3d_ctx* c) {
         nT[k] = c->mapT[order[k]];
         nA[k] = c->mapA[order[k]];
         nB[k] = c->mapB[order[k]];
+        nBl[k] = c->mapBlo[order[k]];
+        nBh[k] = c->mapBhi[order[k]];
     }
     for (int k = 0; k < 4; ++k) {
         c->buf[k] = nb[k];
@@ -569,6 +587,8 @@ ws3d_status launch_tb(ws3d_ctx* c) {
         c->mapT[k] = nT[k];
         c->mapA[k] = nA[k];
         c->mapB[k] = nB[k];
+        c->mapBlo[k] = nBl[k];
+        c->mapBhi[k] = nBh[k];
     }
     c->ip = 0;
     c->ipp = 1;
@@ -1675,6 +1695,22 @@ namespace {
 // Called after the neighbours' pointers, caps and sizes are in place.
 ws3d_status attach_common(ws3d_ctx* c) {
     c->halo = c->lo_base[0] != nullptr || c->hi_base[0] != nullptr;
+    // tensor maps over the neighbours' buffers (two-step slabs; see mapBlo)
+    c->peer_maps = c->halo && c->tma_maps && tb_shape_ok(c);
+    for (int b = 0; b < 4 && c->peer_maps; ++b) {
+        if (c->lo_base[b])
+            c->peer_maps = encode_slab_map(c, &c->mapBlo[b], c->lo_base[b], kTbRow, kTbTY + 2,
+                                           (uint64_t)c->lo_nz + 2);
+        if (c->peer_maps && c->hi_base[b])
+            c->peer_maps = encode_slab_map(c, &c->mapBhi[b], c->hi_base[b], kTbRow, kTbTY + 2,
+                                           (uint64_t)c->hi_nz + 2);
+    }
+    if (c->peer_maps && c->lo_c2)
+        c->peer_maps = encode_slab_map(c, &c->mapC2lo, c->lo_c2, kTbRow, kTbTY + 2,
+                                       (uint64_t)c->lo_nz + 2);
+    if (c->peer_maps && c->hi_c2)
+        c->peer_maps = encode_slab_map(c, &c->mapC2hi, c->hi_c2, kTbRow, kTbTY + 2,
+                                       (uint64_t)c->hi_nz + 2);
     c->halo_synced = false;
     c->halo_steps = 0;
     c->hdepth = 1;
@@ -1854,6 +1890,10 @@ ws3d_status ws3d_halo_set_depth(ws3d_ctx* c, uint32_t depth) {
                         "halo_set_depth: temporal depth 2 needs this slab and its neighbours "
                         "two-step capable (auto or tma2 variant, TMA kernels, monotone sponge of "
                         "width <= 64, >= 2 planes each) with c2 given the same way");
+        if (!c->peer_maps)
+            return fail(c, WS3D_EPEER,
+                        "halo_set_depth: tensor maps over the neighbours' buffers could not be "
+                        "encoded");
     }
     c->hdepth = depth;
     c->halo_synced = false;

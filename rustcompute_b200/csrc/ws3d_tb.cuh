@@ -39,20 +39,23 @@
 // z-slabs (temporal depth 2, two ghost planes per side in every field
 // buffer): X is also computed on ghost planes -1 / nz, from the two ghost
 // planes of A on that side (stored there by the neighbour's previous launch)
-// and the neighbour's own B and c2 planes, which the consumer warps read over
-// NVLink into the staged rows before that item (B changes between launches
-// and only its owner updates it, so no copy of it is kept here).  Y of planes
-// 0, 1 / nz-2, nz-1 is also stored into the neighbour's Y buffer, i.e. its two
-// ghost planes of the next launch's A.  Runs that read ghost planes or store
-// into a neighbour wait (bounded) for its flag, raised before its launch;
-// those runs take a separate instance of the item code, interior runs the
-// one-GPU code.  Equal to single steps bit for bit.
+// and the neighbour's own B and c2 planes, which the producer stages by TMA
+// straight from the neighbour's buffers over NVLink (tensor maps over the
+// mapped peer buffers; plain loads, no multicast -- B changes between
+// launches and only its owner updates it, so no copy of it is kept here).  Y
+// of planes 0, 1 / nz-2, nz-1 is also stored into the neighbour's Y buffer,
+// i.e. its two ghost planes of the next launch's A.  Runs that read ghost
+// planes or the neighbour's planes, or store into a neighbour, wait (bounded)
+// for its flag, raised before its launch; those runs take a separate
+// instance of the item code, interior runs the one-GPU code.  Equal to single
+// steps bit for bit.
 //
 // Every mbarrier wait is bounded.  The item's barrier is a vote
 // (bar.red.or): if any consumer warp's wait gave up, all consumer warps see
 // it and leave together, so no warp is left waiting at a barrier.
 // The producer waits (bounded) for the copies it issued before it exits.  TMA
-// loads read this GPU's memory only, without multicast; default face layout.
+// loads never use multicast; they read this GPU's memory, and on z-slabs the
+// neighbour's own edge planes of B and c2; default face layout.
 #pragma once
 
 #include "ws3d_lean.cuh"
@@ -102,14 +105,13 @@ struct TbArgs {
     uint64_t step1;           // global index of step t+1
     uint32_t tiles_x, tiles, clen, nitems;
     int a_zoff;               // tensor-map z of A plane q is q + a_zoff
-    // z-slabs (all null on one GPU).  X is also computed on the ghost planes
-    // -1 / nz from the ghost planes of A and the neighbour's own B and c2
-    // planes (read in place over NVLink); Y of the two first / last planes is
-    // stored into the neighbour's Y buffer (its two ghost planes).
-    const float* rem_b_lo;    // lower neighbour's B at its last plane (= our plane -1)
-    const float* rem_b_hi;    // upper neighbour's B at its plane 0 (= our plane nz)
-    const float* rem_c_lo;    // the same planes of the neighbours' c2 fields (kC2F)
-    const float* rem_c_hi;
+    // z-slabs (zero / null on one GPU).  X is also computed on the ghost
+    // planes -1 / nz from the ghost planes of A and the neighbour's own B and
+    // c2 planes (staged by TMA from its buffers: tmBlo / tmC2lo at plane
+    // coordinate lo_nz, tmBhi / tmC2hi at 1); Y of the two first / last planes
+    // is stored into the neighbour's Y buffer (its two ghost planes).
+    uint32_t has_lo, has_hi;  // a lower / upper neighbour
+    uint32_t lo_nz;           // the lower neighbour's owned planes
     float* peer_lo_y;         // lower neighbour's Y buffer at its first upper ghost plane
     float* peer_hi_y;         // upper neighbour's Y buffer at its first lower ghost plane
 };
@@ -141,7 +143,9 @@ __device__ __forceinline__ float4 add_at(float4 v, int e, float d) {
 template <bool kC2F, bool kSlab>
 __global__ void __launch_bounds__(32 * (kTbTY + 3), kTbCtasPerSm)
 k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-            const __grid_constant__ CUtensorMap tmC2, TbArgs g) {
+            const __grid_constant__ CUtensorMap tmC2, const __grid_constant__ CUtensorMap tmBlo,
+            const __grid_constant__ CUtensorMap tmBhi, const __grid_constant__ CUtensorMap tmC2lo,
+            const __grid_constant__ CUtensorMap tmC2hi, TbArgs g) {
     using L = TbLayout<kC2F>;
     constexpr int S = kTbStages, TY = kTbTY, R = kTbRow;
     const StepParams& a = g.a;
@@ -196,7 +200,9 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const int x0 = (int)((tile % g.tiles_x) * 128u), y0 = (int)((tile / g.tiles_x) * TY);
             // Runs that read ghost planes (A down to zs-2 / up to ze+1, the
             // neighbour's B and c2) or store into a neighbour's ghost planes
-            // (Y of planes 0, 1 / nz-2, nz-1) wait for that neighbour's flag.
+            // (Y of planes 0, 1 / nz-2, nz-1) wait for that neighbour's flag;
+            // the acquire is then ordered before this thread's TMA loads of
+            // our ghost planes and of the neighbour's planes.
             const bool need_lo = kSlab && a.wait_lo && zs < 2;
             const bool need_hi = kSlab && a.wait_hi && ze + 1 >= (int)a.nz;
             if (need_lo || need_hi) {
@@ -222,10 +228,23 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     const int q = zA - 1;
                     mbar_expect_tx(&full[s], L::kTx);
                     tma_load_3d(st, &tmA, x0 - 4, y0 - 2, zA + g.a_zoff, &full[s]);
-                    tma_load_3d(st + L::kABytes, &tmB, x0 - 4, y0 - 1, q + 1, &full[s]);
+                    // B and c2 of plane q; of the ghost planes -1 / nz from the
+                    // neighbour's own buffers (its last plane / its plane 0)
+                    const CUtensorMap* mb = &tmB;
+                    const CUtensorMap* mc = &tmC2;
+                    int zb = q + 1;
+                    if (kSlab && q < 0 && g.has_lo) {
+                        mb = &tmBlo;
+                        mc = &tmC2lo;
+                        zb = (int)g.lo_nz;
+                    } else if (kSlab && q >= (int)a.nz && g.has_hi) {
+                        mb = &tmBhi;
+                        mc = &tmC2hi;
+                        zb = 1;
+                    }
+                    tma_load_3d(st + L::kABytes, mb, x0 - 4, y0 - 1, zb, &full[s]);
                     if (kC2F)
-                        tma_load_3d(st + L::kABytes + L::kBBytesPad, &tmC2, x0 - 4, y0 - 1, q + 1,
-                                    &full[s]);
+                        tma_load_3d(st + L::kABytes + L::kBBytesPad, mc, x0 - 4, y0 - 1, zb, &full[s]);
                 }
                 ++j;
                 if (++s == S) {
@@ -264,8 +283,8 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     };
 
     // X planes this slab computes: its own, plus ghost plane -1 / nz next to a neighbour
-    const int xlo = kSlab && g.rem_b_lo ? -1 : 0;
-    const int xhi = (int)a.nz + (kSlab && g.rem_b_hi ? 1 : 0);
+    const int xlo = kSlab && g.has_lo ? -1 : 0;
+    const int xhi = (int)a.nz + (kSlab && g.has_hi ? 1 : 0);
     uint32_t s = 0, ph = 0;  // stage and full-barrier parity of the current item
     for (uint32_t item = blockIdx.x; item < g.nitems; item += gridDim.x) {
         const uint32_t chunk = item / g.tiles, tile = item - chunk * g.tiles;
@@ -445,82 +464,25 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             return end_item(ok, true);
         };
 
-        // z-slabs: X on ghost plane q = -1 (item 2 of the first chunk) or
-        // q = nz (the last item of the last chunk) takes the neighbour's own B
-        // and c2 planes, read in place (the staged rows are our stale copy):
-        // warp w overwrites row w of the staged boxes (core and halo columns),
-        // then the consumer warps meet at a barrier before anyone reads them.
         const int last = n + 3;
-        const bool fill_first = zs == 0 && g.rem_b_lo != nullptr;
-        const bool fill_last = ze == (int)a.nz && g.rem_b_hi != nullptr;
-        auto fill = [&](bool lo_side) {
-            const float* rb = lo_side ? g.rem_b_lo : g.rem_b_hi;
-            const float* rc = lo_side ? g.rem_c_lo : g.rem_c_hi;
-            if (__all_sync(0xffffffffu, mbar_wait(&full[s], ph))) {
-                float* Bq = reinterpret_cast<float*>(smem + s * L::kStage + L::kABytes);
-                float* Cq = Bq + L::kBBytesPad / 4;
-                const bool yin = y < a.H;  // row w of the boxes is y0 - 1 + w
-                const int64_t o = (int64_t)y * a.pitch;
-                // peer memory written before the flag the producer waited for: L2 path
-                float4 b4 = z4, c4 = z4;
-                if (yin && x < a.pitch) {
-                    b4 = __ldcg(reinterpret_cast<const float4*>(rb + o + x));
-                    if (kC2F) c4 = __ldcg(reinterpret_cast<const float4*>(rc + o + x));
-                }
-                *reinterpret_cast<float4*>(Bq + w * R + 4 + 4 * lane) = b4;
-                if (kC2F) *reinterpret_cast<float4*>(Cq + w * R + 4 + 4 * lane) = c4;
-                if (lane < 2) {  // halo columns x0-1, x0+128
-                    const uint32_t hx = lane == 0 ? x0 - 1u : x0 + 128u;
-                    const int col = lane == 0 ? 3 : 132;
-                    const bool in = yin && hx < a.pitch;
-                    Bq[w * R + col] = in ? __ldcg(rb + o + hx) : 0.f;
-                    if (kC2F) Cq[w * R + col] = in ? __ldcg(rc + o + hx) : 0.f;
-                }
-                // the producer's later TMA writes into this stage follow these stores
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            }
-            asm volatile("bar.sync 2, %0;" ::"n"(32 * (kTbTY + 2)) : "memory");
-        };
 
         float4 am = z4, ac = z4, ap = z4, xm = z4, xc = z4, xn = z4;
         float hm = 0.f, hc = 0.f, hp = 0.f;
         // Items 2 .. last, three per iteration (the z queues rotate by
-        // renaming).  Slabs: the main loop leaves the last item to the tail,
-        // so that only the tail checks for the ghost-plane fill.
+        // renaming).
         auto run_items = [&](auto tag) -> bool {
             bool ab = false;
             int i = 2;
-            if constexpr (!(kSlab && (decltype(tag)::value & 2) != 0)) {
-                for (; !ab && i + 2 <= last; i += 3) {
-                    ab = body(tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
-                         body(tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
-                         body(tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
-                }
-                if (!ab && i <= last) ab = body(tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
-                if (!ab && i <= last) ab = body(tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
-            } else {
-                for (; !ab && i + 3 <= last; i += 3) {
-                    ab = body(tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
-                         body(tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
-                         body(tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
-                }
-                if (!ab && i <= last) {
-                    if (i == last && fill_last) fill(false);
-                    ab = body(tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
-                }
-                if (!ab && i <= last) {
-                    if (i == last && fill_last) fill(false);
-                    ab = body(tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
-                }
-                if (!ab && i <= last) {
-                    if (fill_last) fill(false);  // i == last here
-                    ab = body(tag, i++, ap, am, ac, xn, xm, xc, hp, hm, hc);
-                }
+            for (; !ab && i + 2 <= last; i += 3) {
+                ab = body(tag, i, am, ac, ap, xm, xc, xn, hm, hc, hp) ||
+                     body(tag, i + 1, ac, ap, am, xc, xn, xm, hc, hp, hm) ||
+                     body(tag, i + 2, ap, am, ac, xn, xm, xc, hp, hm, hc);
             }
+            if (!ab && i <= last) ab = body(tag, i++, am, ac, ap, xm, xc, xn, hm, hc, hp);
+            if (!ab && i <= last) ab = body(tag, i++, ac, ap, am, xc, xn, xm, hc, hp, hm);
             return ab;
         };
         bool abort = prologue(am, hm, false) || prologue(ac, hc, true);
-        if (kSlab && !abort && fill_first) fill(true);  // item 2: X on plane -1
         if (!abort) {
             using I0 = std::integral_constant<int, 0>;
             using I1 = std::integral_constant<int, 1>;

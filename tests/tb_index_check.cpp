@@ -8,8 +8,8 @@
 //     (planes [zs, ze) of the run, rows y < H, x < pitch);
 //   - slabs: Y of planes 0, 1 / nz-2, nz-1 stored into the neighbours' Y
 //     buffers (their ghost planes nz_lo, nz_lo+1 / -1, -2);
-//   - slabs: the fill's loads of the neighbours' own edge planes (p_{t-1}
-//     and c2, core float4 per lane and the two halo columns);
+//   - slabs: the plane coordinates of the producer's TMA boxes of the
+//     neighbours' own edge planes (p_{t-1} and c2);
 //   - the single-step kernel's two-plane stores into the neighbours at
 //     temporal depth 2 and the source-ghost offsets of the host.
 // Allocations: a slab's field buffer holds planes [-2, nz + 2), the c2 field
@@ -64,7 +64,6 @@ int main(int argc, char** argv) {
         const int ze = (int)(nz < chunk * sch.clen + sch.clen ? nz : chunk * sch.clen + sch.clen);
         const uint32_t x0 = (tile % tiles_x) * 128u, y0 = (tile / tiles_x) * TY;
         const bool push_lo = has_lo && zs < 2, push_hi = has_hi && ze + 2 > (int)nz;
-        const bool fill_first = zs == 0 && has_lo, fill_last = ze == (int)nz && has_hi;
         for (int w = 0; w < TY + 2; ++w) {
             const bool do_y = w >= 1 && w <= TY;
             for (int lane = 0; lane < 32; ++lane) {
@@ -88,28 +87,30 @@ int main(int argc, char** argv) {
                         check("Y push hi", ((int64_t)qy - (int64_t)nz) * P + row, 4, P, pitch, -2,
                               (int)hi_nz + 2, (int)item, w, lane);
                 }
-                // the fill of the staged rows from the neighbours' own edge planes
-                for (int side = 0; side < 2; ++side) {
-                    if (!(side == 0 ? fill_first : fill_last)) continue;
-                    const int nb_nz = (int)(side == 0 ? lo_nz : hi_nz);
-                    const int edge = side == 0 ? nb_nz - 1 : 0;   // their last / first plane
-                    const bool yin = y < H;
-                    if (yin && x < pitch) {
-                        check("fill B", (int64_t)edge * P + (int64_t)y * pitch + x, 4, P, pitch,
-                              -2, nb_nz + 2, (int)item, w, lane);
-                        check("fill c2", (int64_t)edge * P + (int64_t)y * pitch + x, 4, P, pitch,
-                              -1, nb_nz + 1, (int)item, w, lane);
-                    }
-                    if (lane < 2) {
-                        const uint32_t hx = lane == 0 ? x0 - 1u : x0 + 128u;
-                        if (yin && hx < pitch) {
-                            check("fill B halo", (int64_t)edge * P + (int64_t)y * pitch + hx, 1, P,
-                                  pitch, -2, nb_nz + 2, (int)item, w, lane);
-                            check("fill c2 halo", (int64_t)edge * P + (int64_t)y * pitch + hx, 1,
-                                  P, pitch, -1, nb_nz + 1, (int)item, w, lane);
-                        }
-                    }
+            }
+        }
+        // the producer's TMA boxes of p_{t-1} and c2 for the ghost planes -1 / nz
+        // come from the neighbour's own buffers (maps over its planes -1 .. nz_nb,
+        // coordinate = plane + 1): its last plane / its plane 0, whole boxes
+        // inside the map's plane range (x and y are clipped by the hardware)
+        for (int i = 2; i <= (ze - zs) + 3; ++i) {
+            const int q = zs - 3 + i;
+            ++g_checked;
+            if (q < 0 && has_lo) {
+                const int zc = (int)lo_nz;   // its plane lo_nz - 1
+                if (!(zc >= 0 && zc < (int)lo_nz + 2)) {
+                    if (g_bad < 20) fprintf(stderr, "OUT OF BOUNDS peer B/c2 lo plane %d\n", zc);
+                    ++g_bad;
                 }
+            } else if (q >= (int)nz && has_hi) {
+                const int zc = 1;            // its plane 0
+                if (!(zc >= 0 && zc < (int)hi_nz + 2)) {
+                    if (g_bad < 20) fprintf(stderr, "OUT OF BOUNDS peer B/c2 hi plane %d\n", zc);
+                    ++g_bad;
+                }
+            } else if (q < -1 || q > (int)nz) {
+                if (g_bad < 20) fprintf(stderr, "own B/c2 box outside planes -1..nz: %d\n", q);
+                ++g_bad;
             }
         }
     }
