@@ -165,9 +165,10 @@ struct ws3d_ctx {
 namespace {
 
 constexpr size_t kFlagWords = 32;
-// Flag block words: 0 / 1 the lower / upper neighbour's flag, 2 status, 4 / 5
-// the persistent grid barrier, 6 the resident kernel's decision, 8 / 9 the
-// neighbour-wait accumulators (ns, count).
+// Flag block words: 0 / 1 the lower / upper neighbour's flag, 2 status, 4 the
+// persistent grid barrier's arrival counter, 6 the resident kernel's decision,
+// 8 / 9 the neighbour-wait accumulators (ns, count).
+constexpr size_t kBarWord = 4;
 constexpr size_t kWaitAccWord = 8;
 
 struct DeviceGuard {
@@ -669,8 +670,9 @@ ws3d_status launch_persistent(ws3d_ctx* c, uint64_t n) {
     q.lo_flag = c->halo ? c->lo_flag : nullptr;
     q.hi_flag = c->halo ? c->hi_flag : nullptr;
     q.halo_base = c->halo_steps;
-    q.bar_count = reinterpret_cast<unsigned int*>(c->flags + 4);
-    q.bar_gen = reinterpret_cast<unsigned int*>(c->flags + 5);
+    q.bar = c->flags + kBarWord;
+    // the barrier's arrival counter starts every launch at zero (stream order)
+    WS3D_CUDA(c, cudaMemsetAsync(q.bar, 0, sizeof *q.bar, c->stream), WS3D_ELAUNCH);
     q.src_off = c->src_off;
     q.wavelet = c->wavelet;
     q.src_ghost = c->src_ghost;
@@ -2053,8 +2055,9 @@ ws3d_status res_launch_t(ws3d_ctx* c) {
     q.a = make_params(c);
     q.buf[0] = c->buf[c->ip];
     q.buf[1] = c->buf[c->ipp];
-    q.bar_count = reinterpret_cast<unsigned int*>(c->flags + 4);
-    q.bar_gen = reinterpret_cast<unsigned int*>(c->flags + 5);
+    q.bar = c->flags + kBarWord;
+    // the barrier's arrival counter starts every launch at zero (stream order)
+    WS3D_CUDA(c, cudaMemsetAsync(q.bar, 0, sizeof *q.bar, c->stream), WS3D_ELAUNCH);
     q.src_off = c->src_off;
     q.wavelet = c->wavelet;
     q.n_src = c->n_src;

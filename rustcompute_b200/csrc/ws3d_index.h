@@ -72,22 +72,23 @@ WS3D_HD ZsLane zs_lane(uint32_t bx, uint32_t by, int lane, int w, uint32_t W, ui
 // Offset of plane `z` (may be -1 or nz: the ghosts).
 WS3D_HD int64_t zs_plane(int64_t z, int64_t plane) { return z * plane; }
 
-// Row-parallel persistent body (k_persistent_rows): row r of a step is
-// x-tile tx of row y of plane z, 128 cells.  On z-slabs the interior planes
-// 1 .. nz-2 come first, then plane 0, then plane nz-1 (their waits for the
-// neighbours' flags overlap the interior rows).
+// Block-parallel persistent body (k_persistent_rows, k_resident): block b of
+// a step is x-tile tx of rows yb*NW .. yb*NW + NW - 1 of plane z (one warp per
+// row, 128 cells a row).  On z-slabs the interior planes 1 .. nz-2 come first,
+// then plane 0, then plane nz-1 (their waits for the neighbours' flags overlap
+// the interior blocks).
 struct RowCoord {
-    uint32_t z, y, tx;
+    uint32_t z, yb, tx;
 };
-WS3D_HD RowCoord row_coord(uint64_t r, uint32_t H, uint32_t tiles_x, uint32_t nz, bool slab) {
-    const uint64_t per_plane = (uint64_t)H * tiles_x;
-    const uint64_t k = r / per_plane;
-    const uint32_t rem = (uint32_t)(r - k * per_plane);
+WS3D_HD RowCoord row_coord(uint64_t b, uint32_t yblocks, uint32_t tiles_x, uint32_t nz, bool slab) {
+    const uint64_t per_plane = (uint64_t)yblocks * tiles_x;
+    const uint64_t k = b / per_plane;
+    const uint32_t rem = (uint32_t)(b - k * per_plane);
     RowCoord c;
     c.z = (uint32_t)k;
     if (slab && nz > 1) c.z = k + 2 < nz ? (uint32_t)k + 1u : (k + 2 == nz ? 0u : nz - 1);
-    c.y = rem / tiles_x;
-    c.tx = rem - c.y * tiles_x;
+    c.yb = rem / tiles_x;
+    c.tx = rem - c.yb * tiles_x;
     return c;
 }
 

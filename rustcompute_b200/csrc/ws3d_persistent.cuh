@@ -31,8 +31,7 @@ struct PersistentArgs {
     unsigned long long* lo_flag;  // lower neighbour's flag this slab raises
     unsigned long long* hi_flag;  // upper neighbour's flag this slab raises
     unsigned long long halo_base; // halo steps taken before this launch
-    unsigned int* bar_count;      // grid barrier: arrivals
-    unsigned int* bar_gen;        // grid barrier: generation
+    unsigned long long* bar;      // grid barrier: arrivals (zeroed by the host before the launch)
     const uint64_t* src_off;
     const float* wavelet;
     const long long* src_ghost;
@@ -44,38 +43,43 @@ struct PersistentArgs {
     uint32_t tiles_x, tiles, clen, nitems;
 };
 
-__device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void st_release_gpu_u32(unsigned int* p, unsigned int v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
-// Bounded grid barrier over all CTAs of a cooperative launch.  Returns false
-// on every thread of a CTA whose leader gave up (status bit 3 set).
-__device__ __forceinline__ bool grid_barrier(unsigned int* count, unsigned int* gen,
-                                             unsigned int nblocks, unsigned long long budget_ns,
-                                             unsigned int* status, int* s_ok) {
+// Bounded grid barrier over all CTAs of a cooperative launch.  Each CTA's
+// leader adds one arrival to a 64-bit counter that only grows (the host
+// zeroes it before the launch) with release semantics, which publishes the
+// CTA's writes, and polls the same counter with acquire loads until the
+// round is complete, i.e. until it reaches the next multiple of the CTA
+// count -- one atomic per CTA and no reset, generation word or last-arriver
+// release on the critical path.  Then the status word: any error recorded
+// before some CTA arrived is seen by every CTA after the round.  Returns
+// false on every thread of a CTA whose leader gave up (status bit 3 set) or
+// found an error.
+__device__ __forceinline__ bool grid_barrier(unsigned long long* count, unsigned int nblocks,
+                                             unsigned long long budget_ns, unsigned int* status,
+                                             int* s_ok) {
     __syncthreads();
     if (threadIdx.x == 0 && threadIdx.y == 0) {
         int ok = 1;
-        const unsigned int g = ld_acquire_gpu_u32(gen);
-        __threadfence();
-        if (atomicAdd(count, 1u) == nblocks - 1) {
-            atomicExch(count, 0u);
-            __threadfence();
-            st_release_gpu_u32(gen, g + 1u);
-        } else {
+        unsigned long long old;
+        asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;"
+                     : "=l"(old)
+                     : "l"(count)
+                     : "memory");
+        const unsigned long long target = (old / nblocks + 1ull) * nblocks;
+        if (ld_acquire_gpu_u64(count) < target) {
             bool done = false;
             const unsigned long long t0 = global_ns();
             for (unsigned int it = 0; it < (1u << 26); ++it) {
-                if (ld_acquire_gpu_u32(gen) != g) {
+                __nanosleep(32);
+                if (ld_acquire_gpu_u64(count) >= target) {
                     done = true;
                     break;
                 }
-                __nanosleep(32);
                 if ((it & 63u) == 63u && global_ns() - t0 > budget_ns) break;
             }
             if (!done) {
@@ -115,35 +119,36 @@ __global__ void __launch_bounds__(32 * TY, 3) k_persistent(PersistentArgs q) {
                 if (q.hi_flag) st_release_sys(q.hi_flag, q.halo_base + s + 1);
             }
         }
-        if (q.n_src && !grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok))
+        if (q.n_src && !grid_barrier(q.bar, nb, a.budget_ns, a.status, &s_ok))
             return;
         for (uint32_t item = blockIdx.x; item < q.nitems; item += nb) {
             const uint32_t chunk = item / q.tiles, tile = item - chunk * q.tiles;
             const uint32_t zs = chunk * q.clen, ze = min(a.nz, zs + q.clen);
             zs_tile<kC2F, kCells, TY>(a, tile % q.tiles_x, tile / q.tiles_x, zs, ze);
         }
-        if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok)) return;
+        if (!grid_barrier(q.bar, nb, a.budget_ns, a.status, &s_ok)) return;
     }
 }
 
 // ---------------------------------------------------------------------------
-// Row-parallel persistent step (default face layout).
+// Block-parallel persistent step (default face layout).
 //
 // k_persistent's z-streaming items walk a run of planes through a register
 // queue: on a small, L2-resident grid (config 5, 128^3) every step is then a
-// chain of dependent plane loads per CTA.  Here a step is a flat set of rows
-// -- 128 cells of one (y, z) at one x-tile, a float4 per lane -- spread over
-// every warp of the grid; each row issues all its loads at once (centre, z
-// and y neighbours, p_prev, c2, the two x-halo cells), so a step costs about
+// chain of dependent plane loads per CTA.  Here a step is a flat set of
+// blocks -- NW rows (one per warp) of 128 cells of one plane z at one x-tile --
+// spread over the CTAs; each row issues all its loads at once (centre, z
+// neighbours, p_prev, c2, the two x-halo cells), the y neighbours come from
+// the other rows of the block through shared memory, so a step costs about
 // one L2 round trip plus the grid barrier.  The cell rule is cells4_default,
 // the same operations in the same order as every other kernel here.
 //
 // Fields are rewritten every step inside the launch, so they are read
 // through L2 (ld.global.cg): no SM's L1 can hold a value from an earlier
-// step.  On z-slabs the rows of the first and last owned plane (they read
+// step.  On z-slabs the blocks of the first and last owned plane (they read
 // the ghost planes a neighbour stores into, and store into the neighbour's
-// ghost planes) run after the interior rows of the step; a warp waits
-// (bounded) for the neighbour's flag once before its first such row.
+// ghost planes) run after the interior blocks of the step; a CTA waits
+// (bounded) for the neighbour's flag once before its first such block.
 // ---------------------------------------------------------------------------
 constexpr int kRowThreads = 512;
 
@@ -151,24 +156,32 @@ __device__ __forceinline__ float4 ldcg4(const float* p) {
     return __ldcg(reinterpret_cast<const float4*>(p));
 }
 
-// One step over rows gw, gw + G, ... of the step's row list.
-template <bool kC2F>
+// One step over the blocks cta, cta + ncta, ... of the step's block list;
+// warp w of the CTA computes row w of each block.  The block's rows of the
+// current pressure are shared through shared memory, so each row loads its
+// own p, its z neighbours, p_prev (and c2) from L2, and the y neighbours come
+// from the rows the other warps loaded (plus two halo rows per block).
+template <bool kC2F, int NW>
 __device__ __forceinline__ void step_rows(const StepParams& a, uint32_t tiles_x, bool halo,
-                                          uint32_t gw, uint32_t G) {
+                                          uint32_t w, uint32_t cta, uint32_t ncta) {
+    __shared__ float4 srow[NW + 2][32];
     const uint32_t lane = threadIdx.x & 31u;
-    const uint64_t nrows = (uint64_t)a.H * tiles_x * a.nz;
+    const uint32_t yblocks = (a.H + NW - 1) / NW;
+    const uint64_t nblk = (uint64_t)yblocks * tiles_x * a.nz;
     const int64_t P = (int64_t)a.plane;
+    const int64_t pitch = (int64_t)a.pitch;
     const float* __restrict__ p = a.p;
     float* __restrict__ pp = a.pp;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
     bool waited_lo = a.wait_lo == nullptr, waited_hi = a.wait_hi == nullptr;
-    for (uint64_t r = gw; r < nrows; r += G) {
-        const RowCoord rc = row_coord(r, a.H, tiles_x, a.nz, halo);
-        const uint32_t z = rc.z, y = rc.y;
+    for (uint64_t blk = cta; blk < nblk; blk += ncta) {
+        const RowCoord rc = row_coord(blk, yblocks, tiles_x, a.nz, halo);
+        const uint32_t z = rc.z, y0 = rc.yb * NW, y = y0 + w;
         const uint32_t x0 = rc.tx * 128u, x = x0 + 4u * lane;
-        if (halo) {
+        if (halo) {  // CTA-uniform: one bounded wait per neighbour and step
             const bool lo = z == 0 && !waited_lo, hi = z + 1 == a.nz && !waited_hi;
             if (lo || hi) {
-                if (lane == 0) {
+                if (threadIdx.x == 0 && threadIdx.y == 0) {
                     unsigned int bad = 0;
                     if (lo && !wait_flag_geq(a.wait_lo, a.wait_val, a.budget_ns, a.wait_acc))
                         bad |= 1u;
@@ -176,43 +189,50 @@ __device__ __forceinline__ void step_rows(const StepParams& a, uint32_t tiles_x,
                         bad |= 2u;
                     if (bad) atomicOr(a.status, bad);
                 }
-                __syncwarp();
+                __syncthreads();
                 waited_lo = waited_lo || lo;
                 waited_hi = waited_hi || hi;
             }
         }
-        const bool act = x < a.pitch;
-        const int64_t o = (int64_t)z * P + (int64_t)y * a.pitch + x;
-        const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        float4 pc = z4, pm = z4, pn = z4, S = z4, N = z4, vpp = z4;
+        const bool xin = x < a.pitch;
+        const bool act = xin && y < a.H;
+        const int64_t o = (int64_t)z * P + (int64_t)y * pitch + x;
+        float4 pc = z4, pm = z4, pn = z4, vpp = z4;
         float4 c2v = make_float4(a.c2, a.c2, a.c2, a.c2);
         float hl = 0.f, hr = 0.f;
         if (act) {
-            // rows y - 1 / y + 1 of plane z exist in the allocation (the ghost
-            // planes frame it); at y = 0 / H - 1 the cells are faces and the
-            // values are not used
             pc = ldcg4(p + o);
             pm = ldcg4(p + o - P);
             pn = ldcg4(p + o + P);
-            S = ldcg4(p + o - (int64_t)a.pitch);
-            N = ldcg4(p + o + (int64_t)a.pitch);
             vpp = ldcg4(pp + o);
             if (kC2F) c2v = __ldg(reinterpret_cast<const float4*>(a.c2f + o));
+            if (lane == 0 && x0 > 0) hl = __ldcg(p + o - 1);
+            if (lane == 31 && x0 + 128u < a.pitch) hr = __ldcg(p + o + 4);
         }
-        if (lane == 0 && x0 > 0) hl = __ldcg(p + o - 1);
-        if (lane == 31 && x0 + 128u < a.pitch) hr = __ldcg(p + o + 4);
+        // halo rows y0 - 1 and y0 + NW: inside the allocation (the ghost planes
+        // frame the owned ones); at the faces y = 0 / H - 1 they are not used
+        float4 hy = z4;
+        if (xin && w == 0) hy = ldcg4(p + (int64_t)z * P + ((int64_t)y0 - 1) * pitch + x);
+        if (xin && w == NW - 1 && y0 + NW <= a.H)
+            hy = ldcg4(p + (int64_t)z * P + ((int64_t)y0 + NW) * pitch + x);
+        srow[w + 1][lane] = pc;
+        if (w == 0) srow[0][lane] = hy;
+        if (w == NW - 1) srow[NW + 1][lane] = hy;
         float wl = __shfl_up_sync(0xffffffffu, pc.w, 1);
         float er = __shfl_down_sync(0xffffffffu, pc.x, 1);
         if (lane == 0) wl = hl;
         if (lane == 31) er = hr;
+        __syncthreads();
         if (act) {
+            const float4 S = srow[w][lane], N = srow[w + 2][lane];
             const XYPre xy = make_xypre(x, y, a);
             const float4 out = cells4_default(xy, a.z0 + z, wl, er, S, N, pm, pc, pn, vpp, c2v, a);
             st4(pp + o, out);
-            const int64_t ro = (int64_t)y * a.pitch + x;
+            const int64_t ro = (int64_t)y * pitch + x;
             if (z == 0 && a.peer_lo) st4(a.peer_lo + ro, out);
             if (z + 1 == a.nz && a.peer_hi) st4(a.peer_hi + ro, out);
         }
+        __syncthreads();  // the next block's rows overwrite srow
     }
 }
 
@@ -222,8 +242,6 @@ __global__ void __launch_bounds__(kRowThreads, 2) k_persistent_rows(PersistentAr
     const unsigned int nb = gridDim.x;
     const bool leader = blockIdx.x == 0 && threadIdx.x == 0;
     const bool halo = q.lo_base[0] != nullptr || q.hi_base[0] != nullptr;
-    const uint32_t G = nb * (kRowThreads / 32);
-    const uint32_t gw = blockIdx.x * (kRowThreads / 32) + (threadIdx.x >> 5);
     for (uint64_t s = 0; s < q.nsteps; ++s) {
         const int cur = (int)((q.cur0 + s) & 1u);
         StepParams a = q.a;
@@ -243,10 +261,10 @@ __global__ void __launch_bounds__(kRowThreads, 2) k_persistent_rows(PersistentAr
                 if (q.hi_flag) st_release_sys(q.hi_flag, q.halo_base + s + 1);
             }
         }
-        if (q.n_src && !grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok))
+        if (q.n_src && !grid_barrier(q.bar, nb, a.budget_ns, a.status, &s_ok))
             return;
-        step_rows<kC2F>(a, q.tiles_x, halo, gw, G);
-        if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok)) return;
+        step_rows<kC2F, kRowThreads / 32>(a, q.tiles_x, halo, threadIdx.x >> 5, blockIdx.x, nb);
+        if (!grid_barrier(q.bar, nb, a.budget_ns, a.status, &s_ok)) return;
     }
 }
 
@@ -400,7 +418,7 @@ __device__ __forceinline__ bool res_energy(const ResidentArgs& r, const float* p
         for (int k = 0; k < TY; ++k) b += s_part[k];
         r.partial[blockIdx.x] = b;
     }
-    if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, s_ok)) return false;
+    if (!grid_barrier(q.bar, nb, a.budget_ns, a.status, s_ok)) return false;
     if (blockIdx.x == 0 && t == 0) {
         double e = 0.0;
         for (unsigned int k = 0; k < nb; ++k) e += r.partial[k];
@@ -510,7 +528,7 @@ __global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
     };
     // Barrier that also hands the leader's decision to every thread.
     auto barrier_decision = [&]() -> bool {
-        if (!grid_barrier(q.bar_count, q.bar_gen, nb, q.a.budget_ns, q.a.status, &s_ok))
+        if (!grid_barrier(q.bar, nb, q.a.budget_ns, q.a.status, &s_ok))
             return false;
         if (threadIdx.x == 0 && threadIdx.y == 0)
             s_op = *reinterpret_cast<volatile unsigned int*>(r.decision);
@@ -526,7 +544,7 @@ __global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
         if (pre && leader) apply_pending();
         if (op == kResExitTerm || op == kResExitIdle) {
             // the final energy reads the impulses just applied
-            if (pre && !grid_barrier(q.bar_count, q.bar_gen, nb, q.a.budget_ns, q.a.status, &s_ok))
+            if (pre && !grid_barrier(q.bar, nb, q.a.budget_ns, q.a.status, &s_ok))
                 ok = false;
             break;
         }
@@ -550,14 +568,14 @@ __global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
             if (leader && q.n_src)
                 inject_sources_dev(q.buf[cur], q.buf[cur ^ 1], q.src_off, q.wavelet, q.n_src,
                                    q.wl_len, q.step0 + ran, nullptr, nullptr, nullptr);
-            if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok)) {
+            if (!grid_barrier(q.bar, nb, a.budget_ns, a.status, &s_ok)) {
                 ok = false;
                 break;
             }
         }
         if constexpr (!kCells) {
             // default faces: the row-parallel body (one warp per row of 128 cells)
-            step_rows<kC2F>(a, q.tiles_x, false, blockIdx.x * TY + threadIdx.y, nb * TY);
+            step_rows<kC2F, TY>(a, q.tiles_x, false, threadIdx.y, blockIdx.x, nb);
         } else {
             for (uint32_t item = blockIdx.x; item < q.nitems; item += nb) {
                 const uint32_t chunk = item / q.tiles, tile = item - chunk * q.tiles;
@@ -570,7 +588,7 @@ __global__ void __launch_bounds__(32 * TY, 3) k_resident(ResidentArgs r) {
         const bool progress = (q.step0 + ran) % interval == 0;
         if (progress) {  // every CTA's writes of the step, then sum p^2
             double e = 0.0;
-            if (!grid_barrier(q.bar_count, q.bar_gen, nb, a.budget_ns, a.status, &s_ok) ||
+            if (!grid_barrier(q.bar, nb, a.budget_ns, a.status, &s_ok) ||
                 !res_energy<TY>(r, q.buf[cur] + a.plane, &e, &s_ok)) {
                 ok = false;
                 break;

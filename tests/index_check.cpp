@@ -174,51 +174,58 @@ static void run_async(uint32_t W, uint32_t H, uint32_t nz, int sms, bool halo) {
     }
 }
 
-// k_persistent_rows: every row of one step (row_coord, the kernel's own
-// mapping), every lane: the seven float4 loads, the two x-halo loads, the
-// store and the z-slab peer stores.
-static void run_rows(uint32_t W, uint32_t H, uint32_t nz, bool slab) {
+// k_persistent_rows / k_resident's block body: every block of one step
+// (row_coord, the kernels' own mapping), every warp row and lane: the four or
+// five float4 loads of its own row, the block's two halo rows, the two x-halo
+// loads, the store and the z-slab peer stores; every float4 of the owned
+// planes written exactly once.
+static void run_rows(uint32_t W, uint32_t H, uint32_t nz, bool slab, int NW) {
     const uint32_t pitch = (W + 31u) & ~31u;
     const int64_t P = (int64_t)H * pitch;
     const uint32_t tiles_x = (pitch + 127u) / 128u;
-    const uint64_t nrows = (uint64_t)H * tiles_x * nz;
+    const uint32_t yblocks = (H + NW - 1) / NW;
+    const uint64_t nblk = (uint64_t)yblocks * tiles_x * nz;
     const Field fp{"p", true}, fpp{"pp", false}, fc2{"c2", false}, fpeer{"peer plane", false};
-    std::vector<unsigned char> seen((size_t)nrows * 32, 0);
-    for (uint64_t r = 0; r < nrows; ++r) {
-        const RowCoord rc = row_coord(r, H, tiles_x, nz, slab);
-        const uint32_t x0 = rc.tx * 128u;
-        for (int lane = 0; lane < 32; ++lane) {
-            const uint32_t x = x0 + 4u * (uint32_t)lane;
-            const int64_t o = (int64_t)rc.z * P + (int64_t)rc.y * pitch + x;
-            if (x < pitch) {
-                const size_t cell = ((size_t)rc.z * H + rc.y) * pitch + x;
-                if (cell / 4 < seen.size()) seen[cell / 4]++;
-                check(fp, o, 4, pitch, nz, P, "rows centre", rc.tx, rc.y, rc.z, lane, 0);
-                check(fp, o - P, 4, pitch, nz, P, "rows z-1", rc.tx, rc.y, rc.z, lane, 0);
-                check(fp, o + P, 4, pitch, nz, P, "rows z+1", rc.tx, rc.y, rc.z, lane, 0);
-                check(fp, o - (int64_t)pitch, 4, pitch, nz, P, "rows y-1", rc.tx, rc.y, rc.z, lane, 0);
-                check(fp, o + (int64_t)pitch, 4, pitch, nz, P, "rows y+1", rc.tx, rc.y, rc.z, lane, 0);
-                check(fpp, o, 4, pitch, nz, P, "rows p_prev / store", rc.tx, rc.y, rc.z, lane, 0);
-                check(fc2, o, 4, pitch, nz, P, "rows c2", rc.tx, rc.y, rc.z, lane, 0);
-                if (slab && (rc.z == 0 || rc.z + 1 == nz))
-                    check(fpeer, (int64_t)rc.y * pitch + x, 4, pitch, 1, P, "rows peer store", rc.tx,
-                          rc.y, rc.z, lane, 0);
+    std::vector<unsigned char> seen((size_t)nz * H * pitch / 4 + 1, 0);
+    for (uint64_t blk = 0; blk < nblk; ++blk) {
+        const RowCoord rc = row_coord(blk, yblocks, tiles_x, nz, slab);
+        const uint32_t x0 = rc.tx * 128u, y0 = rc.yb * (uint32_t)NW;
+        for (int w = 0; w < NW; ++w)
+            for (int lane = 0; lane < 32; ++lane) {
+                const uint32_t x = x0 + 4u * (uint32_t)lane, y = y0 + (uint32_t)w;
+                const bool xin = x < pitch, act = xin && y < H;
+                const int64_t o = (int64_t)rc.z * P + (int64_t)y * pitch + x;
+                if (act) {
+                    seen[(((size_t)rc.z * H + y) * pitch + x) / 4]++;
+                    check(fp, o, 4, pitch, nz, P, "rows centre", rc.tx, y, rc.z, lane, w);
+                    check(fp, o - P, 4, pitch, nz, P, "rows z-1", rc.tx, y, rc.z, lane, w);
+                    check(fp, o + P, 4, pitch, nz, P, "rows z+1", rc.tx, y, rc.z, lane, w);
+                    check(fpp, o, 4, pitch, nz, P, "rows p_prev / store", rc.tx, y, rc.z, lane, w);
+                    check(fc2, o, 4, pitch, nz, P, "rows c2", rc.tx, y, rc.z, lane, w);
+                    if (lane == 0 && x0 > 0)
+                        check(fp, o - 1, 1, pitch, nz, P, "rows x-1", rc.tx, y, rc.z, lane, w);
+                    if (lane == 31 && x0 + 128u < pitch)
+                        check(fp, o + 4, 1, pitch, nz, P, "rows x+128", rc.tx, y, rc.z, lane, w);
+                    if (slab && (rc.z == 0 || rc.z + 1 == nz))
+                        check(fpeer, (int64_t)y * pitch + x, 4, pitch, 1, P, "rows peer store",
+                              rc.tx, y, rc.z, lane, w);
+                }
+                if (xin && w == 0)
+                    check(fp, (int64_t)rc.z * P + ((int64_t)y0 - 1) * pitch + x, 4, pitch, nz, P,
+                          "rows halo y0-1", rc.tx, y, rc.z, lane, w);
+                if (xin && w == NW - 1 && y0 + NW <= H)
+                    check(fp, (int64_t)rc.z * P + ((int64_t)y0 + NW) * pitch + x, 4, pitch, nz, P,
+                          "rows halo y0+NW", rc.tx, y, rc.z, lane, w);
             }
-            if (lane == 0 && x0 > 0)
-                check(fp, o - 1, 1, pitch, nz, P, "rows x-1", rc.tx, rc.y, rc.z, lane, 0);
-            if (lane == 31 && x0 + 128u < pitch)
-                check(fp, o + 4, 1, pitch, nz, P, "rows x+128", rc.tx, rc.y, rc.z, lane, 0);
-        }
     }
-    // every float4 of the owned planes exactly once per step
     for (uint32_t z = 0; z < nz; ++z)
         for (uint32_t y = 0; y < H; ++y)
             for (uint32_t x = 0; x < pitch; x += 4) {
-                const size_t cell = ((size_t)z * H + y) * pitch + x;
-                if (seen[cell / 4] != 1) {
+                const size_t c = (((size_t)z * H + y) * pitch + x) / 4;
+                if (seen[c] != 1) {
                     if (g_bad < 20)
                         fprintf(stderr, "rows: float4 at (%u,%u,%u) covered %d times\n", x, y, z,
-                                seen[cell / 4]);
+                                seen[c]);
                     ++g_bad;
                 }
             }
@@ -235,7 +242,7 @@ int main(int argc, char** argv) {
     const int ty = argc > 5 ? atoi(argv[5]) : 8;
     const bool halo = argc > 6 && atoi(argv[6]) != 0;
     if (argc > 7 && atoi(argv[7]) == 2) {
-        run_rows(W, H, nz, halo);
+        run_rows(W, H, nz, halo, ty);
         printf("checked %lld accesses, %d out of bounds\n", g_checked, g_bad);
         return g_bad == 0 ? 0 : 1;
     }

@@ -61,12 +61,13 @@ ROW_SHAPES = [(13, 7, 5), (130, 9, 20), (257, 11, 6), (3, 3, 3), (128, 128, 128)
 
 
 @pytest.mark.parametrize("shape", ROW_SHAPES)
-@pytest.mark.parametrize("halo", [0, 1])
-def test_persistent_row_kernel_accesses_in_bounds(checker, shape, halo):
-    """k_persistent_rows: every access in bounds and every float4 of the owned
-    planes written exactly once per step."""
+@pytest.mark.parametrize("halo,nw", [(0, 16), (1, 16), (0, 8)])
+def test_persistent_row_kernel_accesses_in_bounds(checker, shape, halo, nw):
+    """The block body of k_persistent_rows (16 warps) and k_resident (8): every
+    access in bounds and every float4 of the owned planes written exactly once
+    per step."""
     W, H, nz = shape
-    r = subprocess.run([checker, str(W), str(H), str(nz), "148", "8", str(halo), "2"],
+    r = subprocess.run([checker, str(W), str(H), str(nz), "148", str(nw), str(halo), "2"],
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr + r.stdout
 
