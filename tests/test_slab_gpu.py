@@ -112,6 +112,10 @@ def test_bounded_wait_times_out_and_context_stays_usable(grid):
         with pytest.raises(TimeoutError_):
             b.sync()
         assert time.time() - t0 < 30
+        # the waits that gave up are accounted: each ran for its whole budget
+        ns, n = b.halo_wait_stats(reset=True)
+        assert n >= 1 and ns >= n * 150_000_000, (ns, n)
+        assert b.halo_wait_stats() == (0, 0)
         # the status was reported and cleared; the context still works
         b.sync()
         assert np.isfinite(b.energy())
@@ -181,6 +185,8 @@ def test_two_step_slabs_ghost_plane_sources_odd_counts_and_impulses(nslab, grid)
                 b.inject_spherical_impulse(W // 4, H // 2, zb - 1, -0.3, 2.0)
     full.step_n(None, 7)
     grp.step_n(7)
+    # same-device slabs are ordered by the stream: no device-side waits at all
+    assert all(b.halo_wait_stats() == (0, 0) for b in slabs)
     fp, fpp = full.download_field(with_prev=True)
     gp = np.concatenate([b.download_field() for b in slabs])
     gpp = np.concatenate([b.download_field(with_prev=True)[1] for b in slabs])
