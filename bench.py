@@ -308,8 +308,8 @@ def pinned(a):
 def kernel_name(variant, wl, world, mode="step", depth=1):
     """The step kernel the library runs; on z-slabs two-step launches need
     temporal depth 2 (`depth`, as negotiated by slab.connect)."""
-    if mode == "persistent":
-        return "k_persistent"
+    if mode == "persistent":   # rows of at most 128 cells on one GPU: field in shared memory
+        return "k_persistent_smem" if world == 1 and wl.W <= 128 else "k_persistent_rows"
     if mode == "resident":
         return "k_resident"
     if variant in ("auto", "tma2"):   # mirrors the library's choice for the default faces
@@ -422,8 +422,9 @@ def c5_latency(world, rank, local, pg, barrier, per_rank, stream, dev, device_ga
             "persistent_steps": wl5.steps,
             "launch_per_step_us_per_step": launch_ms * 1e3 / n_launch,
             "launch_per_step_steps": n_launch,
-            "kernels": "k_persistent (one cooperative launch, one grid barrier per step) vs "
-                       "one k_step_zstream launch per step"}
+            "kernels": "one cooperative launch (k_persistent_smem on one GPU: the field in "
+                       "shared memory; k_persistent_rows on z-slabs), one grid barrier per step, "
+                       "vs one k_step_zstream launch per step"}
 
 
 def run_ours(args, wl):

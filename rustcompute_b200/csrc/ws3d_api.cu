@@ -9,6 +9,7 @@
 #include "ws3d_nvtx.h"
 #include "ws3d_async.cuh"
 #include "ws3d_persistent.cuh"
+#include "ws3d_smemstep.cuh"
 #include "ws3d_tb.cuh"
 #include "ws3d_tma.cuh"
 #include "ws3d_volume.cuh"
@@ -128,6 +129,9 @@ struct ws3d_ctx {
     uint64_t tb_launches = 0;
     int async_grid[2] = {0, 0};
     uint32_t tma_min_chunk = 32;  // WS3D_TMA_MIN_CHUNK (schedule tuning), read at create
+    // persistent launches of small one-GPU grids keep the field in shared
+    // memory (k_persistent_smem); WS3D_PERSISTENT_SMEM=0 at create turns it off
+    bool smem_persistent = true;
 
     // persistent mode: co-resident CTAs of k_persistent per instantiation
     int pers_resident[4] = {0, 0, 0, 0};
@@ -641,10 +645,69 @@ ws3d_status ensure_cell_arrays(ws3d_ctx* c);
 // ---- persistent mode --------------------------------------------------------
 constexpr int kPersTY = 8;
 
-// Default face layout: the row-parallel body (k_persistent_rows, one L2
-// round trip per step); per-cell boundary arrays: the z-streaming body.
+// Small one-GPU grids with the default faces and rows of at most 128 cells:
+// the field stays in shared memory for the whole launch (k_persistent_smem,
+// block shape from smem_step_shape).  *launched = false when the grid does
+// not qualify.
+template <bool kC2F>
+ws3d_status launch_persistent_smem(ws3d_ctx* c, uint64_t n, bool* launched) {
+    *launched = false;
+    if (!c->smem_persistent || c->halo || !c->cells_default || c->pitch > 128) return WS3D_OK;
+    auto kern = k_persistent_smem<kC2F>;
+    uint32_t by = 0, bz = 0;
+    if (!smem_step_shape(c->pitch, c->H, c->nz, (uint32_t)std::max(1, c->sm_count), kC2F,
+                         (uint64_t)kSmemMaxBytes, &by, &bz))
+        return WS3D_OK;
+    const int bytes = (int)smem_step_bytes(c->pitch, by, bz, kC2F);
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return cuda_fail(c, WS3D_ELAUNCH, e, "cudaFuncSetAttribute(smem step)");
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSmemThreads, bytes);
+    const uint32_t yblocks = (c->H + by - 1) / by;
+    const uint32_t nblk = yblocks * ((c->nz + bz - 1) / bz);
+    if (e != cudaSuccess || per_sm < 1 || nblk > (uint32_t)(per_sm * std::max(1, c->sm_count))) {
+        cudaGetLastError();
+        return WS3D_OK;  // not co-resident here: the row body takes the launch
+    }
+    SmemArgs q{};
+    q.a = make_params(c);
+    q.buf[0] = c->buf[c->ip];
+    q.buf[1] = c->buf[c->ipp];
+    q.bar = c->flags + kBarWord;
+    WS3D_CUDA(c, cudaMemsetAsync(q.bar, 0, sizeof *q.bar, c->stream), WS3D_ELAUNCH);
+    q.src_off = c->src_off;
+    q.wavelet = c->wavelet;
+    q.n_src = c->n_src;
+    q.wl_len = c->wl_len;
+    q.step0 = c->step;
+    q.nsteps = n;
+    q.by = by;
+    q.bz = bz;
+    q.yblocks = yblocks;
+    void* args[] = {&q};
+    e = cudaLaunchCooperativeKernel((const void*)kern, dim3(nblk), dim3(kSmemThreads), args,
+                                    (size_t)bytes, c->stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(c, WS3D_ELAUNCH, e, "cudaLaunchCooperativeKernel(k_persistent_smem)");
+    }
+    c->launches++;
+    c->persistent_launches++;
+    *launched = true;
+    return WS3D_OK;
+}
+
+// Default face layout: the field in shared memory for small one-GPU grids
+// (above), else the block-parallel body (k_persistent_rows, one L2 round trip
+// per step); per-cell boundary arrays: the z-streaming body.
 template <bool kC2F, bool kCells>
 ws3d_status launch_persistent(ws3d_ctx* c, uint64_t n) {
+    if constexpr (!kCells) {
+        bool launched = false;
+        ws3d_status s = launch_persistent_smem<kC2F>(c, n, &launched);
+        if (s != WS3D_OK || launched) return s;
+    }
     const void* kern = kCells ? (const void*)k_persistent<kC2F, kCells, kPersTY>
                               : (const void*)k_persistent_rows<kC2F>;
     const int threads = kCells ? 32 * kPersTY : kRowThreads;
@@ -1033,6 +1096,7 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
         const long v = strtol(mc, nullptr, 10);
         if (v >= 1 && v <= (1 << 20)) c->tma_min_chunk = (uint32_t)v;
     }
+    if (const char* ps = getenv("WS3D_PERSISTENT_SMEM")) c->smem_persistent = atoi(ps) != 0;
     build_tma_maps(c);
     // The two-step buffers are part of the auto / tma2 working set: allocate
     // them with the fields, not inside the first step (a failure only leaves

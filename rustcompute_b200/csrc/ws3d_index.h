@@ -72,6 +72,35 @@ WS3D_HD ZsLane zs_lane(uint32_t bx, uint32_t by, int lane, int w, uint32_t W, ui
 // Offset of plane `z` (may be -1 or nz: the ghosts).
 WS3D_HD int64_t zs_plane(int64_t z, int64_t plane) { return z * plane; }
 
+// Persistent steps with the field in shared memory (k_persistent_smem): bytes
+// of one CTA's block (p and p_prev with a one-cell halo, c2 of its own cells)
+// and the block shape: the fewest cells per CTA such that every block is
+// co-resident (at most `max_blocks`, one per SM) and fits `max_bytes`, then
+// the fewest face rows (by + bz).  Returns false when no shape qualifies.
+WS3D_HD uint64_t smem_step_bytes(uint32_t pitch, uint32_t by, uint32_t bz, bool c2f) {
+    const uint64_t vol = (uint64_t)(pitch + 2) * (by + 2) * (bz + 2);
+    return 2 * vol * 4 + (c2f ? (uint64_t)pitch * by * bz * 4 : 0);
+}
+WS3D_HD bool smem_step_shape(uint32_t pitch, uint32_t H, uint32_t nz, uint32_t max_blocks,
+                             bool c2f, uint64_t max_bytes, uint32_t* by, uint32_t* bz) {
+    *by = *bz = 0;
+    uint64_t best_cells = ~0ull, best_face = ~0ull;
+    for (uint32_t cy = 1; cy <= 128; cy *= 2)
+        for (uint32_t cz = 1; cz <= 128; cz *= 2) {
+            if (smem_step_bytes(pitch, cy, cz, c2f) > max_bytes) continue;
+            const uint64_t nblk = (uint64_t)((H + cy - 1) / cy) * (uint64_t)((nz + cz - 1) / cz);
+            if (nblk > max_blocks) continue;
+            const uint64_t cells = (uint64_t)cy * cz, face = cy + cz;
+            if (cells < best_cells || (cells == best_cells && face < best_face)) {
+                best_cells = cells;
+                best_face = face;
+                *by = cy;
+                *bz = cz;
+            }
+        }
+    return *by != 0;
+}
+
 // Block-parallel persistent body (k_persistent_rows, k_resident): block b of
 // a step is x-tile tx of rows yb*NW .. yb*NW + NW - 1 of plane z (one warp per
 // row, 128 cells a row).  On z-slabs the interior planes 1 .. nz-2 come first,

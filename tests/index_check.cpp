@@ -231,6 +231,93 @@ static void run_rows(uint32_t W, uint32_t H, uint32_t nz, bool slab, int NW) {
             }
 }
 
+// k_persistent_smem: the block shape the host picks (smem_step_shape, 148
+// SMs, 220 KiB, with or without a c2 field), then every shared-memory index the kernel forms (loads, the
+// cell rule's six neighbours, sources anywhere in the block and its halo,
+// faces, halo rows, the final write) against the two volumes and the c2
+// block, and every global offset against the owned planes; every cell of
+// the grid owned by exactly one block.
+static void run_smem(uint32_t W, uint32_t H, uint32_t nz, bool c2f) {
+    const uint32_t pitch = (W + 31u) & ~31u;
+    const int64_t P = (int64_t)H * pitch;
+    uint32_t by = 0, bz = 0;
+    if (!smem_step_shape(pitch, H, nz, 148, c2f, 220u * 1024u, &by, &bz)) {
+        printf("no shared-memory shape for %u x %u x %u (the row body takes it)\n", W, H, nz);
+        return;
+    }
+    const int SX = (int)pitch + 2, SY = (int)by + 2, SP = SX * SY, SV = SP * ((int)bz + 2);
+    const uint64_t c2n = (uint64_t)pitch * by * bz;
+    if (smem_step_bytes(pitch, by, bz, c2f) != (uint64_t)(2 * SV) * 4 + (c2f ? c2n * 4 : 0)) ++g_bad;
+    const uint32_t yblocks = (H + by - 1) / by, zblocks = (nz + bz - 1) / bz;
+    std::vector<unsigned char> owner((size_t)nz * H, 0);
+    auto sm_ok = [&](int x, int y, int z, const char* what) {
+        ++g_checked;
+        const int64_t i = (int64_t)(z + 1) * SP + (int64_t)(y + 1) * SX + (x + 1);
+        if (x < -1 || x > (int)pitch || i < 0 || i >= SV) {
+            if (g_bad < 20) fprintf(stderr, "SMEM OUT OF BOUNDS %s (%d,%d,%d) i=%lld\n", what, x, y, z,
+                                    (long long)i);
+            ++g_bad;
+        }
+    };
+    auto g_ok = [&](uint32_t x, int64_t y, int64_t z, const char* what) {
+        ++g_checked;
+        if (x >= pitch || y < 0 || y >= (int64_t)H || z < 0 || z >= (int64_t)nz) {
+            if (g_bad < 20) fprintf(stderr, "GLOBAL OUT OF RANGE %s (%u,%lld,%lld)\n", what, x,
+                                    (long long)y, (long long)z);
+            ++g_bad;
+        }
+        (void)P;
+    };
+    for (uint32_t blk = 0; blk < yblocks * zblocks; ++blk) {
+        const uint32_t y0 = (blk % yblocks) * by, z0 = (blk / yblocks) * bz;
+        const uint32_t ny = by < H - y0 ? by : H - y0, nzb = bz < nz - z0 ? bz : nz - z0;
+        for (int zz = -1; zz <= (int)nzb; ++zz)   // loads (in-grid rows only) and sources
+            for (int yy = -1; yy <= (int)ny; ++yy)
+                for (uint32_t x = 0; x < pitch; ++x) {
+                    sm_ok((int)x, yy, zz, "load / source");
+                    const int64_t gz = (int64_t)z0 + zz, gy = (int64_t)y0 + yy;
+                    if (gz >= 0 && gz < (int64_t)nz && gy >= 0 && gy < (int64_t)H)
+                        g_ok(x, gy, gz, "load");
+                }
+        for (int zz = 0; zz < (int)nzb; ++zz)
+            for (int yy = 0; yy < (int)ny; ++yy) {
+                owner[(size_t)(z0 + zz) * H + y0 + yy]++;
+                for (uint32_t x = 0; x < pitch; ++x) {
+                    sm_ok((int)x - 1, yy, zz, "w");
+                    sm_ok((int)x + 1, yy, zz, "e");
+                    sm_ok((int)x, yy - 1, zz, "s");
+                    sm_ok((int)x, yy + 1, zz, "n");
+                    sm_ok((int)x, yy, zz - 1, "d");
+                    sm_ok((int)x, yy, zz + 1, "u");
+                    ++g_checked;
+                    if ((uint64_t)(((uint64_t)zz * by + yy) * pitch + x) >= c2n) ++g_bad;
+                    g_ok(x, (int64_t)y0 + yy, (int64_t)z0 + zz, "face / final write");
+                }
+            }
+        // halo rows read back from the neighbours' faces: in-grid ones only
+        for (int zz = -1; zz <= (int)nzb; zz += (int)nzb + 1)
+            for (int yy = 0; yy < (int)ny; ++yy)
+                for (uint32_t x = 0; x < pitch; ++x) {
+                    sm_ok((int)x, yy, zz, "z halo");
+                    const int64_t gz = (int64_t)z0 + zz;
+                    if (gz >= 0 && gz < (int64_t)nz) g_ok(x, (int64_t)y0 + yy, gz, "z halo");
+                }
+        for (int yy = -1; yy <= (int)ny; yy += (int)ny + 1)
+            for (int zz = 0; zz < (int)nzb; ++zz)
+                for (uint32_t x = 0; x < pitch; ++x) {
+                    sm_ok((int)x, yy, zz, "y halo");
+                    const int64_t gy = (int64_t)y0 + yy;
+                    if (gy >= 0 && gy < (int64_t)H) g_ok(x, gy, (int64_t)z0 + zz, "y halo");
+                }
+    }
+    for (size_t r = 0; r < owner.size(); ++r)
+        if (owner[r] != 1) {
+            if (g_bad < 20) fprintf(stderr, "smem: row %zu owned %d times\n", r, owner[r]);
+            ++g_bad;
+        }
+    printf("shape %u x %u x %u, %u blocks\n", pitch, by, bz, yblocks * zblocks);
+}
+
 int main(int argc, char** argv) {
     if (argc < 5) {
         fprintf(stderr, "usage: %s W H nz sm_count [TY]\n", argv[0]);
@@ -241,6 +328,11 @@ int main(int argc, char** argv) {
     const int sms = atoi(argv[4]);
     const int ty = argc > 5 ? atoi(argv[5]) : 8;
     const bool halo = argc > 6 && atoi(argv[6]) != 0;
+    if (argc > 7 && atoi(argv[7]) == 3) {
+        run_smem(W, H, nz, halo);   // the sixth argument selects a c2 field here
+        printf("checked %lld accesses, %d out of bounds\n", g_checked, g_bad);
+        return g_bad == 0 ? 0 : 1;
+    }
     if (argc > 7 && atoi(argv[7]) == 2) {
         run_rows(W, H, nz, halo, ty);
         printf("checked %lld accesses, %d out of bounds\n", g_checked, g_bad);

@@ -49,7 +49,10 @@ def test_kernel_name_follows_the_library_choice():
     assert bench.kernel_name("auto", narrow, 1) == "k_step_zstream"      # boxes do not fit
     assert bench.kernel_name("auto", many, 1) == "k_step_tma"
     assert bench.kernel_name("tma", c3, 1) == "k_step_tma"
-    assert bench.kernel_name("auto", c3, 1, mode="persistent") == "k_persistent"
+    small = configs.build("c5", 128, 128, 128, steps=10)
+    assert bench.kernel_name("auto", c3, 1, mode="persistent") == "k_persistent_rows"
+    assert bench.kernel_name("auto", small, 1, mode="persistent") == "k_persistent_smem"
+    assert bench.kernel_name("auto", small, 2, mode="persistent") == "k_persistent_rows"
     assert bench.kernel_name("auto", c3, 1, mode="resident") == "k_resident"
 
 

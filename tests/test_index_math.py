@@ -72,6 +72,21 @@ def test_persistent_row_kernel_accesses_in_bounds(checker, shape, halo, nw):
     assert r.returncode == 0, r.stderr + r.stdout
 
 
+SMEM_SHAPES = [(128, 128, 128), (64, 64, 64), (13, 7, 5), (3, 3, 3), (1, 1, 1), (128, 37, 29),
+               (100, 130, 17), (70, 50, 41), (96, 80, 64), (128, 200, 200), (31, 1, 2)]
+
+
+@pytest.mark.parametrize("shape", SMEM_SHAPES)
+@pytest.mark.parametrize("c2f", [0, 1])
+def test_shared_memory_persistent_kernel_indices_in_bounds(checker, shape, c2f):
+    """k_persistent_smem: every shared-memory index inside its volumes, every
+    global offset inside the owned planes, every row owned by one block."""
+    W, H, nz = shape
+    r = subprocess.run([checker, str(W), str(H), str(nz), "148", "8", str(c2f), "3"],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr + r.stdout
+
+
 def test_checker_catches_the_unsigned_wrap(checker, tmp_path):
     """The check must flag the bug class it exists for: a ghost-plane offset
     computed in uint32 (zb - 1 wrapping to 2^32 - 1)."""
