@@ -125,7 +125,8 @@ struct ws3d_ctx {
     bool tb_buffers = false;   // buffers 2 and 3 allocated, their maps encoded
     bool tb_failed = false;    // their allocation failed: run single steps
     int tma_grid[4] = {0, 0, 0, 0};  // co-resident CTAs: [c2 field + 2 * lean rule]
-    int tb_grid[4] = {0, 0, 0, 0};  // [c2 field + 2 * slab]
+    int tb_grid[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // [c2 field + 2 * slab + 4 * deep pipeline]
+    int tb_stages_env = 0;  // WS3D_TWO_STEP_STAGES read at create; 0: by plane width
     uint64_t tb_launches = 0;
     int async_grid[2] = {0, 0};
     uint32_t tma_min_chunk = 32;  // WS3D_TMA_MIN_CHUNK (schedule tuning), read at create
@@ -505,15 +506,25 @@ uint32_t halo_caps(ws3d_ctx* c) {
     return caps;
 }
 
-template <bool kC2F>
-ws3d_status launch_tb(ws3d_ctx* c) {
-    using L = TbLayout<kC2F>;
+// TMA stages of the two-step kernel: five for rows up to 768 floats, four
+// above.  Measured on B200 (C3 recipe, µs per launch, 4 / 5 stages): 512^3
+// 517.6 / 495.1, 640^3 1005.6 / 959.5, 768x768x512 1131.9 / 1086.8, but
+// 1024^3 4131.7 / 4513.3; widths between 768 and 1024 were not measured.
+// WS3D_TWO_STEP_STAGES (4 or 5) at create overrides.
+int tb_stages(const ws3d_ctx* c) {
+    if (c->tb_stages_env) return c->tb_stages_env;
+    return c->pitch <= 768 ? kTbStagesHi : kTbStagesLo;
+}
+
+template <bool kC2F, int kS>
+ws3d_status launch_tb_stages(ws3d_ctx* c) {
+    using L = TbLayout<kC2F, kS>;
     constexpr int kThreads = 32 * (kTbTY + 3);
     const int smem = L::smem_bytes();
     // one GPU and z-slabs run separate instances (the slab code stays out
     // of the one-GPU item loop)
-    auto kern = c->halo ? k_step_tma2<kC2F, true> : k_step_tma2<kC2F, false>;
-    int& grid = c->tb_grid[(kC2F ? 1 : 0) + (c->halo ? 2 : 0)];
+    auto kern = c->halo ? k_step_tma2<kC2F, true, kS> : k_step_tma2<kC2F, false, kS>;
+    int& grid = c->tb_grid[(kC2F ? 1 : 0) + (c->halo ? 2 : 0) + (kS == kTbStagesHi ? 4 : 0)];
     if (grid == 0) {
         cudaError_t e =
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -598,6 +609,12 @@ ws3d_status launch_tb(ws3d_ctx* c) {
     c->ip = 0;
     c->ipp = 1;
     return WS3D_OK;
+}
+
+template <bool kC2F>
+ws3d_status launch_tb(ws3d_ctx* c) {
+    return tb_stages(c) == kTbStagesHi ? launch_tb_stages<kC2F, kTbStagesHi>(c)
+                                       : launch_tb_stages<kC2F, kTbStagesLo>(c);
 }
 
 // ---- cp.async kernel (one GPU or z-slabs, default face layout) -------------
@@ -1097,6 +1114,10 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
         if (v >= 1 && v <= (1 << 20)) c->tma_min_chunk = (uint32_t)v;
     }
     if (const char* ps = getenv("WS3D_PERSISTENT_SMEM")) c->smem_persistent = atoi(ps) != 0;
+    if (const char* ts = getenv("WS3D_TWO_STEP_STAGES")) {
+        const int v = atoi(ts);
+        if (v == kTbStagesLo || v == kTbStagesHi) c->tb_stages_env = v;
+    }
     build_tma_maps(c);
     // The two-step buffers are part of the auto / tma2 working set: allocate
     // them with the fields, not inside the first step (a failure only leaves

@@ -19,10 +19,18 @@
 // also compute the halo columns x0-1 and x0+128 of all TY+2 rows (ten lanes
 // each, one cell per lane) into a small shared array.  Warps 1 .. TY then
 // compute Y(q-1) on their (core) row: z neighbours X(q-2), X(q-1), X(q) from
-// registers, y neighbours from a two-slot shared ring of X planes, x halo from
-// the shared halo array, p_prev = A(q-1) from registers.  One named barrier
-// per item (consumer warps only) orders the shared X planes: slot q&1 is
-// written in item i and read in item i+1.  Cells use the lean rule of
+// registers, y neighbours from a three-slot shared ring of X planes, x halo
+// from the shared halo array, p_prev = A(q-1) from registers.  The ring is
+// ordered by one mbarrier per slot instead of a CTA barrier per item: a warp
+// stores X(q) into slot u % 3 (u counts its items), waits until every
+// consumer warp has arrived on the slot of item u-1 (they stored X(q-1) and
+// finished reading slot (u-2) % 3), computes Y(q-1) and arrives on slot u % 3.
+// The slot a warp writes in item u was last read in item u-2, whose end it
+// waited for in item u-1, so three slots need no second wait.  Warps drift up
+// to about half an item apart, and with a fifth TMA stage that took 512^3 from
+// 515 to 495 us per launch (neither change alone did: 4 stages with the split
+// ring 518 us, 5 stages with a CTA barrier per item 514 us).  Cells use the
+// lean rule of
 // ws3d_lean.cuh (packed f32x2, same bits as the one-step kernels): the sponge
 // factor is applied to every cell (1.0 outside it), lanes with boundary
 // cells take a fix-up branch.  The item loop is
@@ -50,10 +58,10 @@
 // instance of the item code, interior runs the one-GPU code.  Equal to single
 // steps bit for bit.
 //
-// Every mbarrier wait is bounded.  The item's barrier is a vote
-// (bar.red.or): if any consumer warp's wait gave up, all consumer warps see
-// it and leave together, so no warp is left waiting at a barrier.
-// The producer waits (bounded) for the copies it issued before it exits.  TMA
+// Every wait is a bounded mbarrier wait; the item loop has no hardware
+// barrier.  A consumer warp whose wait gives up stops arriving and leaves, so
+// the other warps' waits on its arrivals give up too (warp 0 reports it), and
+// so do the producer's waits for free stages.  The producer waits (bounded) for the copies it issued before it exits.  TMA
 // loads never use multicast; they read this GPU's memory, and on z-slabs the
 // neighbour's own edge planes of B and c2; default face layout.
 #pragma once
@@ -63,19 +71,21 @@
 
 namespace ws3d {
 
-// Pipeline depth.  With 16-row tiles (one CTA per SM) 4 stages measured
-// best: 5 took the same time at C3 but 15 % longer at C4 1024^3, 6 longer
-// still -- more planes in flight per SM evict the halo rows neighbouring
-// tiles would have read from L2.
-#ifndef WS3D_TB_STAGES
-#define WS3D_TB_STAGES 4
+// Pipeline depth kS (stages of the TMA ring) is a template parameter; the
+// host picks kTbStagesLo or kTbStagesHi from the plane width (tb_stages in
+// ws3d_api.cu): more stages in flight help narrow planes, while on wide ones
+// they evict the halo rows neighbouring tiles would have read from L2.
+#ifndef WS3D_TB_STAGES_HI
+#define WS3D_TB_STAGES_HI 5
 #endif
-constexpr int kTbStages = WS3D_TB_STAGES;
+constexpr int kTbStagesLo = 4;
+constexpr int kTbStagesHi = WS3D_TB_STAGES_HI;
+constexpr int kTbXSlots = 3;      // slots of the shared X ring
 constexpr int kTbRow = 136;       // floats per staged row (x0-4 .. x0+131)
 constexpr int kTbMaxSrc = 32;     // sources per launch (one per lane)
 constexpr int kTbSpongeMax = 64;  // sponge widths the kernel takes (table in shared memory)
 
-template <bool kC2F>
+template <bool kC2F, int kS>
 struct TbLayout {
     static constexpr int kABytes = kTbRow * (kTbTY + 4) * 4;             // 6528
     static constexpr int kBBytes = kTbRow * (kTbTY + 2) * 4;             // 5440
@@ -83,14 +93,14 @@ struct TbLayout {
     static constexpr int kStage = kABytes + kBBytesPad * (kC2F ? 2 : 1);
     static constexpr int kTx = kABytes + kBBytes * (kC2F ? 2 : 1);
     static constexpr int kRingPlane = 128 * (kTbTY + 2);                 // floats
-    static constexpr int kRingBytes = 2 * kRingPlane * 4;
-    static constexpr int kHaloBytes = (2 * (kTbTY + 2) * 2 * 4 + 127) / 128 * 128;  // [2][TY+2][2]
+    static constexpr int kRingBytes = kTbXSlots * kRingPlane * 4;
+    static constexpr int kHaloBytes = (kTbXSlots * (kTbTY + 2) * 2 * 4 + 127) / 128 * 128;  // [slot][TY+2][2]
     static constexpr int kTabBytes = kTbSpongeMax * 4;
     static constexpr int kSrcBytes = kTbMaxSrc * 16;
-    // stages | X ring | X halo columns | sponge table | sources | 2*S mbarriers | slack
+    // stages | X ring | X halo columns | sponge table | sources | 2*S + slots mbarriers | slack
     static constexpr int smem_bytes() {
-        return kTbStages * kStage + kRingBytes + kHaloBytes + kTabBytes + kSrcBytes +
-               16 * kTbStages + 128;
+        return kS * kStage + kRingBytes + kHaloBytes + kTabBytes + kSrcBytes + 16 * kS +
+               8 * kTbXSlots + 128;
     }
 };
 
@@ -117,19 +127,6 @@ struct TbArgs {
 };
 
 
-// Named barrier of the consumer warps that also ORs a predicate over them:
-// every consumer thread gets the same answer.
-__device__ __forceinline__ bool tb_bar_any(bool p) {
-    uint32_t r;
-    asm volatile(
-        "{\n .reg .pred ip, op;\n setp.ne.u32 ip, %1, 0;\n"
-        " bar.red.or.pred op, 1, %2, ip;\n selp.u32 %0, 1, 0, op;\n}\n"
-        : "=r"(r)
-        : "r"((uint32_t)p), "n"(32 * (kTbTY + 2))
-        : "memory");
-    return r != 0;
-}
-
 __device__ __forceinline__ float4 add_at(float4 v, int e, float d) {
     if (e == 0) v.x = __fadd_rn(v.x, d);
     else if (e == 1) v.y = __fadd_rn(v.y, d);
@@ -140,14 +137,14 @@ __device__ __forceinline__ float4 add_at(float4 v, int e, float d) {
 
 // kSlab: the z-slab instance (ghost-plane X, neighbour waits, pushes); the
 // one-GPU instance compiles none of that into its item loop.
-template <bool kC2F, bool kSlab>
+template <bool kC2F, bool kSlab, int kS>
 __global__ void __launch_bounds__(32 * (kTbTY + 3), kTbCtasPerSm)
 k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmC2, const __grid_constant__ CUtensorMap tmBlo,
             const __grid_constant__ CUtensorMap tmBhi, const __grid_constant__ CUtensorMap tmC2lo,
             const __grid_constant__ CUtensorMap tmC2hi, TbArgs g) {
-    using L = TbLayout<kC2F>;
-    constexpr int S = kTbStages, TY = kTbTY, R = kTbRow;
+    using L = TbLayout<kC2F, kS>;
+    constexpr int S = kS, TY = kTbTY, R = kTbRow;
     const StepParams& a = g.a;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -160,6 +157,7 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * L::kStage + L::kRingBytes +
                                                  L::kHaloBytes + L::kTabBytes + L::kSrcBytes);
     uint64_t* empty = full + S;
+    uint64_t* xbar = empty + S;  // X ring slot k: every consumer warp stored its X rows there
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (blockIdx.x >= g.nitems) return;  // uniform over the CTA, before any barrier
@@ -168,6 +166,7 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], TY + 2);
         }
+        for (int k = 0; k < kTbXSlots; ++k) mbar_init(&xbar[k], TY + 2);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (threadIdx.x < kTbSpongeMax)
@@ -286,6 +285,8 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const int xlo = kSlab && g.has_lo ? -1 : 0;
     const int xhi = (int)a.nz + (kSlab && g.has_hi ? 1 : 0);
     uint32_t s = 0, ph = 0;  // stage and full-barrier parity of the current item
+    uint32_t xs = 0, xph = 0;  // X ring slot of the current X item and its xbar parity
+    bool xany = false;         // an earlier item stored X planes
     for (uint32_t item = blockIdx.x; item < g.nitems; item += gridDim.x) {
         const uint32_t chunk = item / g.tiles, tile = item - chunk * g.tiles;
         const int zs = (int)(chunk * g.clen);
@@ -318,16 +319,27 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         const bool push_hi = kSlab && g.peer_hi_y != nullptr && ze + 2 > (int)a.nz;
 
         // Ends an item: release the previous item's stage (this warp no longer
-        // reads it), barrier with abort vote, next stage.  True = abort.
-        auto end_item = [&](bool ok, bool release) -> bool {
+        // reads it); after an X item, arrive on its ring slot (this warp's X
+        // rows are stored and its reads of the previous slot are done); next
+        // stage and slot.  True = a wait gave up: leave.
+        auto end_item = [&](bool ok, bool release, bool xitem) -> bool {
             __syncwarp();
-            if (release && lane == 0) mbar_arrive(&empty[s == 0 ? S - 1 : s - 1]);
-            const bool abort = tb_bar_any(!ok);
+            if (lane == 0) {
+                if (release) mbar_arrive(&empty[s == 0 ? S - 1 : s - 1]);
+                if (xitem && ok) mbar_arrive(&xbar[xs]);
+            }
+            if (xitem) {
+                xany = true;
+                if (++xs == (uint32_t)kTbXSlots) {
+                    xs = 0;
+                    xph ^= 1u;
+                }
+            }
             if (++s == S) {
                 s = 0;
                 ph ^= 1u;
             }
-            return abort;
+            return !ok;
         };
         // Items 0, 1: A planes zs-2, zs-1 of this row (and of the halo cell).
         auto prologue = [&](float4& av, float& hv, bool release) -> bool {
@@ -337,7 +349,7 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 av = *reinterpret_cast<const float4*>(Ac + arow + 4 + 4 * lane);
                 hv = hlane ? Ac[hr] : 0.f;
             }
-            return end_item(ok, release);
+            return end_item(ok, release, false);
         };
         // Item i >= 2: X(q), q = zs-3+i, from A(q-1) = a_m, A(q) = a_c and the
         // staged A(q+1) (kept in a_p); then Y(q-1) from X(q-2) = x_m,
@@ -350,9 +362,12 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                         float4& x_c, float4& x_n, float& h_m, float& h_c, float& h_p) -> bool {
             constexpr bool kSrc = (decltype(tag)::value & 1) != 0;
             constexpr bool kEdge = kSlab && (decltype(tag)::value & 2) != 0;
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph));
+            bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph));
             if (ok) {
                 const int q = zs - 3 + i;
+                // X ring slots: this item's X(q) and the previous item's X(q-1)
+                const uint32_t xw = xs;
+                const uint32_t xr = xs == 0 ? kTbXSlots - 1 : xs - 1;
                 const uint32_t sp = s == 0 ? S - 1 : s - 1;
                 const float* Ac = reinterpret_cast<const float*>(smem + s * L::kStage);
                 const float* Ap = reinterpret_cast<const float*>(smem + sp * L::kStage);
@@ -389,7 +404,7 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                             if (dx >= 0 && dx < 128 && lane == (dx >> 2)) xv = add_at(xv, dx & 3, amp);
                         }
                     }
-                    *reinterpret_cast<float4*>(ring + (q & 1) * L::kRingPlane + w * 128 + 4 * lane) = xv;
+                    *reinterpret_cast<float4*>(ring + xw * L::kRingPlane + w * 128 + 4 * lane) = xv;
                     if (act && q >= zs && q < ze) st4(g.X + zs_plane(q, P) + row, xv);
                     x_n = xv;
                     if (hwarp) {
@@ -415,20 +430,25 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                                 if (hlane && kx == hx && ky == hy) xh = __fadd_rn(xh, amp);
                             }
                         }
-                        if (hlane) hring[((q & 1) * (TY + 2) + hrow) * 2 + hside] = xh;
+                        if (hlane) hring[(xw * (TY + 2) + hrow) * 2 + hside] = xh;
                     }
                 }
+                // every consumer warp stored its rows of X(q-1) and finished
+                // reading the slot that X(q+1) will overwrite next item
+                if (xany)
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(&xbar[xr], xs == 0 ? xph ^ 1u : xph));
                 // ---- Y(q-1) on core row w (shared X(q-1) written last item)
                 const int qy = q - 1;
-                if (do_y && qy >= zs && qy < ze) {
-                    const float* Xr = ring + (qy & 1) * L::kRingPlane;
+                if (ok && do_y && qy >= zs && qy < ze) {
+                    const float* Xr = ring + xr * L::kRingPlane;
                     const float4 sv = *reinterpret_cast<const float4*>(Xr + (w - 1) * 128 + 4 * lane);
                     const float4 nv = *reinterpret_cast<const float4*>(Xr + (w + 1) * 128 + 4 * lane);
                     const float* Cp = reinterpret_cast<const float*>(smem + sp * L::kStage) +
                                       (L::kABytes + L::kBBytesPad) / 4;
                     const float4 c2y = kC2F ? *reinterpret_cast<const float4*>(Cp + w * R + 4 + 4 * lane)
                                             : make_float4(a.c2, a.c2, a.c2, a.c2);
-                    const float eh = hring[((qy & 1) * (TY + 2) + w) * 2 + (lane == 31 ? 1 : 0)];
+                    const float eh = hring[(xr * (TY + 2) + w) * 2 + (lane == 31 ? 1 : 0)];
                     float wl = __shfl_up_sync(0xffffffffu, x_c.w, 1);
                     float er = __shfl_down_sync(0xffffffffu, x_c.x, 1);
                     if (lane == 0) wl = eh;
@@ -461,7 +481,7 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     }
                 }
             }
-            return end_item(ok, true);
+            return end_item(ok, true, true);
         };
 
         const int last = n + 3;
@@ -498,12 +518,21 @@ k_step_tma2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             }
         }
         if (abort) {
+            // a wait gave up; the other warps' waits on this warp's arrivals
+            // give up in turn, so warp 0 reports it
             if (threadIdx.x == 0) atomicOr(a.status, 4u);
-            return;  // every consumer thread saw the same vote
+            return;
         }
         // the run's last stage
         if (lane == 0) mbar_arrive(&empty[s == 0 ? S - 1 : s - 1]);
     }
+    // Warp 0 also waits for every warp's arrival on the CTA's last item, so a
+    // warp that gave up there is reported as well.
+    if (warp == 0 && xany &&
+        !__all_sync(0xffffffffu, mbar_wait(&xbar[xs == 0 ? kTbXSlots - 1 : xs - 1],
+                                           xs == 0 ? xph ^ 1u : xph)) &&
+        lane == 0)
+        atomicOr(a.status, 4u);
     if (kSlab && (g.peer_lo_y || g.peer_hi_y)) __threadfence_system();
 }
 

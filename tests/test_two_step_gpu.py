@@ -75,6 +75,34 @@ def test_two_step_equals_one_step(shape, c2f, sponge, steps):
     two.close()
 
 
+@pytest.mark.parametrize("stages", ["4", "5", None])
+@pytest.mark.parametrize("shape", [(520, 21, 12), (384, 72, 100), (768, 24, 10), (1024, 26, 9)])
+def test_both_pipeline_depths_equal_one_step(monkeypatch, stages, shape):
+    """The two-step kernel has a 4- and a 5-stage TMA pipeline (chosen by row
+    width, 5 up to 768 floats; WS3D_TWO_STEP_STAGES at create forces one):
+    both equal single steps bit for bit, with a c2 field, a sponge and edge
+    sources."""
+    if stages is None:
+        monkeypatch.delenv("WS3D_TWO_STEP_STAGES", raising=False)
+    else:
+        monkeypatch.setenv("WS3D_TWO_STEP_STAGES", stages)
+    W, H, D = shape
+    rng = np.random.default_rng(W * 7 + D)
+    c2 = rng.uniform(0.01, 0.25, W * H * D).astype(np.float32)
+    src, wav = edge_sources(W, H, D, 12, rng)
+    one = make(W, H, D, "tma", c2=c2, sponge=3, sources=src, wavelet=wav, seed=D)
+    two = make(W, H, D, "tma2", c2=c2, sponge=3, sources=src, wavelet=wav, seed=D)
+    one.step_n(None, 9)
+    two.step_n(None, 9)
+    p1, pp1 = one.download_field(with_prev=True)
+    p2, pp2 = two.download_field(with_prev=True)
+    assert same_bits(p2, p1), f"pressure differs in {(p1 != p2).sum()} cells"
+    assert same_bits(pp2, pp1), f"pressure_prev differs in {(pp1 != pp2).sum()} cells"
+    assert two.stats()["two_step_launches"] == 4
+    one.close()
+    two.close()
+
+
 def test_two_step_matches_oracle_with_sources():
     wl = configs.build("c2", 144, 40, 36, steps=30)
     ref = oracle.from_workload(wl)
