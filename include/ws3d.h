@@ -67,7 +67,10 @@ enum {
     WS3D_VARIANT_AUTO = 0,     /* default: on one GPU with the default face layout and
                                   W > 128, H >= 16 the two-step kernel of TMA2 where it
                                   applies, else single TMA steps; ZSTREAM otherwise
-                                  (z-slabs, cell arrays, narrow grids) */
+                                  (z-slabs, cell arrays, narrow grids), except that
+                                  ws3d_step(n >= 2) on a small one-GPU grid (rows of at
+                                  most 128 cells, default faces) is one persistent launch
+                                  with the field in shared memory */
     WS3D_VARIANT_ZSTREAM = 1,  /* 2-D tile streaming along z, 128-bit loads, register
                                   prefetch; the kernel used for z-slabs and cell arrays */
     WS3D_VARIANT_NAIVE = 2,    /* one thread per cell, fused boundary (comparator) */
@@ -167,7 +170,12 @@ WS3D_API ws3d_status ws3d_set_c2_field(ws3d_ctx *ctx, const float *c2);
 WS3D_API ws3d_status ws3d_set_sources(ws3d_ctx *ctx, uint32_t n, const uint32_t *xyz,
                              const float *wavelet, uint64_t len);
 
-/* GpuBackend3D::step (gpu_backend.rs:314-380), n times.  Asynchronous. */
+/* GpuBackend3D::step (gpu_backend.rs:314-380), n times.  Asynchronous.  With
+ * the auto variant the library picks the launches: pairs of steps of wide
+ * grids go to the two-step kernel, and n >= 2 steps of a small one-GPU grid
+ * (rows of at most 128 cells, default faces, field within the SMs' shared
+ * memory) to one persistent launch; the fields are bit-identical to single
+ * steps either way. */
 WS3D_API ws3d_status ws3d_step(ws3d_ctx *ctx, uint64_t n);
 
 /* ws3d_step plus CUDA-event timing of every step-kernel launch on the

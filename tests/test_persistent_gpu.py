@@ -48,7 +48,7 @@ def test_persistent_equals_step_and_oracle(name, grid, steps):
     bp.step_persistent(steps)
     bp.sync()
     pp_, ppp = bp.download_field(with_prev=True)
-    _, bs = backend_for(wl)
+    _, bs = backend_for(wl, variant="zstream")   # one launch per step
     bs.step_n(None, steps)
     sp, spp = bs.download_field(with_prev=True)
     assert np.array_equal(pp_.view(np.uint32), sp.view(np.uint32))
@@ -66,7 +66,7 @@ def test_persistent_with_cell_arrays():
     cells = (g.cell_types.copy(), g.reflection_coeff.copy())
     _, bp = backend_for(wl, cells=cells)
     bp.step_persistent(60)
-    _, bs = backend_for(wl, cells=cells)
+    _, bs = backend_for(wl, variant="zstream", cells=cells)
     bs.step_n(None, 60)
     assert np.array_equal(bp.download_field(), bs.download_field())
 
@@ -78,10 +78,47 @@ def test_persistent_mixes_with_per_step_calls():
     a.step_n(None, 13)
     a.step_persistent(49)
     a.step_n(None, 1)
-    _, b = backend_for(wl)
+    _, b = backend_for(wl, variant="zstream")
     b.step_n(None, 100)
     assert np.array_equal(a.download_field(), b.download_field())
     assert a.stats()["step"] == 100
+
+
+@pytest.mark.parametrize("name,grid", [("c2", (96, 40, 37)), ("c3", (128, 48, 33)),
+                                       ("c1", (64, 64, 64)), ("c2", (33, 17, 9)),
+                                       ("c5", (128, 128, 128))])
+def test_auto_multi_step_calls_on_small_grids(name, grid):
+    """variant auto runs ws3d_step(n >= 2) on a small one-GPU grid as one
+    persistent launch (field in shared memory) and single calls as one step
+    launch; any mix of call sizes equals one launch per step bit for bit
+    (sources, c2 field and sponge of the recipe)."""
+    wl = configs.build(name, *grid, steps=60)
+    _, a = backend_for(wl)
+    _, b = backend_for(wl, variant="zstream")
+    l0 = a.stats()["kernel_launches"]
+    a.step_n(None, 25)
+    assert a.stats()["kernel_launches"] - l0 == 1      # the 25 steps in one launch
+    for n in (1, 2, 1, 7, 24):
+        a.step_n(None, n)
+    b.step_n(None, 60)
+    pa, ppa = a.download_field(with_prev=True)
+    pb, ppb = b.download_field(with_prev=True)
+    assert np.array_equal(pa.view(np.uint32), pb.view(np.uint32))
+    assert np.array_equal(ppa.view(np.uint32), ppb.view(np.uint32))
+    assert a.stats()["step"] == 60
+    a.close()
+    b.close()
+
+
+def test_auto_multi_step_routing_can_be_turned_off(monkeypatch):
+    """WS3D_PERSISTENT_SMEM=0 at create keeps one launch per step."""
+    monkeypatch.setenv("WS3D_PERSISTENT_SMEM", "0")
+    wl = configs.build("c1", 64, 64, 64, steps=10)
+    _, a = backend_for(wl)
+    l0 = a.stats()["kernel_launches"]
+    a.step_n(None, 10)
+    assert a.stats()["kernel_launches"] - l0 == 10
+    a.close()
 
 
 def test_persistent_backend_api_restated():
