@@ -425,8 +425,9 @@ def c5_latency(world, rank, local, pg, barrier, per_rank, stream, dev, device_ga
             "launch_per_step_us_per_step": launch_ms * 1e3 / n_launch,
             "launch_per_step_steps": n_launch,
             "kernels": "one cooperative launch (k_persistent_smem on one GPU: the field in "
-                       "shared memory; k_persistent_rows on z-slabs), one grid barrier per step, "
-                       "vs one k_step_zstream launch per step"}
+                       "shared memory, faces exchanged as step-tagged words; k_persistent_rows "
+                       "on z-slabs: one grid barrier per step) vs one k_step_zstream launch per "
+                       "step"}
 
 
 def run_ours(args, wl):

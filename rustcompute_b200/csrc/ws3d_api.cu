@@ -136,6 +136,10 @@ struct ws3d_ctx {
     // its block shape per c2 instance, found on first use: 0 unknown, 1 fits, -1 does not
     int smem_plan[2] = {0, 0};
     uint32_t smem_by[2] = {0, 0}, smem_bz[2] = {0, 0};
+    // its face exchange rows (tagged words) and the next launch's first tag
+    unsigned long long* smem_xch = nullptr;
+    size_t smem_xch_words = 0;
+    uint32_t smem_tag = 0;
 
     // persistent mode: co-resident CTAs of k_persistent per instantiation
     int pers_resident[4] = {0, 0, 0, 0};
@@ -702,14 +706,34 @@ ws3d_status launch_persistent_smem(ws3d_ctx* c, uint64_t n, bool* launched) {
         plan = 1;
     }
     const int bytes = (int)smem_step_bytes(c->pitch, by, bz, kC2F);
-    const uint32_t yblocks = (c->H + by - 1) / by;
-    const uint32_t nblk = yblocks * ((c->nz + bz - 1) / bz);
+    const uint32_t yblocks = (c->H + by - 1) / by, zblocks = (c->nz + bz - 1) / bz;
+    const uint32_t nblk = yblocks * zblocks;
+    // exchange rows: two parities of 2 (by + bz) rows per block, allocated
+    // (zeroed: tag 0 never matches) on first use; tags restart from a zeroed
+    // buffer before the 32-bit tag would wrap
+    if (n + 1 >= 0xffffffffull)
+        return fail(c, WS3D_EINVAL, "step_persistent: at most 2^32 - 2 steps per launch");
+    const size_t words = 2 * (size_t)nblk * smem_xch_rows(by, bz) * c->pitch;
+    if (c->smem_xch_words < words || (uint64_t)c->smem_tag + n + 1 >= 0xffffffffull) {
+        if (c->smem_xch_words < words) {
+            dfree(c, c->smem_xch, c->smem_xch_words);
+            c->smem_xch_words = 0;
+            ws3d_status s = dalloc(c, &c->smem_xch, words, "shared-memory step exchange rows");
+            if (s != WS3D_OK) return s;
+            c->smem_xch_words = words;
+        }
+        WS3D_CUDA(c, cudaMemsetAsync(c->smem_xch, 0, c->smem_xch_words * sizeof *c->smem_xch,
+                                     c->stream),
+                  WS3D_EMEMORY);
+        c->smem_tag = 0;
+    }
     SmemArgs q{};
     q.a = make_params(c);
     q.buf[0] = c->buf[c->ip];
     q.buf[1] = c->buf[c->ipp];
-    q.bar = c->flags + kBarWord;
-    WS3D_CUDA(c, cudaMemsetAsync(q.bar, 0, sizeof *q.bar, c->stream), WS3D_ELAUNCH);
+    q.xch = c->smem_xch;
+    q.tag0 = c->smem_tag;
+    c->smem_tag += (uint32_t)n;
     q.src_off = c->src_off;
     q.wavelet = c->wavelet;
     q.n_src = c->n_src;
@@ -719,6 +743,7 @@ ws3d_status launch_persistent_smem(ws3d_ctx* c, uint64_t n, bool* launched) {
     q.by = by;
     q.bz = bz;
     q.yblocks = yblocks;
+    q.zblocks = zblocks;
     void* args[] = {&q};
     cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, dim3(nblk), dim3(kSmemThreads),
                                                 args, (size_t)bytes, c->stream);
@@ -1176,6 +1201,7 @@ void ws3d_destroy(ws3d_ctx* c) {
         dfree(c, c->tb_src_off, c->tb_n_src);
         dfree(c, c->tb_wavelet, (size_t)c->tb_n_src * c->wl_len);
         dfree(c, c->flags, kFlagWords);
+        dfree(c, c->smem_xch, c->smem_xch_words);
         for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
         for (cudaEvent_t ev : c->tev) cudaEventDestroy(ev);
         dfree(c, c->vol16, c->vol_elems);

@@ -101,6 +101,52 @@ WS3D_HD bool smem_step_shape(uint32_t pitch, uint32_t H, uint32_t nz, uint32_t m
     return *by != 0;
 }
 
+// Face exchange of k_persistent_smem.  Block b receives its halo faces in
+// 2 * (by + bz) rows of pitch tagged words of its own: rows [0, bz) the
+// y-halo row below (row -1) of planes 0..bz-1, [bz, 2bz) the y-halo row above
+// (row ny), [2bz, 2bz + by) the z-halo plane below (plane -1) of rows
+// 0..by-1, [2bz + by, 2bz + 2by) the plane above (plane nzb).  side: 0 below
+// in y, 1 above in y, 2 below in z, 3 above in z; i: the plane (sides 0, 1)
+// or the row (sides 2, 3).
+WS3D_HD uint32_t smem_xch_rows(uint32_t by, uint32_t bz) { return 2u * (by + bz); }
+WS3D_HD uint32_t smem_xch_slot(uint32_t by, uint32_t bz, int side, int i) {
+    return side == 0 ? (uint32_t)i
+         : side == 1 ? bz + (uint32_t)i
+         : side == 2 ? 2u * bz + (uint32_t)i
+                     : 2u * bz + by + (uint32_t)i;
+}
+// Where face row (yy, zz) of block b goes.  kind 0: row 0 of plane zz (to the
+// block below in y, which holds it as its halo above); 1: the last row (block
+// above, halo below); 2: plane 0 (block below in z, halo above); 3: the last
+// plane (block above in z, halo below).  Blocks are numbered zb * yblocks +
+// yb.  False when there is no neighbour on that side.
+WS3D_HD bool smem_face_dest(uint32_t b, uint32_t yblocks, uint32_t zblocks, int kind, int yy,
+                            int zz, uint32_t* nb, int* side, int* i) {
+    const uint32_t yb = b % yblocks, zb = b / yblocks;
+    if (kind == 0) {
+        if (yb == 0) return false;
+        *nb = b - 1;
+        *side = 1;
+        *i = zz;
+    } else if (kind == 1) {
+        if (yb + 1 >= yblocks) return false;
+        *nb = b + 1;
+        *side = 0;
+        *i = zz;
+    } else if (kind == 2) {
+        if (zb == 0) return false;
+        *nb = b - yblocks;
+        *side = 3;
+        *i = yy;
+    } else {
+        if (zb + 1 >= zblocks) return false;
+        *nb = b + yblocks;
+        *side = 2;
+        *i = yy;
+    }
+    return true;
+}
+
 // Block-parallel persistent body (k_persistent_rows, k_resident): block b of
 // a step is x-tile tx of rows yb*NW .. yb*NW + NW - 1 of plane z (one warp per
 // row, 128 cells a row).  On z-slabs the interior planes 1 .. nz-2 come first,

@@ -8,29 +8,34 @@
 // with a one-cell halo in y and z, in shared memory for the whole launch.  A
 // step reads only shared memory; the only global traffic per step is the
 // block's four faces (first / last row of every plane, first / last plane)
-// written out and the neighbours' faces read back into the halo:
+// sent to the neighbours and theirs received into the halo:
 //
 //   step s: apply the sources of step s to the block and its halo copies
 //           (each CTA from the global list, in source order: p += a, and
 //           p_prev += a/2 on its own cells) -> compute p_{s+1} into the
-//           p_prev slot (each cell reads its own p_prev only) -> write the
-//           faces of p_{s+1} to global buffer buf[(s+1) & 1] -> grid barrier
-//           -> read the neighbours' faces of p_{s+1} into the halo.
+//           p_prev slot (each cell reads its own p_prev only) -> store the
+//           faces of p_{s+1} into the neighbours' exchange rows -> read the
+//           neighbours' faces of p_{s+1} from this CTA's exchange rows into
+//           the halo.
 //
-// The two field buffers alternate as the exchange area: a fast CTA writes the
-// faces of step s+1 into the other buffer, and cannot reach step s+2's
-// writes (into this step's buffer) before every CTA has passed step s+1's
-// barrier, i.e. finished reading this step's faces -- one barrier per step,
-// no barrier for sources.  Step 0 writes into buf[1], which the initial loads
-// read only at the CTAs' own cells.  After the last step each CTA writes its
+// Exchange rows hold 64-bit words (tag << 32 | value bits), stored and loaded
+// as single relaxed 64-bit accesses, so a word that shows the expected tag
+// also carries its value: no fence, no flag and no grid-wide barrier -- a
+// CTA waits only for the words its halo needs (the scheme of NCCL's
+// low-latency protocol).  Tags are tag0 + s + 1, increasing across launches
+// (the host restarts them from a zeroed buffer before they wrap), so a word
+// from an earlier step or launch never matches.  Rows alternate between two
+// parities: a CTA stores the faces of step s+2 into the rows of step s only
+// after it has received its neighbours' faces of step s+1, which they store
+// after reading the faces of step s.  After the last step each CTA writes its
 // block of p_n to buf[n & 1] and of p_{n-1} to buf[(n - 1) & 1] -- the roles
 // k_persistent leaves -- so the fields are bit-identical to per-step launches
 // (cell_rule<false>, the reference operation order).
 //
 // Halo cells outside the grid (y = -1 / H, z = -1 / D) and the x halo (x = -1
 // and x = pitch, outside every row) stay zero; the cells next to them are
-// faces, whose rule reads none of their neighbours.  Waits are bounded (the
-// grid barrier of ws3d_persistent.cuh).
+// faces, whose rule reads none of their neighbours.  Every wait for a tagged
+// word is bounded, and gives up at once when another CTA recorded an error.
 #pragma once
 
 #include "ws3d_persistent.cuh"
@@ -43,20 +48,53 @@ constexpr int kSmemMaxBytes = 220 * 1024;
 struct SmemArgs {
     StepParams a;                        // geometry and constants
     float* buf[2];                       // plane -1 of the two field buffers (pressure, prev)
-    unsigned long long* bar;             // grid barrier: arrivals (zeroed before the launch)
+    unsigned long long* xch;             // exchange rows: [parity][block][2 (by + bz)][pitch]
+    uint32_t tag0;                       // faces of step s carry tag tag0 + s + 1
     const uint64_t* src_off;             // (z+1) * plane + y * pitch + x
     const float* wavelet;
     uint32_t n_src;
     uint64_t wl_len;
     uint64_t step0;
     uint64_t nsteps;
-    uint32_t by, bz, yblocks;            // block shape, blocks along y
+    uint32_t by, bz, yblocks, zblocks;   // block shape, blocks along y and z
 };
+
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait for the word at p to carry `tag` (high 32 bits); returns the
+// word.  On a give-up (budget spent: status bit 3; or another CTA already
+// recorded an error) *ok = 0 and the value is meaningless.
+__device__ __noinline__ unsigned long long smem_tag_wait(const unsigned long long* p,
+                                                         unsigned long long tag,
+                                                         unsigned long long budget_ns,
+                                                         unsigned int* status, int* ok) {
+    const unsigned long long t0 = global_ns();
+    for (unsigned int it = 0; it < (1u << 26); ++it) {
+        const unsigned long long v = ld_relaxed_gpu_u64(p);
+        if ((v & 0xffffffff00000000ull) == tag) return v;
+        if ((it & 63u) == 63u) {
+            if (*reinterpret_cast<volatile unsigned int*>(status) != 0u) {
+                *ok = 0;
+                return 0;
+            }
+            if (global_ns() - t0 > budget_ns) break;
+        }
+    }
+    atomicOr(status, 8u);
+    *ok = 0;
+    return 0;
+}
 
 template <bool kC2F>
 __global__ void __launch_bounds__(kSmemThreads, 1) k_persistent_smem(SmemArgs q) {
     extern __shared__ float sm[];
-    __shared__ int s_ok;
     const StepParams& a = q.a;
     const uint32_t pitch = a.pitch;
     const int SX = (int)pitch + 2, SY = (int)q.by + 2;
@@ -68,8 +106,8 @@ __global__ void __launch_bounds__(kSmemThreads, 1) k_persistent_smem(SmemArgs q)
     const uint32_t y0 = yb * q.by, z0 = zb * q.bz;
     const uint32_t ny = min(q.by, a.H - y0), nzb = min(q.bz, a.nz - z0);
     const int64_t P = (int64_t)a.plane;
-    const unsigned int nb = gridDim.x;
     const int t = threadIdx.x;
+    const size_t nblk = gridDim.x, R = smem_xch_rows(q.by, q.bz);
     auto sidx = [&](int x, int y, int z) { return (z + 1) * SP + (y + 1) * SX + (x + 1); };
     auto gofs = [&](uint32_t x, uint32_t y, uint32_t z) {  // from plane -1
         return (int64_t)(z + 1) * P + (int64_t)y * pitch + x;
@@ -148,42 +186,74 @@ __global__ void __launch_bounds__(kSmemThreads, 1) k_persistent_smem(SmemArgs q)
         }
         __syncthreads();
 
-        // ---- faces of p_{s+1} -> buf[(s+1) & 1]; then the neighbours' faces
+        // ---- faces of p_{s+1} into the neighbours' exchange rows, then theirs
+        // into the halo: 64-bit words of (tag << 32 | value bits), so a word
+        // read with the expected tag carries its value -- no fence, no flag
         const bool last = s + 1 == q.nsteps;
-        float* gout = q.buf[(s + 1) & 1];
         if (!last) {
-            // first / last row of every plane, first / last plane
+            const uint32_t par = (uint32_t)((s + 1) & 1);
+            const unsigned long long tag = (unsigned long long)(q.tag0 + (uint32_t)s + 1u) << 32;
             const int rows = 2 * (int)nzb + 2 * (int)ny;
             for (int r = warp; r < rows; r += kSmemThreads / 32) {
-                int yy, zz;
+                int yy, zz, kind;
                 if (r < 2 * (int)nzb) {
                     zz = r >> 1;
-                    yy = (r & 1) ? (int)ny - 1 : 0;
+                    kind = r & 1;
+                    yy = kind ? (int)ny - 1 : 0;
                 } else {
                     yy = (r - 2 * (int)nzb) >> 1;
-                    zz = ((r - 2 * (int)nzb) & 1) ? (int)nzb - 1 : 0;
+                    kind = 2 + ((r - 2 * (int)nzb) & 1);
+                    zz = kind == 3 ? (int)nzb - 1 : 0;
                 }
+                uint32_t nbk;
+                int side, i;
+                if (!smem_face_dest(blockIdx.x, q.yblocks, q.zblocks, kind, yy, zz, &nbk, &side, &i))
+                    continue;
+                unsigned long long* dst =
+                    q.xch + (((size_t)par * nblk + nbk) * R + smem_xch_slot(q.by, q.bz, side, i)) * pitch;
+                const float* src = pv + sidx(0, yy, zz);
                 for (uint32_t x = (uint32_t)lane; x < pitch; x += 32)
-                    gout[gofs(x, y0 + (uint32_t)yy, z0 + (uint32_t)zz)] = pv[sidx((int)x, yy, zz)];
+                    st_relaxed_gpu_u64(dst + x, tag | __float_as_uint(src[x]));
             }
-            if (!grid_barrier(q.bar, nb, a.budget_ns, a.status, &s_ok)) return;
-            // neighbours' rows y0 - 1 / y0 + ny of every plane, planes z0 - 1 / z0 + nzb
-            const int hrows = 2 * (int)nzb + 2 * (int)ny;
-            for (int r = warp; r < hrows; r += kSmemThreads / 32) {
-                int yy, zz;
+            // the halo: rows y0 - 1 / y0 + ny of every plane, planes z0 - 1 / z0 + nzb
+            int ok = 1;
+            for (int r = warp; r < rows && ok; r += kSmemThreads / 32) {
+                int yy, zz, side, i;
+                bool have;
                 if (r < 2 * (int)nzb) {
                     zz = r >> 1;
-                    yy = (r & 1) ? (int)ny : -1;
+                    side = r & 1;
+                    yy = side ? (int)ny : -1;
+                    i = zz;
+                    have = side ? yb + 1 < q.yblocks : yb > 0;
                 } else {
                     yy = (r - 2 * (int)nzb) >> 1;
-                    zz = ((r - 2 * (int)nzb) & 1) ? (int)nzb : -1;
+                    side = 2 + ((r - 2 * (int)nzb) & 1);
+                    zz = side == 3 ? (int)nzb : -1;
+                    i = yy;
+                    have = side == 3 ? zb + 1 < q.zblocks : zb > 0;
                 }
-                const int64_t gy = (int64_t)y0 + yy, gz = (int64_t)z0 + zz;
-                if (gy < 0 || gy >= (int64_t)a.H || gz < 0 || gz >= (int64_t)a.nz) continue;
-                for (uint32_t x = (uint32_t)lane; x < pitch; x += 32)
-                    pv[sidx((int)x, yy, zz)] = __ldcg(gout + gofs(x, (uint32_t)gy, (uint32_t)gz));
+                if (!have) continue;
+                const unsigned long long* srcw =
+                    q.xch + (((size_t)par * nblk + blockIdx.x) * R + smem_xch_slot(q.by, q.bz, side, i)) * pitch;
+                // all of this lane's words in flight at once (rows are at most
+                // 128 cells: four per lane), then the tags
+                unsigned long long v[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t x = (uint32_t)lane + 32u * k;
+                    v[k] = x < pitch ? ld_relaxed_gpu_u64(srcw + x) : tag;
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t x = (uint32_t)lane + 32u * k;
+                    if (x >= pitch) continue;
+                    if ((v[k] & 0xffffffff00000000ull) != tag)
+                        v[k] = smem_tag_wait(srcw + x, tag, a.budget_ns, a.status, &ok);
+                    pv[sidx((int)x, yy, zz)] = __uint_as_float((uint32_t)v[k]);
+                }
             }
-            __syncthreads();
+            if (!__syncthreads_and(ok)) return;
         }
     }
 

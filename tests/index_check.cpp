@@ -250,6 +250,8 @@ static void run_smem(uint32_t W, uint32_t H, uint32_t nz, bool c2f) {
     if (smem_step_bytes(pitch, by, bz, c2f) != (uint64_t)(2 * SV) * 4 + (c2f ? c2n * 4 : 0)) ++g_bad;
     const uint32_t yblocks = (H + by - 1) / by, zblocks = (nz + bz - 1) / bz;
     std::vector<unsigned char> owner((size_t)nz * H, 0);
+    // exchange rows: [block][slot] -> global rows (z * H + y) stored there
+    std::vector<std::vector<int64_t>> sent((size_t)yblocks * zblocks * smem_xch_rows(by, bz));
     auto sm_ok = [&](int x, int y, int z, const char* what) {
         ++g_checked;
         const int64_t i = (int64_t)(z + 1) * SP + (int64_t)(y + 1) * SX + (x + 1);
@@ -294,21 +296,82 @@ static void run_smem(uint32_t W, uint32_t H, uint32_t nz, bool c2f) {
                     g_ok(x, (int64_t)y0 + yy, (int64_t)z0 + zz, "face / final write");
                 }
             }
-        // halo rows read back from the neighbours' faces: in-grid ones only
-        for (int zz = -1; zz <= (int)nzb; zz += (int)nzb + 1)
-            for (int yy = 0; yy < (int)ny; ++yy)
-                for (uint32_t x = 0; x < pitch; ++x) {
-                    sm_ok((int)x, yy, zz, "z halo");
-                    const int64_t gz = (int64_t)z0 + zz;
-                    if (gz >= 0 && gz < (int64_t)nz) g_ok(x, (int64_t)y0 + yy, gz, "z halo");
-                }
-        for (int yy = -1; yy <= (int)ny; yy += (int)ny + 1)
-            for (int zz = 0; zz < (int)nzb; ++zz)
-                for (uint32_t x = 0; x < pitch; ++x) {
-                    sm_ok((int)x, yy, zz, "y halo");
-                    const int64_t gy = (int64_t)y0 + yy;
-                    if (gy >= 0 && gy < (int64_t)H) g_ok(x, gy, (int64_t)z0 + zz, "y halo");
-                }
+        // face rows into the neighbours' exchange rows (smem_face_dest)
+        const uint32_t yb = blk % yblocks, zb = blk / yblocks;
+        for (int r = 0; r < 2 * (int)nzb + 2 * (int)ny; ++r) {
+            int yy, zz, kind;
+            if (r < 2 * (int)nzb) {
+                zz = r >> 1;
+                kind = r & 1;
+                yy = kind ? (int)ny - 1 : 0;
+            } else {
+                yy = (r - 2 * (int)nzb) >> 1;
+                kind = 2 + ((r - 2 * (int)nzb) & 1);
+                zz = kind == 3 ? (int)nzb - 1 : 0;
+            }
+            uint32_t nb;
+            int side, i;
+            ++g_checked;
+            if (!smem_face_dest(blk, yblocks, zblocks, kind, yy, zz, &nb, &side, &i)) {
+                const bool edge = kind == 0 ? yb == 0 : kind == 1 ? yb + 1 == yblocks
+                                : kind == 2 ? zb == 0 : zb + 1 == zblocks;
+                if (!edge) ++g_bad;   // a neighbour exists but gets nothing
+                continue;
+            }
+            const uint32_t slot = smem_xch_slot(by, bz, side, i);
+            if (nb >= yblocks * zblocks || slot >= smem_xch_rows(by, bz)) {
+                if (g_bad < 20) fprintf(stderr, "smem xch: block %u row (%d,%d) -> %u slot %u\n",
+                                        blk, yy, zz, nb, slot);
+                ++g_bad;
+                continue;
+            }
+            sent[(size_t)nb * smem_xch_rows(by, bz) + slot].push_back(
+                (int64_t)(z0 + zz) * H + (y0 + yy));
+        }
+    }
+    // every in-grid halo row a block reads comes from exactly one face row,
+    // the same global row; the halo rows stay inside the shared volume
+    for (uint32_t blk = 0; blk < yblocks * zblocks; ++blk) {
+        const uint32_t yb = blk % yblocks, zb = blk / yblocks;
+        const uint32_t y0 = yb * by, z0 = zb * bz;
+        const uint32_t ny = by < H - y0 ? by : H - y0, nzb = bz < nz - z0 ? bz : nz - z0;
+        std::vector<unsigned char> used(smem_xch_rows(by, bz), 0);
+        for (int r = 0; r < 2 * (int)nzb + 2 * (int)ny; ++r) {
+            int yy, zz, side, i;
+            bool have;
+            if (r < 2 * (int)nzb) {
+                zz = r >> 1;
+                side = r & 1;
+                yy = side ? (int)ny : -1;
+                i = zz;
+                have = side ? yb + 1 < yblocks : yb > 0;
+            } else {
+                yy = (r - 2 * (int)nzb) >> 1;
+                side = 2 + ((r - 2 * (int)nzb) & 1);
+                zz = side == 3 ? (int)nzb : -1;
+                i = yy;
+                have = side == 3 ? zb + 1 < zblocks : zb > 0;
+            }
+            const int64_t gy = (int64_t)y0 + yy, gz = (int64_t)z0 + zz;
+            const bool in_grid = gy >= 0 && gy < (int64_t)H && gz >= 0 && gz < (int64_t)nz;
+            ++g_checked;
+            if (have != in_grid) ++g_bad;   // a halo row in the grid must have a sender
+            if (!have) continue;
+            for (uint32_t x = 0; x < pitch; ++x) sm_ok((int)x, yy, zz, "halo");
+            const uint32_t slot = smem_xch_slot(by, bz, side, i);
+            ++g_checked;
+            if (slot >= used.size() || used[slot]++) {
+                ++g_bad;
+                continue;
+            }
+            const auto& got = sent[(size_t)blk * smem_xch_rows(by, bz) + slot];
+            ++g_checked;
+            if (got.size() != 1 || got[0] != gz * (int64_t)H + gy) {
+                if (g_bad < 20) fprintf(stderr, "smem xch: block %u halo (%d,%d) slot %u gets %zu rows\n",
+                                        blk, yy, zz, slot, got.size());
+                ++g_bad;
+            }
+        }
     }
     for (size_t r = 0; r < owner.size(); ++r)
         if (owner[r] != 1) {

@@ -80,7 +80,9 @@ SMEM_SHAPES = [(128, 128, 128), (64, 64, 64), (13, 7, 5), (3, 3, 3), (1, 1, 1), 
 @pytest.mark.parametrize("c2f", [0, 1])
 def test_shared_memory_persistent_kernel_indices_in_bounds(checker, shape, c2f):
     """k_persistent_smem: every shared-memory index inside its volumes, every
-    global offset inside the owned planes, every row owned by one block."""
+    global offset inside the owned planes, every row owned by one block, and
+    every in-grid halo row received from exactly one neighbour's face row of
+    the same global row (exchange rows inside the block's range)."""
     W, H, nz = shape
     r = subprocess.run([checker, str(W), str(H), str(nz), "148", "8", str(c2f), "3"],
                        capture_output=True, text=True, timeout=600)
@@ -103,6 +105,24 @@ def test_checker_catches_the_unsigned_wrap(checker, tmp_path):
     subprocess.run(["g++", "-O1", "-std=c++17", "-o", str(exe), str(probe)], check=True)
     r = subprocess.run([str(exe), "40", "36", "34", "148"], capture_output=True, text=True)
     assert r.returncode == 1 and "OUT OF BOUNDS" in r.stderr
+
+
+def test_checker_catches_a_misrouted_face(tmp_path):
+    """The replay of k_persistent_smem's face exchange flags a face row sent
+    to the wrong exchange row of its neighbour (the mistake is planted in a
+    copy of the index header)."""
+    bad = tmp_path / "bad_index.h"
+    src = open(os.path.join(ROOT, "rustcompute_b200", "csrc", "ws3d_index.h")).read()
+    old = "        *nb = b - 1;\n        *side = 1;"
+    assert src.count(old) == 1
+    bad.write_text(src.replace(old, "        *nb = b - 1;\n        *side = 0;"))
+    probe = tmp_path / "probe.cpp"
+    probe.write_text(open(SRC).read().replace('#include "ws3d_index.h"', f'#include "{bad}"'))
+    exe = tmp_path / "probe"
+    subprocess.run(["g++", "-O1", "-std=c++17", "-o", str(exe), str(probe)], check=True)
+    r = subprocess.run([str(exe), "64", "64", "64", "148", "8", "0", "3"], capture_output=True,
+                       text=True)
+    assert r.returncode == 1 and "smem xch" in r.stderr
 
 
 TB_SRC = os.path.join(ROOT, "tests", "tb_index_check.cpp")
