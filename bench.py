@@ -317,7 +317,9 @@ def kernel_name(variant, wl, world, mode="step", depth=1):
         tma_ok = wl.W > 128 and wl.H >= 16
         two_step = (world == 1 or depth == 2) and tma_ok and len(wl.sources) <= 32 and \
             wl.sponge_width <= 64 and wl.H >= _ffi.WS3D_TWO_STEP_ROWS + 4
-        variant = "tma2" if two_step else ("tma" if tma_ok else "zstream")
+        pitch = (wl.W + 31) // 32 * 32
+        small = world == 1 and pitch * wl.H * wl.D * 4 <= 8 << 20   # one thread per cell
+        variant = "tma2" if two_step else ("tma" if tma_ok else "naive" if small else "zstream")
     return {"tma": "k_step_tma", "tma2": "k_step_tma2", "async": "k_step_async",
             "zstream": "k_step_zstream",
             "naive": "k_step_naive", "refshape": "k_ref_stencil+k_ref_boundary"}[variant]

@@ -67,7 +67,8 @@ enum {
     WS3D_VARIANT_AUTO = 0,     /* default: on one GPU with the default face layout and
                                   W > 128, H >= 16 the two-step kernel of TMA2 where it
                                   applies, else single TMA steps; ZSTREAM otherwise
-                                  (z-slabs, cell arrays, narrow grids), except that
+                                  (z-slabs, cell arrays, narrow grids; NAIVE for
+                                  narrow one-GPU grids of at most 8 MiB a field), except that
                                   ws3d_step(n >= 2) on a small one-GPU grid (rows of at
                                   most 128 cells, default faces) is one persistent launch
                                   with the field in shared memory */

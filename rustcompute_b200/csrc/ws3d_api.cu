@@ -836,8 +836,14 @@ ws3d_status launch_step(ws3d_ctx* c) {
     // auto (single steps; pairs of steps go to k_step_tma2, see use_two_step):
     // the TMA pipeline on one GPU and on z-slabs (0.91 of measured HBM peak at
     // 512^3 on one GPU); cell arrays and grids too narrow for its boxes take
-    // the register-prefetch z-stream kernel (0.75).
-    if (v == WS3D_VARIANT_AUTO) v = tma_eligible(c) ? WS3D_VARIANT_TMA : WS3D_VARIANT_ZSTREAM;
+    // the register-prefetch z-stream kernel (0.75), except small one-GPU
+    // grids (each field at most 8 MiB, L2-resident), where one thread per cell
+    // is faster than a few tiles walking z: at 64^3 3.8 us of kernel time per
+    // step against 7.3 us (128^3: 12.8 against 13.7 us per launch).
+    if (v == WS3D_VARIANT_AUTO) {
+        const bool small = !c->halo && (uint64_t)c->pitch * c->H * c->nz * 4u <= (8ull << 20);
+        v = tma_eligible(c) ? WS3D_VARIANT_TMA : small ? WS3D_VARIANT_NAIVE : WS3D_VARIANT_ZSTREAM;
+    }
     if (v == WS3D_VARIANT_TMA2) v = WS3D_VARIANT_TMA;  // single steps of the two-step variant
     if (v == WS3D_VARIANT_ASYNC) {
         if (!c->cells_default)

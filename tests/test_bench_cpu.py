@@ -46,7 +46,10 @@ def test_kernel_name_follows_the_library_choice():
     assert bench.kernel_name("auto", c3, 1) == "k_step_tma2"
     assert bench.kernel_name("auto", c3, 2) == "k_step_tma"              # slabs at depth 1
     assert bench.kernel_name("auto", c3, 2, depth=2) == "k_step_tma2"    # slabs at depth 2
-    assert bench.kernel_name("auto", narrow, 1) == "k_step_zstream"      # boxes do not fit
+    assert bench.kernel_name("auto", narrow, 1) == "k_step_naive"        # boxes do not fit, small
+    assert bench.kernel_name("auto", narrow, 2) == "k_step_zstream"      # z-slabs
+    wide_narrow = configs.build("c3", 96, 512, 512, steps=10)
+    assert bench.kernel_name("auto", wide_narrow, 1) == "k_step_zstream"
     assert bench.kernel_name("auto", many, 1) == "k_step_tma"
     assert bench.kernel_name("tma", c3, 1) == "k_step_tma"
     small = configs.build("c5", 128, 128, 128, steps=10)
