@@ -119,7 +119,7 @@ class ClockSampler:
         0x100: "display_clock_setting",
     }
 
-    def __init__(self, device: int, period_s: float = 0.02):
+    def __init__(self, device: int, period_s: float = 0.005):
         self.samples, self.reasons = [], 0
         self.period = period_s
         self._stop = threading.Event()
