@@ -187,6 +187,14 @@ WS3D_API ws3d_status ws3d_step(ws3d_ctx *ctx, uint64_t n);
  * waits for the oldest one before reusing its pair. */
 WS3D_API ws3d_status ws3d_step_timed(ws3d_ctx *ctx, uint64_t n, double *kernel_ms);
 
+/* ws3d_step_timed in two halves, so that a caller can record its own event
+ * right behind the last launch: _begin enqueues the n steps with their event
+ * pairs and returns without synchronising; _end synchronises, returns the
+ * summed kernel time of the launches since _begin and reports device-side
+ * errors.  (No counterpart in the reference: benchmark support.) */
+WS3D_API ws3d_status ws3d_step_timed_begin(ws3d_ctx *ctx, uint64_t n);
+WS3D_API ws3d_status ws3d_step_timed_end(ws3d_ctx *ctx, double *kernel_ms);
+
 /* z-slab diagnostics: device nanoseconds this slab's step kernels spent in
  * neighbour-flag waits that did not pass at once, and how many such waits
  * there were, summed since the last reset (ws3d_halo_sync also clears them).

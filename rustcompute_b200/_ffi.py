@@ -210,6 +210,8 @@ SIGNATURES = {
     "ws3d_set_sources": (C.c_int, [_CTX, C.c_uint32, _U32, _F, C.c_uint64]),
     "ws3d_step": (C.c_int, [_CTX, C.c_uint64]),
     "ws3d_step_timed": (C.c_int, [_CTX, C.c_uint64, C.POINTER(C.c_double)]),
+    "ws3d_step_timed_begin": (C.c_int, [_CTX, C.c_uint64]),
+    "ws3d_step_timed_end": (C.c_int, [_CTX, C.POINTER(C.c_double)]),
     "ws3d_halo_wait_stats": (C.c_int, [_CTX, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
                                        C.c_int]),
     "ws3d_step_persistent": (C.c_int, [_CTX, C.c_uint64]),

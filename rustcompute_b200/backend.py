@@ -203,6 +203,18 @@ class GpuBackend3D:
         self._chk(self._lib.ws3d_step_timed(self._ctx, int(n), C.byref(out)), "step_timed")
         return float(out.value)
 
+    def step_timed_begin(self, n: int) -> None:
+        """step_timed without the synchronisation: enqueues `n` timed steps, so
+        the caller can record its own event right behind the last launch."""
+        self._chk(self._lib.ws3d_step_timed_begin(self._ctx, int(n)), "step_timed_begin")
+
+    def step_timed_end(self) -> float:
+        """Synchronises and returns the summed kernel time (ms) of the launches
+        since step_timed_begin."""
+        out = C.c_double()
+        self._chk(self._lib.ws3d_step_timed_end(self._ctx, C.byref(out)), "step_timed_end")
+        return float(out.value)
+
     def halo_wait_stats(self, reset: bool = False) -> tuple[int, int]:
         """z-slabs: (device ns spent in neighbour-flag waits that did not pass at
         once, number of such waits) since the last reset.  Synchronises."""

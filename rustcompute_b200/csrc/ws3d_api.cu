@@ -1510,21 +1510,33 @@ ws3d_status ws3d_step(ws3d_ctx* c, uint64_t n) {
     return step_impl(c, n, false);
 }
 
-ws3d_status ws3d_step_timed(ws3d_ctx* c, uint64_t n, double* kernel_ms) {
+ws3d_status ws3d_step_timed_begin(ws3d_ctx* c, uint64_t n) {
     WS3D_NOT_RESIDENT(c);
-    if (!c || !kernel_ms) return c ? fail(c, WS3D_EINVAL, "step_timed: kernel_ms is NULL")
-                                   : WS3D_EINVAL;
+    if (!c) return WS3D_EINVAL;
     if (n > (1u << 20)) return fail(c, WS3D_EINVAL, "step_timed: more than 2^20 steps");
     NvtxRange nv("ws3d.steps_timed", kNvtxKernel);
     DeviceGuard g(c->desc.device);
     c->tev_rec = c->tev_done = 0;
     c->tev_ms = 0.0;
-    ws3d_status s = step_impl(c, n, true);
-    if (s != WS3D_OK) return s;
+    return step_impl(c, n, true);
+}
+
+ws3d_status ws3d_step_timed_end(ws3d_ctx* c, double* kernel_ms) {
+    WS3D_NOT_RESIDENT(c);
+    if (!c || !kernel_ms) return c ? fail(c, WS3D_EINVAL, "step_timed: kernel_ms is NULL")
+                                   : WS3D_EINVAL;
+    DeviceGuard g(c->desc.device);
     WS3D_CUDA(c, cudaStreamSynchronize(c->stream), WS3D_ELAUNCH);
-    if ((s = timed_fold(c, c->tev_rec)) != WS3D_OK) return s;
+    ws3d_status s = timed_fold(c, c->tev_rec);
+    if (s != WS3D_OK) return s;
     *kernel_ms = c->tev_ms;
     return check_device_status(c);
+}
+
+ws3d_status ws3d_step_timed(ws3d_ctx* c, uint64_t n, double* kernel_ms) {
+    if (c && !kernel_ms) return fail(c, WS3D_EINVAL, "step_timed: kernel_ms is NULL");
+    ws3d_status s = ws3d_step_timed_begin(c, n);
+    return s != WS3D_OK ? s : ws3d_step_timed_end(c, kernel_ms);
 }
 
 ws3d_status ws3d_halo_wait_stats(ws3d_ctx* c, uint64_t* wait_ns, uint64_t* waits, int reset) {
