@@ -671,61 +671,94 @@ constexpr int kPersTY = 8;
 
 // Small one-GPU grids with the default faces and rows of at most 128 cells:
 // the field stays in shared memory for the whole launch (k_persistent_smem,
-// block shape from smem_step_shape, found once per context).  *launched =
-// false when the grid does not qualify.
+// block shape from smem_step_shape, found once per context and c2 instance).
+// False when the grid does not qualify.
 template <bool kC2F>
-ws3d_status launch_persistent_smem(ws3d_ctx* c, uint64_t n, bool* launched) {
-    *launched = false;
-    if (!c->smem_persistent || c->halo || !c->cells_default || c->pitch > 128) return WS3D_OK;
+bool smem_plan(ws3d_ctx* c) {
+    if (!c->smem_persistent || c->halo || !c->cells_default || c->pitch > 128) return false;
     auto kern = k_persistent_smem<kC2F>;
     int& plan = c->smem_plan[kC2F ? 1 : 0];
     uint32_t& by = c->smem_by[kC2F ? 1 : 0];
     uint32_t& bz = c->smem_bz[kC2F ? 1 : 0];
-    if (plan < 0) return WS3D_OK;
-    if (plan == 0) {
-        plan = -1;
-        if (!smem_step_shape(c->pitch, c->H, c->nz, (uint32_t)std::max(1, c->sm_count), kC2F,
-                             (uint64_t)kSmemMaxBytes, &by, &bz))
-            return WS3D_OK;
-        const int want = (int)smem_step_bytes(c->pitch, by, bz, kC2F);
-        // the attribute belongs to the function, not to this context: every
-        // context sets the same bound (the kernel's maximum), so none lowers
-        // it below another context's block size
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSmemMaxBytes);
-        if (e != cudaSuccess)
-            return cuda_fail(c, WS3D_ELAUNCH, e, "cudaFuncSetAttribute(smem step)");
-        int per_sm = 0;
+    if (plan != 0) return plan > 0;
+    plan = -1;
+    if (!smem_step_shape(c->pitch, c->H, c->nz, (uint32_t)std::max(1, c->sm_count), kC2F,
+                         (uint64_t)kSmemMaxBytes, &by, &bz))
+        return false;
+    const int want = (int)smem_step_bytes(c->pitch, by, bz, kC2F);
+    // the attribute belongs to the function, not to this context: every
+    // context sets the same bound (the kernel's maximum), so none lowers it
+    // below another context's block size
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMaxBytes);
+    int per_sm = 0;
+    if (e == cudaSuccess)
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSmemThreads, want);
-        const uint32_t blocks = ((c->H + by - 1) / by) * ((c->nz + bz - 1) / bz);
-        if (e != cudaSuccess || per_sm < 1 ||
-            blocks > (uint32_t)(per_sm * std::max(1, c->sm_count))) {
-            cudaGetLastError();
-            return WS3D_OK;  // not co-resident here: the row body takes the launch
-        }
-        plan = 1;
+    const uint32_t blocks = ((c->H + by - 1) / by) * ((c->nz + bz - 1) / bz);
+    if (e != cudaSuccess || per_sm < 1 || blocks > (uint32_t)(per_sm * std::max(1, c->sm_count))) {
+        cudaGetLastError();
+        return false;  // not co-resident here: the row body takes the launch
     }
+    plan = 1;
+    return true;
+}
+
+// Words of the exchange rows of a planned instance: two parities of
+// 2 (by + bz) rows of pitch words per block.
+size_t smem_xch_words(const ws3d_ctx* c, bool c2f) {
+    const int k = c2f ? 1 : 0;
+    const uint32_t by = c->smem_by[k], bz = c->smem_bz[k];
+    const size_t blocks = (size_t)((c->H + by - 1) / by) * ((c->nz + bz - 1) / bz);
+    return 2 * blocks * smem_xch_rows(by, bz) * c->pitch;
+}
+
+// Allocate (zeroed: tag 0 never matches) exchange rows of at least `words`;
+// tags restart from the zeroed buffer.
+ws3d_status smem_xch_alloc(ws3d_ctx* c, size_t words) {
+    if (c->smem_xch_words < words) {
+        dfree(c, c->smem_xch, c->smem_xch_words);
+        c->smem_xch_words = 0;
+        ws3d_status s = dalloc(c, &c->smem_xch, words, "shared-memory step exchange rows");
+        if (s != WS3D_OK) return s;
+        c->smem_xch_words = words;
+    }
+    WS3D_CUDA(c, cudaMemsetAsync(c->smem_xch, 0, c->smem_xch_words * sizeof *c->smem_xch, c->stream),
+              WS3D_EMEMORY);
+    c->smem_tag = 0;
+    return WS3D_OK;
+}
+
+// At create: the exchange rows of both instances (with and without a c2
+// field), so that stepping allocates nothing; a failure here only leaves the
+// allocation to the first launch.
+void smem_xch_prepare(ws3d_ctx* c) {
+    if (c->nz != c->Dg) return;  // a z-slab: attached slabs take the row body
+    size_t need = 0;
+    if (smem_plan<false>(c)) need = std::max(need, smem_xch_words(c, false));
+    if (smem_plan<true>(c)) need = std::max(need, smem_xch_words(c, true));
+    if (need && smem_xch_alloc(c, need) != WS3D_OK) {
+        cudaGetLastError();
+        c->err.clear();
+    }
+}
+
+template <bool kC2F>
+ws3d_status launch_persistent_smem(ws3d_ctx* c, uint64_t n, bool* launched) {
+    *launched = false;
+    if (!smem_plan<kC2F>(c)) return WS3D_OK;
+    const uint32_t by = c->smem_by[kC2F ? 1 : 0], bz = c->smem_bz[kC2F ? 1 : 0];
     const int bytes = (int)smem_step_bytes(c->pitch, by, bz, kC2F);
     const uint32_t yblocks = (c->H + by - 1) / by, zblocks = (c->nz + bz - 1) / bz;
     const uint32_t nblk = yblocks * zblocks;
-    // exchange rows: two parities of 2 (by + bz) rows per block, allocated
-    // (zeroed: tag 0 never matches) on first use; tags restart from a zeroed
+    // exchange rows: allocated at create (smem_xch_prepare), here only when
+    // that failed or a larger instance needs more; tags restart from a zeroed
     // buffer before the 32-bit tag would wrap
     if (n + 1 >= 0xffffffffull)
         return fail(c, WS3D_EINVAL, "step_persistent: at most 2^32 - 2 steps per launch");
-    const size_t words = 2 * (size_t)nblk * smem_xch_rows(by, bz) * c->pitch;
+    const size_t words = smem_xch_words(c, kC2F);
     if (c->smem_xch_words < words || (uint64_t)c->smem_tag + n + 1 >= 0xffffffffull) {
-        if (c->smem_xch_words < words) {
-            dfree(c, c->smem_xch, c->smem_xch_words);
-            c->smem_xch_words = 0;
-            ws3d_status s = dalloc(c, &c->smem_xch, words, "shared-memory step exchange rows");
-            if (s != WS3D_OK) return s;
-            c->smem_xch_words = words;
-        }
-        WS3D_CUDA(c, cudaMemsetAsync(c->smem_xch, 0, c->smem_xch_words * sizeof *c->smem_xch,
-                                     c->stream),
-                  WS3D_EMEMORY);
-        c->smem_tag = 0;
+        ws3d_status s = smem_xch_alloc(c, words);
+        if (s != WS3D_OK) return s;
     }
     SmemArgs q{};
     q.a = make_params(c);
@@ -745,7 +778,8 @@ ws3d_status launch_persistent_smem(ws3d_ctx* c, uint64_t n, bool* launched) {
     q.yblocks = yblocks;
     q.zblocks = zblocks;
     void* args[] = {&q};
-    cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, dim3(nblk), dim3(kSmemThreads),
+    cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_persistent_smem<kC2F>, dim3(nblk),
+                                                dim3(kSmemThreads),
                                                 args, (size_t)bytes, c->stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -1167,6 +1201,8 @@ ws3d_status ws3d_create(const ws3d_desc* desc, ws3d_ctx** out) {
         if (v == kTbStagesLo || v == kTbStagesHi) c->tb_stages_env = v;
     }
     build_tma_maps(c);
+    // likewise the persistent shared-memory kernel's exchange rows
+    smem_xch_prepare(c);
     // The two-step buffers are part of the auto / tma2 working set: allocate
     // them with the fields, not inside the first step (a failure only leaves
     // the context on single steps).

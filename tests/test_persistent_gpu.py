@@ -189,3 +189,18 @@ def test_persistent_neighbour_wait_times_out():
         parent.send("done")
         proc.join(timeout=60)
     assert proc.exitcode == 0
+
+
+@pytest.mark.parametrize("name,grid", [("c1", (64, 64, 64)), ("c3", (128, 48, 33))])
+def test_small_grid_steps_allocate_nothing(name, grid):
+    """The persistent shared-memory kernel's exchange rows come with the
+    context (for both c2 instances): multi-step calls on a small grid, before
+    and after a c2 field is set, add no device memory."""
+    wl = configs.build(name, *grid, steps=20)
+    _, a = backend_for(wl)          # sets the recipe's c2 field, if any
+    m0 = a.memory_usage()
+    a.step_n(None, 10)
+    a.step_persistent(10)
+    a.sync()
+    assert a.memory_usage() == m0
+    a.close()
