@@ -204,3 +204,32 @@ def test_small_grid_steps_allocate_nothing(name, grid):
     a.sync()
     assert a.memory_usage() == m0
     a.close()
+
+
+@pytest.mark.parametrize("c2f", [False, True])
+def test_small_grid_sources_on_block_faces(c2f):
+    """Sources on the faces of the persistent kernel's blocks (64^3: blocks of
+    4 rows x 8 planes; with a c2 field the shape may differ, so rows and planes
+    around every multiple of 4 and 8 are covered), coinciding pairs included:
+    each block applies them to its cells and to its halo copies, and the
+    result equals one launch per step bit for bit."""
+    W = H = D = 64
+    rng = np.random.default_rng(11)
+    pts = [[x, y, z] for x in (1, 31, 62) for y in (3, 4, 7, 8, 31, 32) for z in (7, 8, 15, 16, 40)]
+    pts = np.array(pts[:60] + pts[:3], np.uint32)          # three coinciding pairs
+    wav = rng.standard_normal((len(pts), 40)).astype(np.float32)
+    c2 = rng.uniform(0.01, 0.25, W * H * D).astype(np.float32) if c2f else None
+    runs = []
+    for variant in ("auto", "zstream"):
+        g = SimulationGrid3D(W, H, D, AcousticParams3D(c_squared=0.2, simple_damping=0.999))
+        b = GpuBackend3D(g, variant=variant, sponge_width=4, sponge_max=0.1)
+        if c2 is not None:
+            b.set_c2_field(c2)
+        b.set_sources(pts, wav)
+        b.step_n(None, 37)
+        runs.append(b.download_field(with_prev=True))
+        b.close()
+    (pa, ppa), (pb, ppb) = runs
+    assert float(np.max(np.abs(pb))) > 1e-6
+    assert np.array_equal(pa.view(np.uint32), pb.view(np.uint32))
+    assert np.array_equal(ppa.view(np.uint32), ppb.view(np.uint32))
