@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 WaveSim3D FDTD step (BASELINE config 3 by default).
+"""Benchmark of the B200 WaveSim3D FDTD step (configuration c3 by default).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload c3] [--variant zstream]
@@ -64,14 +64,14 @@ def parse():
                          "the kernel reporting the last step; one GPU)")
     ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
                     help="N > 1: weak (default) keeps one D-plane slab of the recipe per GPU "
-                         "(grid W x H x D*N, as BASELINE config 4's weak scaling); strong "
+                         "(grid W x H x D*N, as configuration c4's weak scaling); strong "
                          "splits the single-GPU grid into N slabs")
     ap.add_argument("--grid", default=None,
                     help="WxHxD: the workload's recipe at another size (profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-c5", action="store_true",
-                    help="skip the BASELINE config 5 latency figures (persistent launch vs one "
+                    help="skip the configuration c5 latency figures (persistent launch vs one "
                          "launch per step, 128^3) added to the line")
     ap.add_argument("--comparators", action="store_true",
                     help="also time the naive and reference-shaped kernels")
@@ -383,7 +383,7 @@ def slab_parity(b, wl, args, rank, world, local, pg, depth) -> dict:
 
 
 def c5_latency(world, rank, local, pg, barrier, per_rank, stream, dev, device_gate) -> dict:
-    """BASELINE config 5 beside the main line: 128^3 uniform Gaussian on the same
+    """configuration c5 beside the main line: 128^3 uniform Gaussian on the same
     GPUs (z-slabs at N > 1, halos by in-kernel peer stores and flags), all
     10,000 steps in ONE persistent (cooperative) launch against one launch per
     step; microseconds per step, max over ranks, CUDA events on the launch

@@ -1,7 +1,7 @@
 // ws3d_smemstep.cuh -- persistent steps with the field resident in shared
 // memory (one GPU, default face layout, rows of at most 128 cells).
 //
-// For small grids (128^3, 10,000 steps) a persistent step
+// For small grids (configuration c5: 128^3, 10,000 steps) a persistent step
 // is latency-bound: every CTA reloads its cells and their neighbours from L2
 // each step.  Here every CTA owns a block of whole rows -- all x, rows
 // [y0, y0 + by), planes [z0, z0 + bz) -- and keeps p and p_prev of the block,

@@ -10,7 +10,7 @@ stores SHA-256 digests of the final pressure / pressure_prev bytes plus energy
 and peak; the C1 case also stores its three centre slices, and one ragged case
 stores its whole fields.
 
-`--full` runs the five BASELINE configurations at their stated sizes and step
+`--full` runs the five benchmark configurations (c1..c5) at their stated sizes and step
 counts (C2 256^3 x 1000, C3 512^3 x 500, C4 1024^3 x 200, C5 128^3 x 10,000;
 C1 is in golden.json already) on all host threads and stores the same digests
 in golden_full.json.  tests/test_full_configs_gpu.py checks the CUDA path

@@ -1,4 +1,4 @@
-"""GPU parity at the BASELINE configurations' stated sizes and step counts.
+"""GPU parity at the benchmark configurations' (c1..c5) stated sizes and step counts.
 
 Each case runs the path bench.py times -- variant auto through the C-ABI, which
 takes the two-step kernel (k_step_tma2) for every pair of steps where it

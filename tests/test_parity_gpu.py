@@ -63,7 +63,7 @@ def gpu_for(wl, variant="zstream", grid=None):
 
 @pytest.mark.parametrize("variant", VARIANTS)
 def test_c1_full_config_matches_oracle(variant):
-    """BASELINE config 1 exactly: 64^3, Gaussian sigma 3, 200 steps."""
+    """configuration c1 exactly: 64^3, Gaussian sigma 3, 200 steps."""
     wl = configs.build("c1")
     skip_unless_applicable(variant, wl.W, wl.H)
     ref = oracle.from_workload(wl)
@@ -265,7 +265,7 @@ def test_errors_are_raised_not_swallowed():
 
 
 def test_full_size_c3_kernels_agree_and_match_oracle():
-    """BASELINE config 3 at full size (512^3, heterogeneous, sponge, source):
+    """configuration c3 at full size (512^3, heterogeneous, sponge, source):
     size-independent checks -- independent kernels (TMA pipeline, z-stream,
     one thread per cell, and the auto path bench.py times, which runs the
     two-step kernel for every pair of steps) agree bit for bit after 20
