@@ -513,14 +513,17 @@ uint32_t halo_caps(ws3d_ctx* c) {
     return caps;
 }
 
-// TMA stages of the two-step kernel: five for rows up to 768 floats, four
-// above.  Measured on B200 (C3 recipe, µs per launch, 4 / 5 stages): 512^3
-// 517.6 / 495.1, 640^3 1005.6 / 959.5, 768x768x512 1131.9 / 1086.8, but
-// 1024^3 4131.7 / 4513.3; widths between 768 and 1024 were not measured.
+// TMA stages of the two-step kernel: five while a field (this context's
+// planes) takes at most 1.5 GiB, four above.  Measured on B200 (C3 recipe,
+// µs per launch, 4 / 5 stages): 512^3 517.6 / 495.1, 640^3 1005.6 / 959.5,
+// 768x768x512 1131.9 / 1086.8, 896x896x256 772.0 / 727.9, 960x960x256
+// 939.7 / 910.7, 1024x1024x256 1019.3 / 1011.6 -- but 768x768x1024 (2.4 GB a
+// field) 2310.4 / 2399.7 and 1024^3 (4.3 GB) 4131.7 / 4513.3: the loss
+// follows the size of the grid, not the width of its rows.
 // WS3D_TWO_STEP_STAGES (4 or 5) at create overrides.
 int tb_stages(const ws3d_ctx* c) {
     if (c->tb_stages_env) return c->tb_stages_env;
-    return c->pitch <= 768 ? kTbStagesHi : kTbStagesLo;
+    return (uint64_t)c->pitch * c->H * c->nz * 4u <= (3ull << 29) ? kTbStagesHi : kTbStagesLo;
 }
 
 template <bool kC2F, int kS>

@@ -72,9 +72,9 @@
 namespace ws3d {
 
 // Pipeline depth kS (stages of the TMA ring) is a template parameter; the
-// host picks kTbStagesLo or kTbStagesHi from the plane width (tb_stages in
-// ws3d_api.cu): more stages in flight help narrow planes, while on wide ones
-// they evict the halo rows neighbouring tiles would have read from L2.
+// host picks kTbStagesLo or kTbStagesHi from the size of the grid
+// (tb_stages in ws3d_api.cu): a fifth stage in flight helps grids of up to
+// about a gigabyte a field and costs time on larger ones.
 #ifndef WS3D_TB_STAGES_HI
 #define WS3D_TB_STAGES_HI 5
 #endif

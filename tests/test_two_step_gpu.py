@@ -79,7 +79,8 @@ def test_two_step_equals_one_step(shape, c2f, sponge, steps):
 @pytest.mark.parametrize("shape", [(520, 21, 12), (384, 72, 100), (768, 24, 10), (1024, 26, 9)])
 def test_both_pipeline_depths_equal_one_step(monkeypatch, stages, shape):
     """The two-step kernel has a 4- and a 5-stage TMA pipeline (chosen by row
-    width, 5 up to 768 floats; WS3D_TWO_STEP_STAGES at create forces one):
+    size, 5 while a field takes at most 1.5 GiB; WS3D_TWO_STEP_STAGES at create
+    forces one):
     both equal single steps bit for bit, with a c2 field, a sponge and edge
     sources."""
     if stages is None:
